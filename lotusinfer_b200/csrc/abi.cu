@@ -1,0 +1,413 @@
+// C ABI entry points (include/lotus_ops.h): argument validation, shape
+// arithmetic, dispatch to the kernels, status codes and error strings.
+//
+// The reference checks nothing at its launch sites (e.g.
+// source/layer/layer_conv2d.cu:60-69 launches without cudaGetLastError) and
+// aborts through glog CHECK on host-side shape errors
+// (include/lotus_utils.hpp:28-32).  Here every entry point validates its
+// arguments, returns a negative status instead of launching on bad input, and
+// reports launch failures.
+
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "../../include/lotus_ops.h"
+#include "kernels.h"
+
+namespace lotus_impl {
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+static thread_local std::string t_last_error;
+
+static int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+static int ok() {
+  t_last_error.clear();
+  return LOTUS_OK;
+}
+static int cuda_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(LOTUS_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return ok();
+}
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static int cs_of(int c) { return (c + 7) / 8 * 8; }
+static int round64(long v) { return static_cast<int>((v + 63) / 64 * 64); }
+
+static constexpr long kMaxIndex = 0x7FFFFFFFL;
+
+static int check_conv_desc(const lotus_conv2d_desc* d, int* oh, int* ow) {
+  if (!d) return fail(LOTUS_ERR_INVALID, "conv2d: null descriptor");
+  if (d->n <= 0 || d->c_in <= 0 || d->h <= 0 || d->w <= 0 || d->c_out <= 0 || d->kh <= 0 || d->kw <= 0)
+    return fail(LOTUS_ERR_INVALID, "conv2d: sizes must be positive");
+  if (d->stride_h <= 0 || d->stride_w <= 0 || d->pad_h < 0 || d->pad_w < 0)
+    return fail(LOTUS_ERR_INVALID, "conv2d: stride must be positive and padding non-negative");
+  if (d->act < 0 || d->act > 2) return fail(LOTUS_ERR_INVALID, "conv2d: unknown activation");
+  if (d->out_kind != LOTUS_OUT_NHWC_F16 && d->out_kind != LOTUS_OUT_ROWS_F32)
+    return fail(LOTUS_ERR_INVALID, "conv2d: unknown out_kind");
+  const long eh = static_cast<long>(d->h) + 2L * d->pad_h - d->kh;
+  const long ew = static_cast<long>(d->w) + 2L * d->pad_w - d->kw;
+  if (eh < 0 || ew < 0) return fail(LOTUS_ERR_INVALID, "conv2d: kernel larger than padded input");
+  *oh = static_cast<int>(eh / d->stride_h + 1);
+  *ow = static_cast<int>(ew / d->stride_w + 1);
+  if (d->kh > 255 || d->kw > 255) return fail(LOTUS_ERR_UNSUPPORTED, "conv2d: kernel side > 255");
+  if (cs_of(d->c_in) > 65535) return fail(LOTUS_ERR_UNSUPPORTED, "conv2d: more than 65535 input channels");
+  if (static_cast<long>(d->n) * *oh * *ow > kMaxIndex) return fail(LOTUS_ERR_UNSUPPORTED, "conv2d: too many pixels");
+  return ok();
+}
+
+}  // namespace lotus_impl
+
+using namespace lotus_impl;
+
+extern "C" {
+
+const char* lotus_last_error_string(void) { return t_last_error.c_str(); }
+
+uint64_t lotus_launch_count(void) { return g_launches.load(); }
+
+int lotus_device_error(void) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "device_error: synchronize");
+  return read_device_error();
+}
+
+int lotus_channel_stride(int c) { return c <= 0 ? 0 : cs_of(c); }
+
+int lotus_conv2d_out_hw(const lotus_conv2d_desc* d, int* oh, int* ow) {
+  int a, b;
+  const int st = check_conv_desc(d, &a, &b);
+  if (st != LOTUS_OK) return st;
+  if (oh) *oh = a;
+  if (ow) *ow = b;
+  return ok();
+}
+
+size_t lotus_conv2d_packed_weight_bytes(const lotus_conv2d_desc* d) {
+  if (!d || d->c_out <= 0 || d->kh <= 0 || d->kw <= 0 || d->c_in <= 0) return 0;
+  const long k_pad = round64(static_cast<long>(d->kh) * d->kw * cs_of(d->c_in));
+  return static_cast<size_t>(d->c_out) * k_pad * 2;
+}
+
+int lotus_conv2d_prepack(const float* w_oihw, void* w_packed, const lotus_conv2d_desc* d, cudaStream_t stream) {
+  int oh, ow;
+  const int st = check_conv_desc(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  if (!w_oihw || !w_packed) return fail(LOTUS_ERR_INVALID, "conv2d_prepack: null pointer");
+  const int cs = cs_of(d->c_in);
+  const int k_pad = round64(static_cast<long>(d->kh) * d->kw * cs);
+  return cuda_status(launch_conv_prepack(w_oihw, w_packed, d->c_out, d->c_in, d->kh, d->kw, cs, k_pad, stream),
+                     "conv2d_prepack");
+}
+
+int lotus_conv2d_fwd(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                     const lotus_conv2d_desc* d, cudaStream_t stream) {
+  int oh, ow;
+  const int st = check_conv_desc(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  if (!x || !w_packed || !y) return fail(LOTUS_ERR_INVALID, "conv2d: null x, w or y");
+  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y) || (residual && !aligned16(residual)))
+    return fail(LOTUS_ERR_INVALID, "conv2d: x, w, y and residual must be 16-byte aligned");
+  if (residual && d->out_kind != LOTUS_OUT_NHWC_F16)
+    return fail(LOTUS_ERR_INVALID, "conv2d: residual needs the NHWC fp16 output");
+  if (d->out_kind == LOTUS_OUT_ROWS_F32 && (reinterpret_cast<uintptr_t>(y) & 3u))
+    return fail(LOTUS_ERR_INVALID, "conv2d: fp32 output must be 4-byte aligned");
+  ConvTcArgs a{};
+  a.x = x;
+  a.w_packed = w_packed;
+  a.bias = bias;
+  a.residual = residual;
+  a.y = y;
+  a.H = d->h;
+  a.W = d->w;
+  a.Cs_in = cs_of(d->c_in);
+  a.OH = oh;
+  a.OW = ow;
+  a.kh = d->kh;
+  a.kw = d->kw;
+  a.sh = d->stride_h;
+  a.sw = d->stride_w;
+  a.ph = d->pad_h;
+  a.pw = d->pad_w;
+  a.n_cols = d->c_out;
+  a.k_pad = round64(static_cast<long>(d->kh) * d->kw * a.Cs_in);
+  a.Cs_out = cs_of(d->c_out);
+  a.M = d->n * oh * ow;
+  a.act = d->act;
+  a.out_kind = d->out_kind;
+  const char* err = "";
+  const int r = conv_tc_launch(a, stream, &err);
+  if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
+  return ok();
+}
+
+// ------------------------------------------------------------------ tconv
+static int check_tconv(const lotus_tconv2d_desc* d, int* oh, int* ow) {
+  if (!d) return fail(LOTUS_ERR_INVALID, "tconv2d: null descriptor");
+  if (d->n <= 0 || d->c_in <= 0 || d->h <= 0 || d->w <= 0 || d->c_out <= 0 || d->kh <= 0 || d->kw <= 0)
+    return fail(LOTUS_ERR_INVALID, "tconv2d: sizes must be positive");
+  if (d->stride_h <= 0 || d->stride_w <= 0 || d->pad_h < 0 || d->pad_w < 0 || d->out_pad_h < 0 || d->out_pad_w < 0)
+    return fail(LOTUS_ERR_INVALID, "tconv2d: bad stride/padding");
+  if (d->out_pad_h >= d->stride_h || d->out_pad_w >= d->stride_w)
+    return fail(LOTUS_ERR_INVALID, "tconv2d: output_padding must be smaller than stride");
+  if (d->act < 0 || d->act > 2) return fail(LOTUS_ERR_INVALID, "tconv2d: unknown activation");
+  const long a = static_cast<long>(d->h - 1) * d->stride_h - 2L * d->pad_h + d->kh + d->out_pad_h;
+  const long b = static_cast<long>(d->w - 1) * d->stride_w - 2L * d->pad_w + d->kw + d->out_pad_w;
+  if (a <= 0 || b <= 0) return fail(LOTUS_ERR_INVALID, "tconv2d: empty output");
+  if (static_cast<long>(d->n) * a * b > kMaxIndex || static_cast<long>(d->n) * d->h * d->w > kMaxIndex)
+    return fail(LOTUS_ERR_UNSUPPORTED, "tconv2d: too many pixels");
+  if (static_cast<long>(d->kh) * d->kw * d->c_out > 65535)
+    return fail(LOTUS_ERR_UNSUPPORTED, "tconv2d: kh*kw*c_out > 65535");
+  *oh = static_cast<int>(a);
+  *ow = static_cast<int>(b);
+  return ok();
+}
+
+int lotus_tconv2d_out_hw(const lotus_tconv2d_desc* d, int* oh, int* ow) {
+  int a, b;
+  const int st = check_tconv(d, &a, &b);
+  if (st != LOTUS_OK) return st;
+  if (oh) *oh = a;
+  if (ow) *ow = b;
+  return ok();
+}
+
+size_t lotus_tconv2d_packed_weight_bytes(const lotus_tconv2d_desc* d) {
+  if (!d || d->c_out <= 0 || d->kh <= 0 || d->kw <= 0 || d->c_in <= 0) return 0;
+  return static_cast<size_t>(d->kh) * d->kw * d->c_out * round64(cs_of(d->c_in)) * 2;
+}
+
+int lotus_tconv2d_prepack(const float* w, void* w_packed, const lotus_tconv2d_desc* d, cudaStream_t stream) {
+  int oh, ow;
+  const int st = check_tconv(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  if (!w || !w_packed) return fail(LOTUS_ERR_INVALID, "tconv2d_prepack: null pointer");
+  const int cs = cs_of(d->c_in);
+  return cuda_status(
+      launch_tconv_prepack(w, w_packed, d->c_in, d->c_out, d->kh, d->kw, cs, round64(cs), stream), "tconv2d_prepack");
+}
+
+int lotus_tconv2d_fwd(const void* x, const void* w_packed, const float* bias, void* y, const lotus_tconv2d_desc* d,
+                      cudaStream_t stream) {
+  int oh, ow;
+  const int st = check_tconv(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  if (!x || !w_packed || !y) return fail(LOTUS_ERR_INVALID, "tconv2d: null x, w or y");
+  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y))
+    return fail(LOTUS_ERR_INVALID, "tconv2d: x, w and y must be 16-byte aligned");
+  const int cs_in = cs_of(d->c_in), cs_out = cs_of(d->c_out);
+  const int k_pad = round64(cs_in);
+  const size_t out_pixels = static_cast<size_t>(d->n) * oh * ow;
+  const bool no_overlap = d->stride_h >= d->kh && d->stride_w >= d->kw;
+  if (!no_overlap) {
+    return cuda_status(launch_tconv_direct(x, w_packed, k_pad, bias, y, d->n, d->c_in, cs_in, d->h, d->w, d->c_out,
+                                           cs_out, oh, ow, d->kh, d->kw, d->stride_h, d->stride_w, d->pad_h, d->pad_w,
+                                           d->act, stream),
+                       "tconv2d(direct)");
+  }
+  const bool full_cover = d->stride_h == d->kh && d->stride_w == d->kw && d->out_pad_h == 0 && d->out_pad_w == 0;
+  if (!full_cover || cs_out != d->c_out) {
+    const cudaError_t e = launch_tconv_fill_bias(y, bias, d->c_out, cs_out, out_pixels, d->act, stream);
+    if (e != cudaSuccess) return cuda_status(e, "tconv2d(fill)");
+  }
+  ConvTcArgs a{};
+  a.x = x;
+  a.w_packed = w_packed;
+  a.bias = bias;
+  a.residual = nullptr;
+  a.y = y;
+  a.H = d->h;
+  a.W = d->w;
+  a.Cs_in = cs_in;
+  a.OH = d->h;
+  a.OW = d->w;
+  a.kh = 1;
+  a.kw = 1;
+  a.sh = 1;
+  a.sw = 1;
+  a.ph = 0;
+  a.pw = 0;
+  a.n_cols = d->kh * d->kw * d->c_out;
+  a.k_pad = k_pad;
+  a.Cs_out = cs_out;
+  a.M = d->n * d->h * d->w;
+  a.act = d->act;
+  a.out_kind = 2;
+  a.t_oh = oh;
+  a.t_ow = ow;
+  a.t_sh = d->stride_h;
+  a.t_sw = d->stride_w;
+  a.t_ph = d->pad_h;
+  a.t_pw = d->pad_w;
+  a.t_kw = d->kw;
+  a.t_cout = d->c_out;
+  const char* err = "";
+  const int r = conv_tc_launch(a, stream, &err);
+  if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("tconv2d: ") + err);
+  return ok();
+}
+
+// ------------------------------------------------------------------ linear
+size_t lotus_linear_packed_weight_bytes(int in_features, int out_features) {
+  if (in_features <= 0 || out_features <= 0) return 0;
+  return static_cast<size_t>(out_features) * round64(in_features) * 2;
+}
+
+int lotus_linear_prepack(const float* w, void* w_packed, int in_features, int out_features, int fc_c, int fc_h,
+                         int fc_w, cudaStream_t stream) {
+  if (!w || !w_packed) return fail(LOTUS_ERR_INVALID, "linear_prepack: null pointer");
+  if (in_features <= 0 || out_features <= 0) return fail(LOTUS_ERR_INVALID, "linear_prepack: sizes must be positive");
+  if ((fc_c > 0 || fc_h > 0 || fc_w > 0) && static_cast<long>(fc_c) * fc_h * fc_w != in_features)
+    return fail(LOTUS_ERR_INVALID, "linear_prepack: fc_c*fc_h*fc_w != in_features");
+  return cuda_status(
+      launch_linear_prepack(w, w_packed, in_features, out_features, round64(in_features), fc_c, fc_h, fc_w, stream),
+      "linear_prepack");
+}
+
+static int check_linear(const void* x, const void* w, void* y, int m, int in_f, int out_f, int act, int out_kind) {
+  if (!x || !w || !y) return fail(LOTUS_ERR_INVALID, "linear: null x, w or y");
+  if (m <= 0 || in_f <= 0 || out_f <= 0) return fail(LOTUS_ERR_INVALID, "linear: sizes must be positive");
+  if (act < 0 || act > 2) return fail(LOTUS_ERR_INVALID, "linear: unknown activation");
+  if (out_kind != LOTUS_OUT_NHWC_F16 && out_kind != LOTUS_OUT_ROWS_F32)
+    return fail(LOTUS_ERR_INVALID, "linear: unknown out_kind");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y))
+    return fail(LOTUS_ERR_INVALID, "linear: x, w and y must be 16-byte aligned");
+  return ok();
+}
+
+int lotus_gemm_bias_fwd(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
+                        int out_features, int act, int out_kind, cudaStream_t stream) {
+  const int st = check_linear(x, w_packed, y, m, in_features, out_features, act, out_kind);
+  if (st != LOTUS_OK) return st;
+  ConvTcArgs a{};
+  a.x = x;
+  a.w_packed = w_packed;
+  a.bias = bias;
+  a.y = y;
+  a.H = 1;
+  a.W = 1;
+  a.Cs_in = cs_of(in_features);
+  a.OH = 1;
+  a.OW = 1;
+  a.kh = a.kw = a.sh = a.sw = 1;
+  a.ph = a.pw = 0;
+  a.n_cols = out_features;
+  a.k_pad = round64(in_features);
+  a.Cs_out = cs_of(out_features);
+  a.M = m;
+  a.act = act;
+  a.out_kind = out_kind;
+  const char* err = "";
+  const int r = conv_tc_launch(a, stream, &err);
+  if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("gemm: ") + err);
+  return ok();
+}
+
+int lotus_linear_fwd(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
+                     int out_features, int act, int out_kind, cudaStream_t stream) {
+  const int st = check_linear(x, w_packed, y, m, in_features, out_features, act, out_kind);
+  if (st != LOTUS_OK) return st;
+  if (m > 8)
+    return lotus_gemm_bias_fwd(x, w_packed, bias, y, m, in_features, out_features, act, out_kind, stream);
+  const bool f16 = out_kind == LOTUS_OUT_NHWC_F16;
+  const int ldy = f16 ? cs_of(out_features) : out_features;
+  cudaError_t e = launch_gemv(w_packed, 1, round64(in_features), x, 1, cs_of(in_features), bias, y, f16 ? 1 : 0, ldy,
+                              m, out_features, in_features, act, stream);
+  if (e == cudaSuccess && f16 && ldy != out_features)
+    e = cudaMemset2DAsync(static_cast<char*>(y) + static_cast<size_t>(out_features) * 2, static_cast<size_t>(ldy) * 2, 0,
+                          static_cast<size_t>(ldy - out_features) * 2, m, stream);
+  return cuda_status(e, "linear(gemv)");
+}
+
+int lotus_gemv_bias_fwd(const void* w, int w_dtype, const void* x, int x_dtype, const float* bias, void* y,
+                        int y_dtype, int batch, int h_out, int w_in, int act, cudaStream_t stream) {
+  if (!w || !x || !y) return fail(LOTUS_ERR_INVALID, "gemv: null w, x or y");
+  if (batch <= 0 || batch > 8 || h_out <= 0 || w_in <= 0)
+    return fail(LOTUS_ERR_INVALID, "gemv: need 1 <= batch <= 8 and positive sizes");
+  if ((w_dtype != 0 && w_dtype != 1) || (x_dtype != 0 && x_dtype != 1) || (y_dtype != 0 && y_dtype != 1))
+    return fail(LOTUS_ERR_INVALID, "gemv: dtype must be 0 (fp32) or 1 (fp16)");
+  if (act < 0 || act > 2) return fail(LOTUS_ERR_INVALID, "gemv: unknown activation");
+  const int ldw = w_dtype ? round64(w_in) : w_in;
+  const int ldx = x_dtype ? cs_of(w_in) : w_in;
+  const int ldy = y_dtype ? cs_of(h_out) : h_out;
+  cudaError_t e = launch_gemv(w, w_dtype, ldw, x, x_dtype, ldx, bias, y, y_dtype, ldy, batch, h_out, w_in, act, stream);
+  if (e == cudaSuccess && y_dtype && ldy != h_out)
+    e = cudaMemset2DAsync(static_cast<char*>(y) + static_cast<size_t>(h_out) * 2, static_cast<size_t>(ldy) * 2, 0,
+                          static_cast<size_t>(ldy - h_out) * 2, batch, stream);
+  return cuda_status(e, "gemv");
+}
+
+// ------------------------------------------------------------------ pooling
+int lotus_maxpool2d_out_hw(const lotus_pool2d_desc* d, int* oh, int* ow) {
+  if (!d) return fail(LOTUS_ERR_INVALID, "maxpool2d: null descriptor");
+  if (d->n <= 0 || d->c <= 0 || d->h <= 0 || d->w <= 0 || d->kh <= 0 || d->kw <= 0 || d->stride_h <= 0 ||
+      d->stride_w <= 0 || d->pad_h < 0 || d->pad_w < 0)
+    return fail(LOTUS_ERR_INVALID, "maxpool2d: bad sizes");
+  if (2 * d->pad_h > d->kh || 2 * d->pad_w > d->kw)
+    return fail(LOTUS_ERR_INVALID, "maxpool2d: padding must be at most half the kernel");
+  const int eh = d->h + 2 * d->pad_h - d->kh, ew = d->w + 2 * d->pad_w - d->kw;
+  if (eh < 0 || ew < 0) return fail(LOTUS_ERR_INVALID, "maxpool2d: kernel larger than padded input");
+  if (oh) *oh = eh / d->stride_h + 1;
+  if (ow) *ow = ew / d->stride_w + 1;
+  return ok();
+}
+
+int lotus_maxpool2d_fwd(const void* x, void* y, const lotus_pool2d_desc* d, cudaStream_t stream) {
+  int oh, ow;
+  const int st = lotus_maxpool2d_out_hw(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  if (d->act < 0 || d->act > 2) return fail(LOTUS_ERR_INVALID, "maxpool2d: unknown activation");
+  if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(LOTUS_ERR_INVALID, "maxpool2d: bad x or y pointer");
+  return cuda_status(launch_maxpool(x, y, d->n, d->c, cs_of(d->c), d->h, d->w, oh, ow, d->kh, d->kw, d->stride_h,
+                                    d->stride_w, d->pad_h, d->pad_w, d->act, stream),
+                     "maxpool2d");
+}
+
+int lotus_adaptive_avgpool2d_fwd(const void* x, void* y, int n, int c, int h, int w, int oh, int ow, int act,
+                                 int out_f32, cudaStream_t stream) {
+  if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(LOTUS_ERR_INVALID, "adaptive_avgpool2d: bad pointer");
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0 || oh <= 0 || ow <= 0)
+    return fail(LOTUS_ERR_INVALID, "adaptive_avgpool2d: sizes must be positive");
+  if (act < 0 || act > 2) return fail(LOTUS_ERR_INVALID, "adaptive_avgpool2d: unknown activation");
+  return cuda_status(launch_adaptive_avgpool(x, y, n, c, cs_of(c), h, w, oh, ow, act, out_f32 ? 1 : 0, stream),
+                     "adaptive_avgpool2d");
+}
+
+// ------------------------------------------------------------------ eltwise
+int lotus_add_act_fwd(const void* x1, const void* x2, void* y, size_t pixels, int c, int act, cudaStream_t stream) {
+  if (!x1 || !x2 || !y || !aligned16(x1) || !aligned16(x2) || !aligned16(y))
+    return fail(LOTUS_ERR_INVALID, "add: bad pointer");
+  if (c <= 0) return fail(LOTUS_ERR_INVALID, "add: channels must be positive");
+  if (act < 0 || act > 2) return fail(LOTUS_ERR_INVALID, "add: unknown activation");
+  if (pixels == 0) return ok();
+  return cuda_status(launch_add_act(x1, x2, y, pixels, c, cs_of(c), act, stream), "add");
+}
+
+int lotus_concat_channels_fwd(const void* a, int ca, const void* b, int cb, void* y, int n, int h, int w,
+                              cudaStream_t stream) {
+  if (!a || !b || !y) return fail(LOTUS_ERR_INVALID, "concat: null pointer");
+  if (ca <= 0 || cb <= 0 || n <= 0 || h <= 0 || w <= 0) return fail(LOTUS_ERR_INVALID, "concat: bad sizes");
+  const size_t pixels = static_cast<size_t>(n) * h * w;
+  return cuda_status(launch_concat(a, cs_of(ca), b, cs_of(cb), y, ca, cb, cs_of(ca + cb), pixels, stream), "concat");
+}
+
+int lotus_nchw_f32_to_nhwc_f16(const float* x, void* y, int n, int c, int h, int w, cudaStream_t stream) {
+  if (!x || !y || !aligned16(y)) return fail(LOTUS_ERR_INVALID, "nchw_to_nhwc: bad pointer");
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) return fail(LOTUS_ERR_INVALID, "nchw_to_nhwc: bad sizes");
+  return cuda_status(launch_nchw_to_nhwc(x, y, n, c, h, w, cs_of(c), stream), "nchw_to_nhwc");
+}
+
+int lotus_nhwc_f16_to_nchw_f32(const void* x, float* y, int n, int c, int h, int w, cudaStream_t stream) {
+  if (!x || !y || !aligned16(x)) return fail(LOTUS_ERR_INVALID, "nhwc_to_nchw: bad pointer");
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) return fail(LOTUS_ERR_INVALID, "nhwc_to_nchw: bad sizes");
+  return cuda_status(launch_nhwc_to_nchw(x, y, n, c, h, w, cs_of(c), stream), "nhwc_to_nchw");
+}
+
+}  // extern "C"

@@ -1,0 +1,68 @@
+// Host-side declarations of the kernel launchers behind the C ABI.
+// Everything here is internal; the public surface is include/lotus_ops.h.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lotus_impl {
+
+// Counts every kernel launch issued by the library (exported through
+// lotus_launch_count()).
+void note_launch();
+
+struct ConvTcArgs {
+  const void* x;          // NHWC fp16 [.., H, W, Cs_in]
+  const void* w_packed;   // [n_cols, k_pad] fp16
+  const float* bias;      // [bias length] or null
+  const void* residual;   // NHWC fp16 like y, or null
+  void* y;
+  int H, W, Cs_in;
+  int OH, OW;             // GEMM pixel grid (conv output, or tconv input grid)
+  int kh, kw, sh, sw, ph, pw;
+  int n_cols;             // GEMM N (Cout, or kh*kw*Cout for the tconv scatter)
+  int k_pad;              // multiple of 64
+  int Cs_out;             // pixel stride of an NHWC fp16 output
+  int M;                  // GEMM M
+  int act;
+  int out_kind;           // 0 NHWC fp16, 1 fp32 rows, 2 tconv scatter
+  int block_n;            // 0 = choose
+  int t_oh, t_ow, t_sh, t_sw, t_ph, t_pw, t_kw, t_cout;
+};
+
+int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err);
+int read_device_error();
+
+// pack.cu
+cudaError_t launch_conv_prepack(const float* w, void* wp, int cout, int cin, int kh, int kw, int cs_in, int k_pad,
+                                cudaStream_t s);
+cudaError_t launch_tconv_prepack(const float* w, void* wp, int cin, int cout, int kh, int kw, int cs_in, int k_pad,
+                                 cudaStream_t s);
+cudaError_t launch_linear_prepack(const float* w, void* wp, int in_f, int out_f, int k_pad, int fc_c, int fc_h,
+                                  int fc_w, cudaStream_t s);
+cudaError_t launch_nchw_to_nhwc(const float* x, void* y, int n, int c, int h, int w, int cs, cudaStream_t s);
+cudaError_t launch_nhwc_to_nchw(const void* x, float* y, int n, int c, int h, int w, int cs, cudaStream_t s);
+
+// pool.cu
+cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow, int kh, int kw,
+                           int sh, int sw, int ph, int pw, int act, cudaStream_t s);
+cudaError_t launch_adaptive_avgpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow,
+                                    int act, int out_f32, cudaStream_t s);
+
+// eltwise.cu
+cudaError_t launch_add_act(const void* a, const void* b, void* y, size_t pixels, int c, int cs, int act,
+                           cudaStream_t s);
+cudaError_t launch_concat(const void* a, int csa, const void* b, int csb, void* y, int ca, int cb, int csy,
+                          size_t pixels, cudaStream_t s);
+cudaError_t launch_tconv_fill_bias(void* y, const float* bias, int cout, int cs, size_t pixels, int act,
+                                   cudaStream_t s);
+cudaError_t launch_tconv_direct(const void* x, const void* wp, int k_pad, const float* bias, void* y, int n, int cin,
+                                int csi, int h, int w_, int cout, int cso, int oh, int ow, int kh, int kw, int sh,
+                                int sw, int ph, int pw, int act, cudaStream_t s);
+
+// gemv.cu
+cudaError_t launch_gemv(const void* w, int w_f16, int ldw, const void* x, int x_f16, int ldx, const float* bias,
+                        void* y, int y_f16, int ldy, int batch, int h_out, int w_in, int act, cudaStream_t s);
+
+}  // namespace lotus_impl

@@ -1,0 +1,114 @@
+// Bandwidth-bound pooling kernels on NHWC fp16 activations.
+//
+// Each thread owns one output pixel x 8 channels (one 16-byte vector), so a
+// warp reads and writes contiguous channel runs of neighbouring pixels.
+//
+// Reference counterparts: source/operator/maxpool2d.cu:16-66 (whose padding
+// taps leave the running max uninitialised when tap (0,0) is padding; here
+// padding is -inf as in PyTorch) and source/operator/adaptive_avgpool2d.cu:15-52
+// with the window start/size set in source/layer/layer_adaptive_avgpool2d.cu:42-46
+// (integer stride; here PyTorch's [floor(i*H/OH), ceil((i+1)*H/OH)) windows,
+// which agree with the reference for ResNet's 7x7 -> 1x1).
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lotus_impl {
+
+using namespace lotus_dev;
+
+__global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __restrict__ y, int n, int c, int cs, int h,
+                                    int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int act) {
+  const int groups = cs / 8;
+  const size_t total = static_cast<size_t>(n) * oh * ow * groups;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i % groups);
+    const size_t pix = i / groups;
+    const int ox = static_cast<int>(pix % ow);
+    const size_t t = pix / ow;
+    const int oy = static_cast<int>(t % oh);
+    const int img = static_cast<int>(t / oh);
+    float m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = -INFINITY;
+    const int y0 = oy * sh - ph, x0 = ox * sw - pw;
+    const __half* xb = x + static_cast<size_t>(img) * h * w * cs + g * 8;
+    for (int r = 0; r < kh; ++r) {
+      const int iy = y0 + r;
+      if (iy < 0 || iy >= h) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int ix = x0 + s;
+        if (ix < 0 || ix >= w) continue;
+        float f[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (static_cast<size_t>(iy) * w + ix) * cs)), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], f[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = (g * 8 + j < c) ? act_fn(m[j], act) : 0.f;
+    reinterpret_cast<uint4*>(y + pix * cs)[g] = pack8(m);
+  }
+}
+
+__global__ void adaptive_avgpool_nhwc_kernel(const __half* __restrict__ x, void* __restrict__ y, int n, int c, int cs,
+                                             int h, int w, int oh, int ow, int act, int out_f32) {
+  const int groups = cs / 8;
+  const size_t total = static_cast<size_t>(n) * oh * ow * groups;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i % groups);
+    const size_t pix = i / groups;
+    const int ox = static_cast<int>(pix % ow);
+    const size_t t = pix / ow;
+    const int oy = static_cast<int>(t % oh);
+    const int img = static_cast<int>(t / oh);
+    const int hs = (oy * h) / oh, he = ((oy + 1) * h + oh - 1) / oh;
+    const int ws = (ox * w) / ow, we = ((ox + 1) * w + ow - 1) / ow;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const __half* xb = x + static_cast<size_t>(img) * h * w * cs + g * 8;
+    for (int iy = hs; iy < he; ++iy) {
+      for (int ix = ws; ix < we; ++ix) {
+        float f[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (static_cast<size_t>(iy) * w + ix) * cs)), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += f[j];
+      }
+    }
+    const float inv = 1.0f / static_cast<float>((he - hs) * (we - ws));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = (g * 8 + j < c) ? act_fn(acc[j] * inv, act) : 0.f;
+    if (out_f32) {
+      float* yr = static_cast<float*>(y) + pix * c;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (g * 8 + j < c) yr[g * 8 + j] = acc[j];
+    } else {
+      reinterpret_cast<uint4*>(static_cast<__half*>(y) + pix * cs)[g] = pack8(acc);
+    }
+  }
+}
+
+cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow, int kh, int kw,
+                           int sh, int sw, int ph, int pw, int act, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
+  maxpool_nhwc_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y), n,
+                                                           c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_adaptive_avgpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow,
+                                    int act, int out_f32, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
+  adaptive_avgpool_nhwc_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half*>(x), y, n, c, cs, h, w,
+                                                                    oh, ow, act, out_f32);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace lotus_impl

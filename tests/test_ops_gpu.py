@@ -1,0 +1,239 @@
+"""GPU parity of every operator against the CPU oracle, through the C ABI.
+
+Inputs are seeded; the oracle runs on the original fp32 values, the GPU path
+rounds operands to fp16 (round-to-nearest-even) and accumulates in fp32.
+Tolerance: max-abs <= 1e-2 and rel-L2 <= 1e-3 (tests/_metrics.py); exact for
+max pooling, concatenation and layout moves.
+"""
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests._metrics import assert_close
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _k():
+    from lotusinfer_b200 import kernels
+    return kernels
+
+
+def _no_device_error():
+    from lotusinfer_b200 import abi
+    assert abi.device_error() == 0
+
+
+def _rng(seed):
+    return np.random.default_rng(seed)
+
+
+def _gpu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def _f16(a):
+    """Values as the GPU sees them after fp16 rounding."""
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+
+
+CONV_CASES = [
+    # id, n, c, h, w, cout, k, stride, pad, act, residual
+    ("cfg1_64x56x56_3x3_relu", 1, 64, 56, 56, 64, 3, 1, 1, 1, False),
+    ("stem_7x7_s2_cin3", 2, 3, 64, 64, 64, 7, 2, 3, 1, False),
+    ("ref_test_7x7_s2_cout17", 1, 3, 131, 131, 17, 7, 2, 1, 0, False),
+    ("3x3_s2_64to128", 2, 64, 28, 28, 128, 3, 2, 1, 1, False),
+    ("1x1_s2_128to256", 2, 128, 14, 14, 256, 1, 2, 0, 0, False),
+    ("3x3_residual_relu", 2, 128, 14, 14, 128, 3, 1, 1, 1, True),
+    ("3x3_512_k4608", 1, 512, 7, 7, 512, 3, 1, 1, 1, True),
+    ("cin96_general_path", 1, 96, 12, 12, 64, 3, 1, 1, 2, False),
+    ("m_tail_100px", 1, 64, 10, 10, 64, 3, 1, 1, 0, False),
+    ("unet_32to64", 1, 32, 40, 40, 64, 3, 1, 1, 1, False),
+    ("unet_1x1_sigmoid_cout1", 2, 32, 16, 16, 1, 1, 1, 0, 2, False),
+    ("alexnet_11x11_s4", 1, 3, 63, 63, 64, 11, 4, 2, 1, False),
+    ("5x5_cout192", 1, 64, 13, 13, 192, 5, 1, 2, 1, False),
+]
+
+
+@pytest.mark.parametrize("case", CONV_CASES, ids=[c[0] for c in CONV_CASES])
+def test_conv2d_parity(case):
+    K = _k()
+    _, n, c, h, w, cout, k, s, p, act, with_res = case
+    rng = _rng(zlib.crc32(case[0].encode()))
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / (c * k * k)), (cout, c, k, k)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, cout).astype(np.float32)
+    oh = (h + 2 * p - k) // s + 1
+    ow = (w + 2 * p - k) // s + 1
+    res = rng.normal(0, 1, (n, cout, oh, ow)).astype(np.float32) if with_res else None
+    want = oracle.conv2d(x, wt, b, (s, s), (p, p), act, residual=res)
+
+    xg = K.to_nhwc(_gpu(x))
+    wp = K.conv2d_prepack(_gpu(wt), c)
+    rg = K.to_nhwc(_gpu(res)) if with_res else None
+    y = K.conv2d(xg, c, wp, _gpu(b), cout, k, s, p, act, residual=rg)
+    got = K.from_nhwc(y, cout).cpu().numpy()
+    assert_close(got, want, what=case[0])
+    # pad channels are zero
+    if y.shape[-1] != cout:
+        assert torch.count_nonzero(y[..., cout:]).item() == 0
+    # fp32-row output path (no residual)
+    if not with_res:
+        y32 = K.conv2d(xg, c, wp, _gpu(b), cout, k, s, p, act, out_f32=True)
+        got32 = y32.view(n, oh, ow, cout).permute(0, 3, 1, 2).cpu().numpy()
+        assert_close(got32, want, what=case[0] + "/f32")
+    _no_device_error()
+
+
+def test_conv2d_repeatable_and_no_bias():
+    K = _k()
+    rng = _rng(11)
+    x = rng.normal(0, 1, (2, 64, 20, 20)).astype(np.float32)
+    wt = rng.normal(0, 0.05, (128, 64, 3, 3)).astype(np.float32)
+    xg, wp = K.to_nhwc(_gpu(x)), K.conv2d_prepack(_gpu(wt), 64)
+    a = K.conv2d(xg, 64, wp, None, 128, 3, 1, 1)
+    b = K.conv2d(xg, 64, wp, None, 128, 3, 1, 1)
+    assert torch.equal(a, b)
+    assert_close(K.from_nhwc(a, 128).cpu().numpy(), oracle.conv2d(x, wt, None, (1, 1), (1, 1)))
+
+
+def test_layout_round_trip_exact_for_fp16_values():
+    K = _k()
+    x = _f16(_rng(12).normal(0, 3, (3, 13, 9, 7)))
+    back = K.from_nhwc(K.to_nhwc(_gpu(x)), 13).cpu().numpy()
+    np.testing.assert_array_equal(back, x)
+
+
+def test_gemm_cfg2_parity():
+    K = _k()
+    rng = _rng(21)
+    m, nn, kk = 256, 1000, 512
+    wt = rng.normal(0, np.sqrt(1 / kk), (nn, kk)).astype(np.float32)
+    x = rng.uniform(-1, 1, (m, kk)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, nn).astype(np.float32)
+    want = oracle.gemm(x, wt, b)
+    wp = K.linear_prepack(_gpu(wt))
+    xg = _gpu(x).half()
+    got = K.linear(xg, wp, _gpu(b), kk, nn, out_f32=True, force_gemm=True).cpu().numpy()
+    assert_close(got, want, what="gemm cfg2")
+    # relu + fp16 rows out
+    got16 = K.linear(xg, wp, _gpu(b), kk, nn, act=1, out_f32=False, force_gemm=True)[:, :nn].float().cpu().numpy()
+    assert_close(got16, oracle.gemm(x, wt, b, act=1), what="gemm cfg2 relu f16")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 9, 33])
+def test_linear_dispatch_gemv_and_gemm(m):
+    K = _k()
+    rng = _rng(22 + m)
+    nn, kk = 1000, 512
+    wt = rng.normal(0, np.sqrt(1 / kk), (nn, kk)).astype(np.float32)
+    x = rng.uniform(-1, 1, (m, kk)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, nn).astype(np.float32)
+    wp = K.linear_prepack(_gpu(wt))
+    got = K.linear(_gpu(x).half(), wp, _gpu(b), kk, nn, act=1, out_f32=True).cpu().numpy()
+    assert_close(got, oracle.gemm(x, wt, b, act=1), what=f"linear m={m}")
+
+
+def test_linear_flatten_permutation():
+    """AlexNet's flatten of an NCHW [256,6,6] map: NHWC activations + column-permuted weights."""
+    K = _k()
+    rng = _rng(23)
+    n, c, h, w, nn = 3, 16, 3, 3, 40
+    x = rng.normal(0, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, 0.1, (nn, c * h * w)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, nn).astype(np.float32)
+    want = oracle.gemm(x.reshape(n, -1), wt, b)
+    xg = K.to_nhwc(_gpu(x)).reshape(n, -1)  # (h, w, c) order
+    wp = K.linear_prepack(_gpu(wt), fc_chw=(c, h, w))
+    for force in (False, True):
+        got = K.linear(xg, wp, _gpu(b), c * h * w, nn, out_f32=True, force_gemm=force).cpu().numpy()
+        assert_close(got, want, what=f"flatten force_gemm={force}")
+
+
+@pytest.mark.parametrize("shape", [(1000, 512, 1), (512, 512, 1), (4096, 9216, 1), (1000, 511, 2), (37, 96, 8)])
+def test_gemv_reference_semantics_fp32(shape):
+    """Fgemva semantics: fp32 W [H, W], fp32 x, fp32 y."""
+    K = _k()
+    hh, ww, batch = shape
+    rng = _rng(hh + ww)
+    wt = rng.normal(0, np.sqrt(1 / ww), (hh, ww)).astype(np.float32)
+    x = rng.uniform(-1, 1, (batch, ww)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, hh).astype(np.float32)
+    got = K.gemv(_gpu(wt), _gpu(x), _gpu(b)).cpu().numpy()
+    assert_close(got, oracle.gemv(wt, x, b), max_abs_tol=1e-4, rel_tol=1e-5, what=f"gemv {shape}")
+
+
+@pytest.mark.parametrize("case", [
+    ("resnet_3x3_s2_p1", 2, 64, 112, 112, 3, 2, 1),
+    ("unet_2x2_s2", 1, 32, 64, 64, 2, 2, 0),
+    ("alexnet_3x3_s2", 2, 64, 55, 55, 3, 2, 0),
+    ("ref_test_9x9_s2_p4", 1, 3, 65, 65, 9, 2, 4),
+], ids=lambda c: c[0])
+def test_maxpool_exact(case):
+    K = _k()
+    _, n, c, h, w, k, s, p = case
+    x = _f16(_rng(31).normal(0, 1, (n, c, h, w)) - 2.0)  # negatives: -inf padding matters
+    for act in (0, 1):
+        want = oracle.maxpool2d(x, (k, k), (s, s), (p, p), act)
+        got = K.from_nhwc(K.maxpool2d(K.to_nhwc(_gpu(x)), c, k, s, p, act), c).cpu().numpy()
+        np.testing.assert_array_equal(got, _f16(want))
+
+
+@pytest.mark.parametrize("case", [((2, 512, 7, 7), (1, 1)), ((1, 256, 6, 6), (6, 6)), ((1, 24, 13, 9), (6, 4)),
+                                  ((1, 3, 257, 257), (64, 64))])
+def test_adaptive_avgpool(case):
+    K = _k()
+    shape, out = case
+    x = _f16(_rng(41).normal(0, 1, shape))
+    want = oracle.adaptive_avgpool2d(x, out)
+    xg = K.to_nhwc(_gpu(x))
+    got = K.from_nhwc(K.adaptive_avgpool2d(xg, shape[1], out), shape[1]).cpu().numpy()
+    assert_close(got, want, what=f"aap {case}")
+    got32 = K.adaptive_avgpool2d(xg, shape[1], out, out_f32=True).cpu().numpy()
+    got32 = got32.reshape(shape[0], out[0], out[1], shape[1]).transpose(0, 3, 1, 2)
+    assert_close(got32, want, max_abs_tol=1e-5, rel_tol=1e-6, what=f"aap f32 {case}")
+
+
+def test_add_act_and_concat():
+    K = _k()
+    rng = _rng(51)
+    a = _f16(rng.normal(0, 1, (2, 20, 9, 9)))
+    b = _f16(rng.normal(0, 1, (2, 20, 9, 9)))
+    got = K.from_nhwc(K.add_act(K.to_nhwc(_gpu(a)), K.to_nhwc(_gpu(b)), 20, 1), 20).cpu().numpy()
+    assert_close(got, oracle.add(a, b, 1), what="add relu")
+    for ca, cb in ((32, 32), (3, 5), (256, 256)):
+        x1 = _f16(rng.normal(0, 1, (1, ca, 6, 7)))
+        x2 = _f16(rng.normal(0, 1, (1, cb, 6, 7)))
+        y = K.concat_channels(K.to_nhwc(_gpu(x1)), ca, K.to_nhwc(_gpu(x2)), cb)
+        np.testing.assert_array_equal(K.from_nhwc(y, ca + cb).cpu().numpy(), oracle.concat(x1, x2))
+
+
+TCONV_CASES = [
+    ("unet_upconv4_512to256", 1, 512, 16, 16, 256, 2, 2, 0, 0),
+    ("unet_upconv1_64to32", 2, 64, 32, 32, 32, 2, 2, 0, 0),
+    ("ref_test_k2_s3_gaps", 1, 16, 64, 64, 8, 2, 3, 0, 0),
+    ("overlap_k3_s2_p1_op1", 1, 24, 9, 7, 12, 3, 2, 1, 1),
+    ("cout5_k2_s2", 1, 8, 5, 5, 5, 2, 2, 0, 0),
+]
+
+
+@pytest.mark.parametrize("case", TCONV_CASES, ids=[c[0] for c in TCONV_CASES])
+def test_tconv2d_parity(case):
+    K = _k()
+    _, n, cin, h, w, cout, k, s, p, op = case
+    rng = _rng(61)
+    x = rng.uniform(-1, 1, (n, cin, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(1.0 / cin), (cin, cout, k, k)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, cout).astype(np.float32)
+    for act in (0, 1):
+        want = oracle.tconv2d(x, wt, b, (s, s), (p, p), (op, op), act)
+        wp = K.tconv2d_prepack(_gpu(wt))
+        y = K.tconv2d(K.to_nhwc(_gpu(x)), cin, wp, _gpu(b), cout, k, s, p, op, act)
+        assert_close(K.from_nhwc(y, cout).cpu().numpy(), want, what=f"{case[0]} act={act}")
+    _no_device_error()
