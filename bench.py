@@ -1,0 +1,307 @@
+"""ResNet-18 batch-256 inference throughput on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+A step is one forward pass of ResNet-18 over one batch of 256 synthetic
+3x224x224 images (inputs ~N(0,1), random Kaiming weights, seed 0) through the
+native graph runtime (tcgen05 convs, CUDA-graph replay).  Weak scaling: every
+rank runs its own batch of 256 and the logits are gathered over NCCL once per
+step.  Timing: W untimed warm-up steps, then exactly K steps between a barrier
+plus device synchronisation on both sides, CUDA events on the graph stream,
+max over ranks.  The input batch (154 MB fp32) and the activations (~4 GB)
+exceed the 126 MB L2, so no flush is needed between steps.
+
+Rank 0 prints one JSON line.  `e2e` repeats the measurement through the
+public API with host buffers: pinned-host -> device input copy, forward, and
+device -> host logits copy inside every timed step.  `roofline` covers the
+dominant kernel (the tcgen05 implicit-GEMM conv), from per-layer CUDA events
+of one profiled pass.  `cpu_baseline` times the CPU oracle on a small sample.
+`--impl reference` times the reference path on the host cores instead (the
+reference has no CPU inference path of its own; its per-operator host loops
+are restated by the oracle), on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ResNet-18 images/sec (bs256) at 1/2/4/8 B200; conv TFLOPS as % of tensor peak"
+UNIT = "images/s"
+MODEL_DIR = os.environ.get("LOTUS_MODEL_DIR", os.path.join(tempfile.gettempdir(), "lotus_models"))
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained"), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of one GPU during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None}
+
+
+def cpu_baseline_sample(seconds_budget: float = 20.0):
+    """The oracle's ResNet-18 on all host threads over a bounded image sample."""
+    from lotusinfer_b200 import synth
+    from oracle import oracle
+    param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
+    from oracle import pnnx_text
+    g = pnnx_text.load(param)
+    w = pnnx_text.shaped_weights(g, pnnx_text.read_weights(binp))
+    x1 = synth.synthetic_input("resnet18", 1, seed=0)
+    t0 = time.perf_counter()
+    oracle.run_graph(param, binp, x1, weights=w)
+    t1 = time.perf_counter() - t0
+    n = int(max(1, min(16, (seconds_budget - t1) / max(t1, 1e-3))))
+    x = synth.synthetic_input("resnet18", n, seed=0)
+    t0 = time.perf_counter()
+    oracle.run_graph(param, binp, x, weights=w)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"ResNet-18 forward over {n} of the 256 synthetic images (fp32 oracle, OpenMP)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from lotusinfer_b200 import synth
+    from oracle import oracle, pnnx_text
+    param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
+    g = pnnx_text.load(param)
+    w = pnnx_text.shaped_weights(g, pnnx_text.read_weights(binp))
+    per_step = int(os.environ.get("LOTUS_REF_IMAGES", "1"))
+    x = synth.synthetic_input("resnet18", per_step, seed=0)
+    for _ in range(max(args.warmup, 0)):
+        oracle.run_graph(param, binp, x, weights=w)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.run_graph(param, binp, x, weights=w)
+    dt = time.perf_counter() - t0
+    val = per_step * args.steps / dt
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "resnet18_bs256_per_gpu", "model": "ResNet-18", "batch_per_gpu": 256,
+                       "sample_images_per_step": per_step, "parallelism": "host cores"},
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+                             "sample": f"{per_step} image(s) of the batch per step through the fp32 oracle "
+                                       "(the reference has no CPU inference path; its test host loops, restated)"},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-reps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from lotusinfer_b200 import abi, synth
+    from lotusinfer_b200.graph import Graph
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    B = args.batch
+    param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
+    g = Graph(param, binp, B, device=local)
+    gstream = torch.cuda.ExternalStream(g.stream, device=torch.device("cuda", local))
+    x_host = torch.from_numpy(synth.synthetic_input("resnet18", B, seed=rank)).pin_memory()
+    logits_host = torch.empty((B, 1000), dtype=torch.float32).pin_memory()
+    gathered = torch.empty((world * B, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
+    logits_dev = torch.empty((B, 1000), dtype=torch.float32, device="cuda") if world > 1 else None
+
+    def gather():
+        # the only collective: all ranks' logits gathered once per step, ordered after the forward
+        if world > 1:
+            g.get_output_into(logits_dev.data_ptr(), logits_dev.numel(), stream=g.stream)
+            with torch.cuda.stream(gstream):
+                dist.all_gather_into_tensor(gathered, logits_dev)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # inputs resident in HBM for the device-timed measurement
+    g.set_input_ptr(x_host.data_ptr(), x_host.numel())
+    for _ in range(args.warmup):
+        g.forward()
+        gather()
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(gstream)
+        for _ in range(args.steps):
+            g.forward()
+            gather()
+        ev1.record(gstream)
+        barrier()
+    clocks = clk.summary()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * B * args.steps / (ms / 1000.0)
+
+    # end to end through the public API with host buffers
+    for _ in range(2):
+        g.set_input_ptr(x_host.data_ptr(), x_host.numel())
+        g.forward()
+        gather()
+        g.get_output_into(logits_host.data_ptr(), logits_host.numel())
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(gstream)
+    for _ in range(args.steps):
+        g.set_input_ptr(x_host.data_ptr(), x_host.numel())
+        g.forward()
+        gather()
+        g.get_output_into(logits_host.data_ptr(), logits_host.numel())
+    e1.record(gstream)
+    barrier()
+    ems = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e = {"value": world * B * args.steps / (ems / 1000.0), "unit": UNIT,
+           "h2d_bytes_per_step": int(x_host.numel() * 4), "d2h_bytes_per_step": int(logits_host.numel() * 4),
+           "ms_per_step": ems / args.steps}
+
+    # roofline of the dominant kernel: per-layer CUDA events of eager passes on the graph stream
+    g.set_input_ptr(x_host.data_ptr(), x_host.numel())
+    layer_ms = g.profile_layers(args.profile_reps)
+    layers = g.layers()
+    conv_ms = sum(t for t, l in zip(layer_ms, layers) if l["type"] == "nn.Conv2d")
+    conv_flops = sum(l["flops"] for l in layers if l["type"] == "nn.Conv2d")
+    conv_launches = sum(1 for l in layers if l["type"] == "nn.Conv2d")
+    peak, peak_sus, hbm, peak_src = _peaks()
+    achieved = conv_flops / (conv_ms / 1000.0) / 1e12 if conv_ms > 0 else 0.0
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "conv_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("dram_bytes_per_forward_bs256")
+        except Exception:
+            traffic = None
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak if peak else None, "traffic": traffic,
+                "kernel": "conv_tc_kernel (tcgen05 implicit GEMM, fp16 x fp16 -> fp32)",
+                "peak_source": f"{peak_src} bf16/fp16 dense burst", "frac_of_sustained": achieved / peak_sus if peak_sus else None,
+                "conv_ms_per_forward": conv_ms, "conv_gflop_per_forward": conv_flops / 1e9,
+                "conv_launches_per_forward": conv_launches,
+                "forward_ms_eager": sum(layer_ms)}
+
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "resnet18_bs256_per_gpu", "model": "ResNet-18", "global_batch": world * B,
+                       "batch_per_gpu": B, "image": "3x224x224", "seq_len": None, "parallelism": f"dp{world}",
+                       "weights": "random Kaiming-normal, seed 0", "input": "N(0,1) synthetic",
+                       "l2": "inputs larger than L2 (154 MB input batch, ~4 GB activations per step); no flush",
+                       "precision": "fp16 operands, fp32 accumulate (TMEM), fp16 activations"},
+            "roofline": roofline, "clocks": clocks, "e2e": e2e,
+            "gpu_launches": g.launches_per_forward() * args.steps,
+            "layer_ms": {l["name"]: round(t, 4) for t, l in zip(layer_ms, layers)}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample()
+    elif rank == 0:
+        line["cpu_baseline"] = None
+    assert abi.device_error() == 0
+    g.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,72 @@
+/*
+ * lotus_graph.h - C ABI of the native PNNX graph runtime (one GPU per graph).
+ *
+ * Wraps lotus::Graph, the counterpart of the reference's lotus::Graph
+ * (include/graph.hpp:15-43, source/graph.cpp): load a .pnnx.param/.pnnx.bin
+ * pair for a fixed batch, take an NCHW fp32 input batch, run every layer,
+ * expose the NCHW fp32 output.  All calls return 0 on success or a negative
+ * LOTUS_ERR_* status with the text in lotus_last_error_string(), except
+ * lotus_graph_create which returns NULL on failure.
+ */
+#ifndef LOTUS_GRAPH_H_
+#define LOTUS_GRAPH_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#include "lotus_ops.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct lotus_graph lotus_graph;
+
+#define LOTUS_GRAPH_NO_CUDA_GRAPH 1     /* flags: launch layers eagerly on every forward */
+#define LOTUS_GRAPH_NO_RESIDUAL_FUSION 2 /* flags: keep pnnx.Expression add as its own kernel */
+
+/* Graph(param, bin, batch) of the reference (source/graph.cpp:44-111) on
+ * `device` (-1 = current). */
+lotus_graph* lotus_graph_create(const char* param_path, const char* bin_path, int batch, int device, int flags);
+void lotus_graph_destroy(lotus_graph* g);
+
+/* Logical NCHW shapes of the input and output operands; *ndim <= 8. */
+int lotus_graph_input_shape(const lotus_graph* g, int64_t* dims, int* ndim);
+int lotus_graph_output_shape(const lotus_graph* g, int64_t* dims, int* ndim);
+/* Device pointers of the fp32 input and output buffers (owned by the graph). */
+float* lotus_graph_input_ptr(lotus_graph* g);
+const float* lotus_graph_output_ptr(lotus_graph* g);
+/* The graph's own stream. */
+cudaStream_t lotus_graph_stream(const lotus_graph* g);
+
+/* Asynchronous copies on `stream` (NULL = graph stream) from / to a host or
+ * device buffer (unified addressing); `count` floats must equal the operand
+ * size.  Host buffers should be pinned for the copy to be asynchronous. */
+int lotus_graph_set_input(lotus_graph* g, const float* src, size_t count, cudaStream_t stream);
+int lotus_graph_get_output(lotus_graph* g, float* dst, size_t count, cudaStream_t stream);
+
+/* Enqueue one forward pass on `stream` (NULL = graph stream).  The first call
+ * runs eagerly; later calls replay a captured CUDA graph unless the graph was
+ * created with LOTUS_GRAPH_NO_CUDA_GRAPH. */
+int lotus_graph_forward(lotus_graph* g, cudaStream_t stream);
+/* Reference Graph::Forward(): forward on the graph stream and wait. */
+int lotus_graph_forward_sync(lotus_graph* g);
+/* Wait for all work queued on the graph stream. */
+int lotus_graph_synchronize(lotus_graph* g);
+
+/* Introspection for profiling and tests. */
+int lotus_graph_layer_count(const lotus_graph* g);
+const char* lotus_graph_layer_name(const lotus_graph* g, int i);
+const char* lotus_graph_layer_type(const lotus_graph* g, int i);
+double lotus_graph_layer_flops(const lotus_graph* g, int i);
+double lotus_graph_layer_bytes(const lotus_graph* g, int i);
+int lotus_graph_launches_per_forward(const lotus_graph* g);
+/* Mean device milliseconds per layer over `reps` eager runs into ms[layer_count]. */
+int lotus_graph_profile_layers(lotus_graph* g, int reps, float* ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOTUS_GRAPH_H_ */

@@ -25,6 +25,11 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 static thread_local std::string t_last_error;
 
+int set_error(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
 static int fail(int code, const std::string& msg) {
   t_last_error = msg;
   return code;

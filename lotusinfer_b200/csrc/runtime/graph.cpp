@@ -1,0 +1,382 @@
+#include "graph.hpp"
+
+#include <algorithm>
+#include <queue>
+#include <set>
+#include <stdexcept>
+
+namespace lotus {
+
+namespace {
+
+const pnnx::Parameter& need(const pnnx::Operator& op, const std::string& key) {
+  auto it = op.params.find(key);
+  if (it == op.params.end()) throw std::runtime_error(op.name + ": missing parameter '" + key + "'");
+  return it->second;
+}
+
+int pair0(const pnnx::Parameter& p) { return p.ai.empty() ? p.i : p.ai.at(0); }
+int pair1(const pnnx::Parameter& p) { return p.ai.size() < 2 ? pair0(p) : p.ai.at(1); }
+
+bool is_act(const std::string& t) { return t == "nn.ReLU" || t == "F.sigmoid"; }
+
+}  // namespace
+
+Graph::Graph(const std::string& param_path, const std::string& bin_path, uint32_t batch_size)
+    : Graph(param_path, bin_path, batch_size, Options()) {}
+
+Graph::Graph(const std::string& param_path, const std::string& bin_path, uint32_t batch_size, const Options& opt)
+    : batch_(batch_size), opt_(opt) {
+  if (batch_size == 0) throw std::runtime_error("batch size must be positive");
+  if (opt_.device >= 0) CudaCheck(cudaSetDevice(opt_.device), "cudaSetDevice");
+  CudaCheck(cudaGetDevice(&device_), "cudaGetDevice");
+  CudaCheck(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+  try {
+    Build(param_path, bin_path);
+  } catch (...) {
+    cudaStreamDestroy(stream_);
+    throw;
+  }
+}
+
+Graph::~Graph() {
+  if (exec_) cudaGraphExecDestroy(exec_);
+  if (stream_) {
+    cudaStreamSynchronize(stream_);
+    cudaStreamDestroy(stream_);
+  }
+}
+
+void Graph::Build(const std::string& param_path, const std::string& bin_path) {
+  pnnx::Graph g;
+  g.Load(param_path, bin_path);
+
+  std::map<std::string, const pnnx::Operator*> op_by_name;
+  for (auto& op : g.ops) op_by_name[op.name] = &op;
+
+  // graph input / output operands (source/graph.cpp:52-63)
+  for (auto& op : g.ops) {
+    if (op.type == "pnnx.Input") {
+      if (!input_operand_.empty() || op.outputs.size() != 1) throw std::runtime_error("graph must have one input");
+      input_operand_ = op.outputs[0];
+    } else if (op.type == "pnnx.Output") {
+      if (!output_operand_.empty() || op.inputs.size() != 1) throw std::runtime_error("graph must have one output");
+      output_operand_ = op.inputs[0];
+    }
+  }
+  if (input_operand_.empty() || output_operand_.empty()) throw std::runtime_error("graph input/output not found");
+
+  // logical shapes with dim 0 := batch (source/graph.cpp:66-72)
+  std::map<std::string, std::vector<uint32_t>> shapes;
+  for (auto& kv : g.operands) {
+    const auto& info = kv.second;
+    if (info.type != "f32") throw std::runtime_error("operand " + kv.first + ": only f32 models are supported");
+    std::vector<uint32_t> s;
+    for (size_t i = 0; i < info.shape.size(); ++i) {
+      if (i > 0 && info.shape[i] <= 0) throw std::runtime_error("operand " + kv.first + ": dynamic shape");
+      s.push_back(i == 0 ? batch_ : static_cast<uint32_t>(info.shape[i]));
+    }
+    shapes[kv.first] = s;
+  }
+
+  // layers, with ReLU/sigmoid folded into the producer (source/layer/layer_conv2d.cu:129-141)
+  for (auto& op : g.ops) {
+    const std::string& t = op.type;
+    if (t == "pnnx.Input" || t == "pnnx.Output" || is_act(t)) continue;
+    std::shared_ptr<Layer> layer;
+    if (t == "nn.Conv2d") {
+      if (need(op, "groups").i != 1) throw std::runtime_error(op.name + ": only groups=1 is supported");
+      const auto& dil = need(op, "dilation");
+      if (pair0(dil) != 1 || pair1(dil) != 1) throw std::runtime_error(op.name + ": only dilation 1 is supported");
+      auto pm = op.params.find("padding_mode");
+      if (pm != op.params.end() && pm->second.s != "zeros") throw std::runtime_error(op.name + ": zero padding only");
+      const auto& ks = need(op, "kernel_size");
+      const auto& st = need(op, "stride");
+      const auto& pd = need(op, "padding");
+      if (pd.type == 4) throw std::runtime_error(op.name + ": string padding is not supported");
+      layer = std::make_shared<Conv2dLayer>(op, need(op, "in_channels").i, need(op, "out_channels").i, pair0(ks),
+                                            pair1(ks), pair0(st), pair1(st), pair0(pd), pair1(pd), stream_);
+    } else if (t == "nn.ConvTranspose2d") {
+      if (need(op, "groups").i != 1) throw std::runtime_error(op.name + ": only groups=1 is supported");
+      const auto& dil = need(op, "dilation");
+      if (pair0(dil) != 1 || pair1(dil) != 1) throw std::runtime_error(op.name + ": only dilation 1 is supported");
+      const auto& ks = need(op, "kernel_size");
+      const auto& st = need(op, "stride");
+      const auto& pd = need(op, "padding");
+      auto opad_it = op.params.find("output_padding");
+      int oph = 0, opw = 0;
+      if (opad_it != op.params.end()) {
+        oph = pair0(opad_it->second);
+        opw = pair1(opad_it->second);
+      }
+      layer = std::make_shared<TransposedConv2dLayer>(op, need(op, "in_channels").i, need(op, "out_channels").i,
+                                                      pair0(ks), pair1(ks), pair0(st), pair1(st), pair0(pd),
+                                                      pair1(pd), oph, opw, stream_);
+    } else if (t == "nn.Linear") {
+      int fc_c = 0, fc_h = 0, fc_w = 0;
+      const auto& in_name = op.inputs.at(0);
+      const auto& prod = g.operands.at(in_name).producer;
+      if (!prod.empty() && op_by_name.at(prod)->type == "torch.flatten") {
+        const auto& src = shapes.at(op_by_name.at(prod)->inputs.at(0));
+        if (src.size() == 4 && (src[2] != 1 || src[3] != 1)) {
+          fc_c = static_cast<int>(src[1]);
+          fc_h = static_cast<int>(src[2]);
+          fc_w = static_cast<int>(src[3]);
+        }
+      }
+      layer = std::make_shared<LinearLayer>(op, need(op, "in_features").i, need(op, "out_features").i, fc_c, fc_h,
+                                            fc_w, stream_);
+    } else if (t == "nn.MaxPool2d") {
+      auto cm = op.params.find("ceil_mode");
+      if (cm != op.params.end() && cm->second.b) throw std::runtime_error(op.name + ": ceil_mode is not supported");
+      auto ri = op.params.find("return_indices");
+      if (ri != op.params.end() && ri->second.b)
+        throw std::runtime_error(op.name + ": return_indices is not supported");
+      const auto& ks = need(op, "kernel_size");
+      const auto& st = need(op, "stride");
+      const auto& pd = need(op, "padding");
+      layer = std::make_shared<Maxpool2dLayer>(op, pair0(ks), pair1(ks), pair0(st), pair1(st), pair0(pd), pair1(pd));
+    } else if (t == "nn.AdaptiveAvgPool2d") {
+      const auto& os = need(op, "output_size");
+      layer = std::make_shared<AdaptiveAvgpool2dLayer>(op, pair0(os), pair1(os));
+    } else if (t == "pnnx.Expression") {
+      layer = std::make_shared<ExpressionLayer>(op);
+    } else if (t == "torch.flatten") {
+      layer = std::make_shared<FlattenLayer>(op);
+    } else if (t == "torch.cat") {
+      layer = std::make_shared<CatLayer>(op);
+    } else {
+      throw std::runtime_error("unsupported layer type " + t);
+    }
+    // fold a sole ReLU / sigmoid consumer
+    const auto& consumers = g.operands.at(op.outputs.at(0)).consumers;
+    if (consumers.size() == 1 && is_act(op_by_name.at(consumers[0])->type) && t != "torch.flatten") {
+      const auto* act = op_by_name.at(consumers[0]);
+      layer->af_ = act->type == "nn.ReLU" ? RELU : SIGMOID;
+      layer->outputs_name_ = {act->outputs.at(0)};
+    }
+    if (layers_.count(op.name)) throw std::runtime_error("duplicate layer name " + op.name);
+    layers_[op.name] = layer;
+    layer_order_.push_back(op.name);
+  }
+  // every activation op must have been folded
+  for (auto& op : g.ops) {
+    if (!is_act(op.type)) continue;
+    bool folded = false;
+    for (auto& kv : layers_)
+      if (!kv.second->outputs_name_.empty() && kv.second->outputs_name_[0] == op.outputs.at(0)) folded = true;
+    if (!folded) throw std::runtime_error(op.name + ": activation without a foldable producer is not supported");
+  }
+
+  // residual fusion: conv (sole consumer: add) -> add (-> act) becomes conv with residual
+  auto consumers_of = [&](const std::string& operand) {
+    std::vector<std::shared_ptr<Layer>> c;
+    for (auto& kv : layers_)
+      for (auto& in : kv.second->inputs_name_)
+        if (in == operand) c.push_back(kv.second);
+    return c;
+  };
+  auto producer_of = [&](const std::string& operand) -> std::shared_ptr<Layer> {
+    for (auto& kv : layers_)
+      for (auto& out : kv.second->outputs_name_)
+        if (out == operand) return kv.second;
+    return nullptr;
+  };
+  if (opt_.fuse_residual) {
+    std::vector<std::string> fused;
+    for (auto& name : layer_order_) {
+      auto expr = std::dynamic_pointer_cast<ExpressionLayer>(layers_.at(name));
+      if (!expr) continue;
+      for (int side = 0; side < 2; ++side) {
+        const std::string& mine = expr->inputs_name_[side];
+        const std::string& other = expr->inputs_name_[1 - side];
+        auto conv = std::dynamic_pointer_cast<Conv2dLayer>(producer_of(mine));
+        if (!conv || conv->af_ != NONE || !conv->Residual().empty() || mine == other) continue;
+        if (consumers_of(mine).size() != 1) continue;
+        if (shapes.at(mine) != shapes.at(other)) continue;
+        conv->SetResidual(other);
+        conv->af_ = expr->af_;
+        conv->outputs_name_ = expr->outputs_name_;
+        fused.push_back(name);
+        break;
+      }
+    }
+    for (auto& n : fused) {
+      layers_.erase(n);
+      layer_order_.erase(std::find(layer_order_.begin(), layer_order_.end(), n));
+    }
+  }
+
+  // operands that carry data after fusion
+  std::set<std::string> live;
+  for (auto& kv : layers_) {
+    for (auto& n : kv.second->inputs_name_) live.insert(n);
+    for (auto& n : kv.second->outputs_name_) live.insert(n);
+  }
+  live.insert(input_operand_);
+  live.insert(output_operand_);
+
+  // input conversion: NCHW fp32 -> NHWC fp16
+  const std::string in_nhwc = input_operand_ + "@nhwc";
+  for (auto& kv : layers_)
+    for (auto& n : kv.second->inputs_name_)
+      if (n == input_operand_) n = in_nhwc;
+  {
+    auto l = std::make_shared<InputConvertLayer>(input_operand_, in_nhwc);
+    layers_[l->Name()] = l;
+    layer_order_.insert(layer_order_.begin(), l->Name());
+  }
+  shapes[in_nhwc] = shapes.at(input_operand_);
+
+  // output: Linear and 1x1 adaptive pooling write fp32 rows directly, others convert
+  auto out_prod = producer_of(output_operand_);
+  if (!out_prod) throw std::runtime_error("graph output has no producer");
+  const bool direct_f32 = std::dynamic_pointer_cast<LinearLayer>(out_prod) != nullptr ||
+                          (std::dynamic_pointer_cast<AdaptiveAvgpool2dLayer>(out_prod) != nullptr &&
+                           (shapes.at(output_operand_).size() == 2 ||
+                            (shapes.at(output_operand_)[2] == 1 && shapes.at(output_operand_)[3] == 1)));
+  if (!direct_f32) {
+    const std::string out_nhwc = output_operand_ + "@nhwc";
+    out_prod->outputs_name_ = {out_nhwc};
+    shapes[out_nhwc] = shapes.at(output_operand_);
+    auto l = std::make_shared<OutputConvertLayer>(out_nhwc, output_operand_);
+    layers_[l->Name()] = l;
+    layer_order_.push_back(l->Name());
+  }
+
+  // allocate operand tensors (flatten outputs alias their input)
+  std::set<std::string> aliased;
+  for (auto& kv : layers_)
+    if (std::dynamic_pointer_cast<FlattenLayer>(kv.second)) aliased.insert(kv.second->outputs_name_[0]);
+  std::set<std::string> needed;
+  for (auto& kv : layers_) {
+    for (auto& n : kv.second->inputs_name_) needed.insert(n);
+    for (auto& n : kv.second->outputs_name_) needed.insert(n);
+  }
+  for (auto& n : needed) {
+    auto opnd = std::make_shared<Operand>();
+    opnd->name_ = n;
+    auto pit = g.operands.find(n);
+    if (pit != g.operands.end()) {
+      opnd->producer_ = pit->second.producer;
+      opnd->consumers_ = pit->second.consumers;
+    }
+    const auto& s = shapes.at(n);
+    const bool f32 = (n == input_operand_) || (n == output_operand_);
+    if (!aliased.count(n)) opnd->tensor_ = Tensor(s, f32 ? Format::kNCHW_F32 : Format::kNHWC_F16);
+    operands_[n] = opnd;
+  }
+
+  TopoSortLayers();
+  // bind in order so flatten aliases exist before their consumers bind
+  for (auto& l : topo_sorted_layers_) l->Bind(operands_);
+  CudaCheck(cudaStreamSynchronize(stream_), "graph build");
+}
+
+void Graph::TopoSortLayers() {
+  // Kahn's algorithm over operand dependencies (source/graph.cpp:5-40);
+  // ties keep the file order so the schedule is deterministic.
+  std::map<std::string, std::string> producer;
+  for (auto& kv : layers_)
+    for (auto& o : kv.second->outputs_name_) producer[o] = kv.first;
+  std::map<std::string, int> indeg;
+  std::map<std::string, std::vector<std::string>> succ;
+  for (auto& kv : layers_) {
+    int d = 0;
+    for (auto& in : kv.second->inputs_name_) {
+      auto it = producer.find(in);
+      if (it != producer.end()) {
+        ++d;
+        succ[it->second].push_back(kv.first);
+      }
+    }
+    indeg[kv.first] = d;
+  }
+  std::map<std::string, size_t> rank;
+  for (size_t i = 0; i < layer_order_.size(); ++i) rank[layer_order_[i]] = i;
+  auto cmp = [&](const std::string& a, const std::string& b) { return rank.at(a) > rank.at(b); };
+  std::priority_queue<std::string, std::vector<std::string>, decltype(cmp)> ready(cmp);
+  for (auto& kv : indeg)
+    if (kv.second == 0) ready.push(kv.first);
+  topo_sorted_layers_.clear();
+  while (!ready.empty()) {
+    const std::string n = ready.top();
+    ready.pop();
+    topo_sorted_layers_.push_back(layers_.at(n));
+    for (auto& s : succ[n])
+      if (--indeg[s] == 0) ready.push(s);
+  }
+  if (topo_sorted_layers_.size() != layers_.size()) throw std::runtime_error("the graph is not acyclic");
+}
+
+void Graph::InitialiseInput(const std::vector<float>& input) { InputTensor().AssignData(input); }
+
+std::shared_ptr<Operand> Graph::Output() { return operands_.at(output_operand_); }
+
+void Graph::RunLayers(cudaStream_t s) {
+  for (auto& l : topo_sorted_layers_) l->Forward(s);
+}
+
+void Graph::ForwardAsync(cudaStream_t stream) {
+  cudaStream_t s = stream ? stream : stream_;
+  CudaCheck(cudaSetDevice(device_), "cudaSetDevice");
+  if (!opt_.cuda_graph || eager_runs_ == 0) {
+    RunLayers(s);
+    ++eager_runs_;
+    return;
+  }
+  if (!exec_) {
+    cudaGraph_t graph = nullptr;
+    CudaCheck(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      RunLayers(s);
+    } catch (...) {
+      cudaStreamEndCapture(s, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    CudaCheck(cudaStreamEndCapture(s, &graph), "end capture");
+    cudaError_t e = cudaGraphInstantiate(&exec_, graph, 0);
+    cudaGraphDestroy(graph);
+    CudaCheck(e, "graph instantiate");
+  }
+  CudaCheck(cudaGraphLaunch(exec_, s), "graph launch");
+}
+
+void Graph::Forward() {
+  ForwardAsync(stream_);
+  CudaCheck(cudaStreamSynchronize(stream_), "Forward");
+}
+
+std::vector<float> Graph::ProfileLayers(int reps) {
+  CudaCheck(cudaSetDevice(device_), "cudaSetDevice");
+  const size_t n = topo_sorted_layers_.size();
+  std::vector<cudaEvent_t> ev(n + 1);
+  for (auto& e : ev) CudaCheck(cudaEventCreate(&e), "event");
+  std::vector<double> acc(n, 0.0);
+  for (int r = 0; r < reps; ++r) {
+    CudaCheck(cudaEventRecord(ev[0], stream_), "record");
+    for (size_t i = 0; i < n; ++i) {
+      topo_sorted_layers_[i]->Forward(stream_);
+      CudaCheck(cudaEventRecord(ev[i + 1], stream_), "record");
+    }
+    CudaCheck(cudaEventSynchronize(ev[n]), "sync");
+    for (size_t i = 0; i < n; ++i) {
+      float ms = 0.f;
+      CudaCheck(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "elapsed");
+      acc[i] += ms;
+    }
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  std::vector<float> out(n);
+  for (size_t i = 0; i < n; ++i) out[i] = static_cast<float>(acc[i] / std::max(reps, 1));
+  return out;
+}
+
+int Graph::LaunchesPerForward() const {
+  int n = 0;
+  for (auto& l : topo_sorted_layers_) n += l->Launches();
+  return n;
+}
+
+}  // namespace lotus

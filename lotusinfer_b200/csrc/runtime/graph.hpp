@@ -1,0 +1,78 @@
+// lotus::Graph - loads a PNNX model and runs it on one GPU.
+//
+// Keeps the reference's public surface (include/graph.hpp:15-43:
+// Graph(param, bin, batch), InitialiseInput, Forward, Output) and its build
+// steps (source/graph.cpp:44-111: one operand per PNNX operand with dim 0 set
+// to the batch, one layer per operator with ReLU/sigmoid folded into the
+// producer, Kahn topological order).  Additions:
+//   - residual fusion: `pnnx.Expression add` (+ReLU) whose operand is the
+//     sole output of a Conv2d becomes that conv's residual epilogue;
+//   - activations are NHWC fp16 between layers, converted once at the graph
+//     input and output;
+//   - Forward runs on one persistent stream with no per-layer sync, and is
+//     captured into a CUDA graph after its first (eager) run.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "layers.hpp"
+
+namespace lotus {
+
+class Graph {
+ public:
+  struct Options {
+    int device = -1;             // -1: the current device
+    bool cuda_graph = true;      // replay Forward from a CUDA graph after the first run
+    bool fuse_residual = true;   // fold conv -> add (-> ReLU) into the conv epilogue
+  };
+
+  Graph(const std::string& param_path, const std::string& bin_path, uint32_t batch_size);
+  Graph(const std::string& param_path, const std::string& bin_path, uint32_t batch_size, const Options& opt);
+  ~Graph();
+  Graph(const Graph&) = delete;
+  Graph& operator=(const Graph&) = delete;
+
+  // Reference API: synchronous H2D of the NCHW fp32 input batch.
+  void InitialiseInput(const std::vector<float>& input);
+  std::shared_ptr<Operand> Output();
+  // Reference API: runs every layer and waits for the result.
+  void Forward();
+  // Enqueues the forward pass on `stream` (nullptr = the graph's own stream).
+  void ForwardAsync(cudaStream_t stream = nullptr);
+
+  Tensor& InputTensor() { return operands_.at(input_operand_)->tensor_; }
+  Tensor& OutputTensor() { return operands_.at(output_operand_)->tensor_; }
+  const std::vector<std::shared_ptr<Layer>>& Layers() const { return topo_sorted_layers_; }
+  cudaStream_t Stream() const { return stream_; }
+  int Device() const { return device_; }
+  uint32_t Batch() const { return batch_; }
+  // Mean device milliseconds of each layer over `reps` eager runs.
+  std::vector<float> ProfileLayers(int reps);
+  // Library kernel launches per Forward.
+  int LaunchesPerForward() const;
+
+ private:
+  void Build(const std::string& param_path, const std::string& bin_path);
+  void TopoSortLayers();
+  void RunLayers(cudaStream_t s);
+
+  std::map<std::string, std::shared_ptr<Layer>> layers_;
+  OperandMap operands_;
+  std::vector<std::shared_ptr<Layer>> topo_sorted_layers_;
+  std::vector<std::string> layer_order_;  // file order, for deterministic ties
+  std::string input_operand_, output_operand_;
+  uint32_t batch_;
+  Options opt_;
+  int device_ = 0;
+  cudaStream_t stream_ = nullptr;
+  cudaGraphExec_t exec_ = nullptr;
+  int eager_runs_ = 0;
+};
+
+}  // namespace lotus

@@ -1,0 +1,339 @@
+#include "layers.hpp"
+
+#include <stdexcept>
+
+namespace lotus {
+
+void LotusCheck(int status, const std::string& where) {
+  if (status != LOTUS_OK) throw std::runtime_error(where + ": " + lotus_last_error_string());
+}
+
+static std::shared_ptr<void> device_buffer(size_t bytes) {
+  void* p = nullptr;
+  CudaCheck(cudaMalloc(&p, bytes ? bytes : 16), "cudaMalloc");
+  return std::shared_ptr<void>(p, [](void* q) { cudaFree(q); });
+}
+
+// Uploads an fp32 attribute; returns an empty pointer when the attribute is absent.
+static std::shared_ptr<void> upload_f32(const pnnx::Operator& op, const std::string& key, size_t expect_elems) {
+  auto it = op.attrs.find(key);
+  if (it == op.attrs.end() || it->second.data.empty()) return nullptr;
+  if (it->second.type != "f32") throw std::runtime_error(op.name + "." + key + ": only f32 weights are supported");
+  if (it->second.data.size() != expect_elems * 4)
+    throw std::runtime_error(op.name + "." + key + ": unexpected size");
+  auto buf = device_buffer(it->second.data.size());
+  CudaCheck(cudaMemcpy(buf.get(), it->second.data.data(), it->second.data.size(), cudaMemcpyHostToDevice),
+            "weight upload");
+  return buf;
+}
+
+static bool param_bool(const pnnx::Operator& op, const std::string& k, bool dflt) {
+  auto it = op.params.find(k);
+  return it == op.params.end() ? dflt : it->second.b;
+}
+
+void Layer::Bind(const OperandMap& operands) {
+  inputs_.clear();
+  outputs_.clear();
+  for (auto& n : inputs_name_) {
+    auto it = operands.find(n);
+    if (it == operands.end()) throw std::runtime_error(name_ + ": missing input operand " + n);
+    inputs_.push_back(it->second);
+  }
+  for (auto& n : outputs_name_) {
+    auto it = operands.find(n);
+    if (it == operands.end()) throw std::runtime_error(name_ + ": missing output operand " + n);
+    outputs_.push_back(it->second);
+  }
+}
+
+double Layer::Bytes() const {
+  double b = 0;
+  for (auto& o : inputs_) b += static_cast<double>(o->tensor_.Bytes());
+  for (auto& o : outputs_) b += static_cast<double>(o->tensor_.Bytes());
+  return b;
+}
+
+// ------------------------------------------------------------------ convert
+InputConvertLayer::InputConvertLayer(const std::string& in, const std::string& out) {
+  name_ = "input_to_nhwc";
+  type_ = "lotus.InputConvert";
+  inputs_name_ = {in};
+  outputs_name_ = {out};
+}
+
+void InputConvertLayer::Forward(cudaStream_t stream) {
+  const Tensor& x = inputs_[0]->tensor_;
+  LotusCheck(lotus_nchw_f32_to_nhwc_f16(x.DataF32(), outputs_[0]->tensor_.Data(), x.Dim(0), x.Dim(1), x.Dim(2),
+                                        x.Dim(3), stream),
+             name_);
+}
+
+OutputConvertLayer::OutputConvertLayer(const std::string& in, const std::string& out) {
+  name_ = "output_to_nchw";
+  type_ = "lotus.OutputConvert";
+  inputs_name_ = {in};
+  outputs_name_ = {out};
+}
+
+void OutputConvertLayer::Forward(cudaStream_t stream) {
+  const Tensor& x = inputs_[0]->tensor_;
+  const auto& s = x.Shape();
+  const int h = s.size() > 2 ? static_cast<int>(s[2]) : 1;
+  const int w = s.size() > 3 ? static_cast<int>(s[3]) : 1;
+  LotusCheck(lotus_nhwc_f16_to_nchw_f32(x.Data(), outputs_[0]->tensor_.DataF32(), s[0], s[1], h, w, stream), name_);
+}
+
+// ------------------------------------------------------------------ conv
+Conv2dLayer::Conv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, int kw, int sh, int sw, int ph,
+                         int pw, cudaStream_t stream) {
+  name_ = op.name;
+  type_ = op.type;
+  inputs_name_ = {op.inputs.at(0)};
+  outputs_name_ = {op.outputs.at(0)};
+  desc_.c_in = c_in;
+  desc_.c_out = c_out;
+  desc_.kh = kh;
+  desc_.kw = kw;
+  desc_.stride_h = sh;
+  desc_.stride_w = sw;
+  desc_.pad_h = ph;
+  desc_.pad_w = pw;
+  desc_.out_kind = LOTUS_OUT_NHWC_F16;
+  // weights: OIHW fp32 (source/layer/layer_conv2d.cu:21) -> packed fp16
+  desc_.n = 1;
+  desc_.h = kh;
+  desc_.w = kw;
+  auto w32 = upload_f32(op, "weight", static_cast<size_t>(c_out) * c_in * kh * kw);
+  if (!w32) throw std::runtime_error(name_ + ": missing weight");
+  w_packed_ = device_buffer(lotus_conv2d_packed_weight_bytes(&desc_));
+  LotusCheck(lotus_conv2d_prepack(static_cast<const float*>(w32.get()), w_packed_.get(), &desc_, stream), name_);
+  CudaCheck(cudaStreamSynchronize(stream), "prepack sync");
+  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", c_out);
+}
+
+void Conv2dLayer::Bind(const OperandMap& operands) {
+  Layer::Bind(operands);
+  const Tensor& x = inputs_[0]->tensor_;
+  const Tensor& y = outputs_[0]->tensor_;
+  if (x.Fmt() != Format::kNHWC_F16 || y.Fmt() != Format::kNHWC_F16 || x.DimSize() != 4 || y.DimSize() != 4)
+    throw std::runtime_error(name_ + ": conv expects NHWC fp16 4-D operands");
+  desc_.n = x.Dim(0);
+  desc_.h = x.Dim(2);
+  desc_.w = x.Dim(3);
+  desc_.act = af_;
+  if (static_cast<int>(x.Dim(1)) != desc_.c_in) throw std::runtime_error(name_ + ": input channel mismatch");
+  int oh = 0, ow = 0;
+  LotusCheck(lotus_conv2d_out_hw(&desc_, &oh, &ow), name_);
+  if (y.Dim(0) != x.Dim(0) || static_cast<int>(y.Dim(1)) != desc_.c_out || static_cast<int>(y.Dim(2)) != oh ||
+      static_cast<int>(y.Dim(3)) != ow)
+    throw std::runtime_error(name_ + ": output shape mismatch");
+  if (!residual_name_.empty() && inputs_.back()->tensor_.Shape() != y.Shape())
+    throw std::runtime_error(name_ + ": residual shape mismatch");
+}
+
+void Conv2dLayer::Forward(cudaStream_t stream) {
+  const void* res = residual_name_.empty() ? nullptr : inputs_.back()->tensor_.Data();
+  LotusCheck(lotus_conv2d_fwd(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()), res,
+                              outputs_[0]->tensor_.Data(), &desc_, stream),
+             name_);
+}
+
+double Conv2dLayer::Flops() const {
+  int oh = 0, ow = 0;
+  lotus_conv2d_out_hw(&desc_, &oh, &ow);
+  return 2.0 * desc_.n * oh * ow * static_cast<double>(desc_.c_out) * desc_.c_in * desc_.kh * desc_.kw;
+}
+
+// ------------------------------------------------------------------ tconv
+TransposedConv2dLayer::TransposedConv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, int kw, int sh,
+                                             int sw, int ph, int pw, int oph, int opw, cudaStream_t stream) {
+  name_ = op.name;
+  type_ = op.type;
+  inputs_name_ = {op.inputs.at(0)};
+  outputs_name_ = {op.outputs.at(0)};
+  desc_ = lotus_tconv2d_desc{1, c_in, kh, kw, c_out, kh, kw, sh, sw, ph, pw, oph, opw, 0};
+  desc_.h = desc_.w = 4;  // any valid size for the prepack validation
+  auto w32 = upload_f32(op, "weight", static_cast<size_t>(c_in) * c_out * kh * kw);
+  if (!w32) throw std::runtime_error(name_ + ": missing weight");
+  w_packed_ = device_buffer(lotus_tconv2d_packed_weight_bytes(&desc_));
+  LotusCheck(lotus_tconv2d_prepack(static_cast<const float*>(w32.get()), w_packed_.get(), &desc_, stream), name_);
+  CudaCheck(cudaStreamSynchronize(stream), "prepack sync");
+  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", c_out);
+}
+
+void TransposedConv2dLayer::Bind(const OperandMap& operands) {
+  Layer::Bind(operands);
+  const Tensor& x = inputs_[0]->tensor_;
+  const Tensor& y = outputs_[0]->tensor_;
+  desc_.n = x.Dim(0);
+  desc_.h = x.Dim(2);
+  desc_.w = x.Dim(3);
+  desc_.act = af_;
+  int oh = 0, ow = 0;
+  LotusCheck(lotus_tconv2d_out_hw(&desc_, &oh, &ow), name_);
+  if (static_cast<int>(y.Dim(2)) != oh || static_cast<int>(y.Dim(3)) != ow ||
+      static_cast<int>(y.Dim(1)) != desc_.c_out)
+    throw std::runtime_error(name_ + ": output shape mismatch");
+}
+
+void TransposedConv2dLayer::Forward(cudaStream_t stream) {
+  LotusCheck(lotus_tconv2d_fwd(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
+                               outputs_[0]->tensor_.Data(), &desc_, stream),
+             name_);
+}
+
+double TransposedConv2dLayer::Flops() const {
+  return 2.0 * desc_.n * desc_.h * desc_.w * static_cast<double>(desc_.c_in) * desc_.c_out * desc_.kh * desc_.kw;
+}
+
+int TransposedConv2dLayer::Launches() const {
+  const bool full = desc_.stride_h == desc_.kh && desc_.stride_w == desc_.kw && desc_.out_pad_h == 0 &&
+                    desc_.out_pad_w == 0 && (desc_.c_out % 8) == 0;
+  return full ? 1 : 2;
+}
+
+// ------------------------------------------------------------------ linear
+LinearLayer::LinearLayer(const pnnx::Operator& op, int in_f, int out_f, int fc_c, int fc_h, int fc_w,
+                         cudaStream_t stream)
+    : in_f_(in_f), out_f_(out_f) {
+  name_ = op.name;
+  type_ = op.type;
+  inputs_name_ = {op.inputs.at(0)};
+  outputs_name_ = {op.outputs.at(0)};
+  auto w32 = upload_f32(op, "weight", static_cast<size_t>(in_f) * out_f);
+  if (!w32) throw std::runtime_error(name_ + ": missing weight");
+  w_packed_ = device_buffer(lotus_linear_packed_weight_bytes(in_f, out_f));
+  LotusCheck(lotus_linear_prepack(static_cast<const float*>(w32.get()), w_packed_.get(), in_f, out_f, fc_c, fc_h, fc_w,
+                                  stream),
+             name_);
+  CudaCheck(cudaStreamSynchronize(stream), "prepack sync");
+  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", out_f);
+}
+
+void LinearLayer::Bind(const OperandMap& operands) {
+  Layer::Bind(operands);
+  const Tensor& x = inputs_[0]->tensor_;
+  const Tensor& y = outputs_[0]->tensor_;
+  m_ = static_cast<int>(x.Dim(0));
+  out_f32_ = y.Fmt() == Format::kNCHW_F32;
+  if (x.Fmt() != Format::kNHWC_F16) throw std::runtime_error(name_ + ": linear input must be fp16 rows");
+  if (static_cast<int>(y.Dim(1)) != out_f_) throw std::runtime_error(name_ + ": output features mismatch");
+}
+
+void LinearLayer::Forward(cudaStream_t stream) {
+  LotusCheck(lotus_linear_fwd(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
+                              outputs_[0]->tensor_.Data(), m_, in_f_, out_f_, af_,
+                              out_f32_ ? LOTUS_OUT_ROWS_F32 : LOTUS_OUT_NHWC_F16, stream),
+             name_);
+}
+
+double LinearLayer::Flops() const { return 2.0 * m_ * static_cast<double>(in_f_) * out_f_; }
+
+// ------------------------------------------------------------------ pooling
+Maxpool2dLayer::Maxpool2dLayer(const pnnx::Operator& op, int kh, int kw, int sh, int sw, int ph, int pw) {
+  name_ = op.name;
+  type_ = op.type;
+  inputs_name_ = {op.inputs.at(0)};
+  outputs_name_ = {op.outputs.at(0)};
+  desc_ = lotus_pool2d_desc{0, 0, 0, 0, kh, kw, sh, sw, ph, pw, 0};
+}
+
+void Maxpool2dLayer::Bind(const OperandMap& operands) {
+  Layer::Bind(operands);
+  const Tensor& x = inputs_[0]->tensor_;
+  desc_.n = x.Dim(0);
+  desc_.c = x.Dim(1);
+  desc_.h = x.Dim(2);
+  desc_.w = x.Dim(3);
+  desc_.act = af_;
+  int oh = 0, ow = 0;
+  LotusCheck(lotus_maxpool2d_out_hw(&desc_, &oh, &ow), name_);
+  const Tensor& y = outputs_[0]->tensor_;
+  if (static_cast<int>(y.Dim(2)) != oh || static_cast<int>(y.Dim(3)) != ow)
+    throw std::runtime_error(name_ + ": output shape mismatch");
+}
+
+void Maxpool2dLayer::Forward(cudaStream_t stream) {
+  LotusCheck(lotus_maxpool2d_fwd(inputs_[0]->tensor_.Data(), outputs_[0]->tensor_.Data(), &desc_, stream), name_);
+}
+
+AdaptiveAvgpool2dLayer::AdaptiveAvgpool2dLayer(const pnnx::Operator& op, int oh, int ow) : oh_(oh), ow_(ow) {
+  name_ = op.name;
+  type_ = op.type;
+  inputs_name_ = {op.inputs.at(0)};
+  outputs_name_ = {op.outputs.at(0)};
+}
+
+void AdaptiveAvgpool2dLayer::Bind(const OperandMap& operands) {
+  Layer::Bind(operands);
+  out_f32_ = outputs_[0]->tensor_.Fmt() == Format::kNCHW_F32;
+  if (out_f32_ && (oh_ != 1 || ow_ != 1))
+    throw std::runtime_error(name_ + ": fp32 output of a spatial pooling must go through the output layer");
+}
+
+void AdaptiveAvgpool2dLayer::Forward(cudaStream_t stream) {
+  const Tensor& x = inputs_[0]->tensor_;
+  LotusCheck(lotus_adaptive_avgpool2d_fwd(x.Data(), outputs_[0]->tensor_.Data(), x.Dim(0), x.Dim(1), x.Dim(2),
+                                          x.Dim(3), oh_, ow_, af_, out_f32_ ? 1 : 0, stream),
+             name_);
+}
+
+// ------------------------------------------------------------------ eltwise
+ExpressionLayer::ExpressionLayer(const pnnx::Operator& op) {
+  name_ = op.name;
+  type_ = op.type;
+  auto it = op.params.find("expr");
+  if (it == op.params.end() || it->second.s.rfind("add(", 0) != 0 || op.inputs.size() != 2)
+    throw std::runtime_error(name_ + ": only expr=add(@0,@1) is supported");
+  inputs_name_ = op.inputs;
+  outputs_name_ = {op.outputs.at(0)};
+}
+
+void ExpressionLayer::Forward(cudaStream_t stream) {
+  const Tensor& a = inputs_[0]->tensor_;
+  size_t pixels = a.Dim(0);
+  for (size_t i = 2; i < a.DimSize(); ++i) pixels *= a.Dim(i);
+  LotusCheck(lotus_add_act_fwd(a.Data(), inputs_[1]->tensor_.Data(), outputs_[0]->tensor_.Data(), pixels, a.Dim(1),
+                               af_, stream),
+             name_);
+}
+
+FlattenLayer::FlattenLayer(const pnnx::Operator& op) {
+  name_ = op.name;
+  type_ = op.type;
+  inputs_name_ = {op.inputs.at(0)};
+  outputs_name_ = {op.outputs.at(0)};
+}
+
+void FlattenLayer::Bind(const OperandMap& operands) {
+  Layer::Bind(operands);
+  const Tensor& x = inputs_[0]->tensor_;
+  uint32_t feat = 1;
+  for (size_t i = 1; i < x.DimSize(); ++i) feat *= x.Dim(i);
+  const bool spatial = x.DimSize() == 4 && (x.Dim(2) != 1 || x.Dim(3) != 1);
+  if (spatial && (x.Dim(1) % 8) != 0)
+    throw std::runtime_error(name_ + ": flatten of a spatial map needs a channel count divisible by 8");
+  // NHWC storage flattened in (h, w, c) order; the consuming Linear permutes its weights to match.
+  outputs_[0]->tensor_ = x.View({x.Dim(0), feat}, Format::kNHWC_F16);
+}
+
+CatLayer::CatLayer(const pnnx::Operator& op) {
+  name_ = op.name;
+  type_ = op.type;
+  auto it = op.params.find("dim");
+  if (op.inputs.size() != 2 || it == op.params.end() || it->second.i != 1)
+    throw std::runtime_error(name_ + ": only two-input torch.cat along dim 1 is supported");
+  inputs_name_ = op.inputs;
+  outputs_name_ = {op.outputs.at(0)};
+}
+
+void CatLayer::Forward(cudaStream_t stream) {
+  const Tensor& a = inputs_[0]->tensor_;
+  const Tensor& b = inputs_[1]->tensor_;
+  LotusCheck(lotus_concat_channels_fwd(a.Data(), a.Dim(1), b.Data(), b.Dim(1), outputs_[0]->tensor_.Data(), a.Dim(0),
+                                       a.Dim(2), a.Dim(3), stream),
+             name_);
+}
+
+}  // namespace lotus

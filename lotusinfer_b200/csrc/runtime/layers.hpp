@@ -1,0 +1,175 @@
+// Layer classes: one per PNNX operator type of the hot path, each a thin
+// caller of the C ABI (include/lotus_ops.h), launched once per layer for the
+// whole batch on the graph's stream.
+//
+// Mirrors the reference's Layer hierarchy (include/layer/layer.hpp:9-27 and
+// include/layer/*.hpp): name, input/output operand names and operands, a
+// fused ActivationFunction, and Forward().  Differences: Forward takes the
+// stream (no per-Forward StreamPool, no per-layer device sync), weights are
+// prepacked to fp16 at construction, Conv2dLayer can fold a residual add.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../../include/lotus_ops.h"
+#include "pnnx.hpp"
+#include "tensor.hpp"
+
+namespace lotus {
+
+// Same values as the reference enum (include/lotus_utils.hpp:44-48).
+enum ActivationFunction { NONE = 0, RELU = 1, SIGMOID = 2 };
+
+struct Operand {
+  Tensor tensor_;
+  std::string name_;
+  std::string producer_;
+  std::vector<std::string> consumers_;
+};
+
+using OperandMap = std::map<std::string, std::shared_ptr<Operand>>;
+
+// Throws std::runtime_error with lotus_last_error_string() on a non-zero status.
+void LotusCheck(int status, const std::string& where);
+
+class Layer {
+ public:
+  virtual ~Layer() = default;
+  const std::string& Name() const { return name_; }
+  const std::string& Type() const { return type_; }
+  const std::vector<std::string>& InputsName() const { return inputs_name_; }
+  const std::vector<std::string>& OutputsName() const { return outputs_name_; }
+  ActivationFunction Activation() const { return af_; }
+  // Binds operand tensors (after allocation) and validates shapes.
+  virtual void Bind(const OperandMap& operands);
+  virtual void Forward(cudaStream_t stream) = 0;
+  // Algorithmic work of one Forward over the whole batch.
+  virtual double Flops() const { return 0.0; }
+  virtual double Bytes() const;
+  // Number of library kernel launches one Forward issues.
+  virtual int Launches() const { return 1; }
+
+ protected:
+  std::string name_, type_;
+  std::vector<std::string> inputs_name_, outputs_name_;
+  std::vector<std::shared_ptr<Operand>> inputs_, outputs_;
+  ActivationFunction af_ = NONE;
+  friend class Graph;
+};
+
+// NCHW fp32 graph input -> NHWC fp16 activation.
+class InputConvertLayer : public Layer {
+ public:
+  InputConvertLayer(const std::string& in, const std::string& out);
+  void Forward(cudaStream_t stream) override;
+};
+
+// NHWC fp16 activation -> NCHW fp32 graph output.
+class OutputConvertLayer : public Layer {
+ public:
+  OutputConvertLayer(const std::string& in, const std::string& out);
+  void Forward(cudaStream_t stream) override;
+};
+
+class Conv2dLayer : public Layer {
+ public:
+  Conv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, int kw, int sh, int sw, int ph, int pw,
+              cudaStream_t stream);
+  void SetResidual(const std::string& operand) {
+    residual_name_ = operand;
+    inputs_name_.push_back(operand);
+  }
+  const std::string& Residual() const { return residual_name_; }
+  void Bind(const OperandMap& operands) override;
+  void Forward(cudaStream_t stream) override;
+  double Flops() const override;
+  lotus_conv2d_desc Desc() const { return desc_; }
+
+ private:
+  std::shared_ptr<void> w_packed_;
+  std::shared_ptr<void> bias_;
+  std::string residual_name_;
+  lotus_conv2d_desc desc_{};
+};
+
+class TransposedConv2dLayer : public Layer {
+ public:
+  TransposedConv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, int kw, int sh, int sw, int ph, int pw,
+                        int oph, int opw, cudaStream_t stream);
+  void Bind(const OperandMap& operands) override;
+  void Forward(cudaStream_t stream) override;
+  double Flops() const override;
+  int Launches() const override;
+
+ private:
+  std::shared_ptr<void> w_packed_;
+  std::shared_ptr<void> bias_;
+  lotus_tconv2d_desc desc_{};
+};
+
+class LinearLayer : public Layer {
+ public:
+  // fc_chw: the flattened spatial input's (C, H, W) when the weight columns
+  // must be permuted to NHWC order, else all zero.
+  LinearLayer(const pnnx::Operator& op, int in_f, int out_f, int fc_c, int fc_h, int fc_w, cudaStream_t stream);
+  void Bind(const OperandMap& operands) override;
+  void Forward(cudaStream_t stream) override;
+  double Flops() const override;
+
+ private:
+  std::shared_ptr<void> w_packed_;
+  std::shared_ptr<void> bias_;
+  int in_f_ = 0, out_f_ = 0, m_ = 0;
+  bool out_f32_ = false;
+};
+
+class Maxpool2dLayer : public Layer {
+ public:
+  Maxpool2dLayer(const pnnx::Operator& op, int kh, int kw, int sh, int sw, int ph, int pw);
+  void Bind(const OperandMap& operands) override;
+  void Forward(cudaStream_t stream) override;
+
+ private:
+  lotus_pool2d_desc desc_{};
+};
+
+class AdaptiveAvgpool2dLayer : public Layer {
+ public:
+  AdaptiveAvgpool2dLayer(const pnnx::Operator& op, int oh, int ow);
+  void Bind(const OperandMap& operands) override;
+  void Forward(cudaStream_t stream) override;
+
+ private:
+  int oh_, ow_;
+  bool out_f32_ = false;
+};
+
+// pnnx.Expression add(@0,@1) not folded into a convolution.
+class ExpressionLayer : public Layer {
+ public:
+  explicit ExpressionLayer(const pnnx::Operator& op);
+  void Forward(cudaStream_t stream) override;
+};
+
+// torch.flatten: the output operand aliases the input (no kernel).
+class FlattenLayer : public Layer {
+ public:
+  explicit FlattenLayer(const pnnx::Operator& op);
+  void Bind(const OperandMap& operands) override;
+  void Forward(cudaStream_t) override {}
+  int Launches() const override { return 0; }
+  double Bytes() const override { return 0.0; }
+};
+
+class CatLayer : public Layer {
+ public:
+  explicit CatLayer(const pnnx::Operator& op);
+  void Forward(cudaStream_t stream) override;
+};
+
+}  // namespace lotus

@@ -1,0 +1,162 @@
+"""Python handle on the native graph runtime (include/lotus_graph.h).
+
+    g = Graph(param_path, bin_path, batch=256)
+    g.set_input(host_nchw_f32)        # pinned host -> device, async on the graph stream
+    g.forward()                       # enqueue (CUDA-graph replay after the first call)
+    out = g.get_output()              # device -> host, waits
+
+Mirrors lotus::Graph of the reference (include/graph.hpp:15-43).  All work is
+done by liblotus_b200.so; this class only forwards pointers and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional
+
+import numpy as np
+
+from . import abi
+from .abi import LotusError
+
+_V, _I, _S, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_double
+_I64P = ctypes.POINTER(ctypes.c_int64)
+_IP = ctypes.POINTER(ctypes.c_int)
+_FP = ctypes.POINTER(ctypes.c_float)
+
+GRAPH_SIGNATURES = {
+    "lotus_graph_create": (_V, [ctypes.c_char_p, ctypes.c_char_p, _I, _I, _I]),
+    "lotus_graph_destroy": (None, [_V]),
+    "lotus_graph_input_shape": (_I, [_V, _I64P, _IP]),
+    "lotus_graph_output_shape": (_I, [_V, _I64P, _IP]),
+    "lotus_graph_input_ptr": (_V, [_V]),
+    "lotus_graph_output_ptr": (_V, [_V]),
+    "lotus_graph_stream": (_V, [_V]),
+    "lotus_graph_set_input": (_I, [_V, _V, _S, _V]),
+    "lotus_graph_get_output": (_I, [_V, _V, _S, _V]),
+    "lotus_graph_forward": (_I, [_V, _V]),
+    "lotus_graph_forward_sync": (_I, [_V]),
+    "lotus_graph_synchronize": (_I, [_V]),
+    "lotus_graph_layer_count": (_I, [_V]),
+    "lotus_graph_layer_name": (ctypes.c_char_p, [_V, _I]),
+    "lotus_graph_layer_type": (ctypes.c_char_p, [_V, _I]),
+    "lotus_graph_layer_flops": (_D, [_V, _I]),
+    "lotus_graph_layer_bytes": (_D, [_V, _I]),
+    "lotus_graph_launches_per_forward": (_I, [_V]),
+    "lotus_graph_profile_layers": (_I, [_V, _I, _FP]),
+}
+
+NO_CUDA_GRAPH = 1
+NO_RESIDUAL_FUSION = 2
+
+_bound = False
+
+
+def _lib():
+    global _bound
+    L = abi.lib()
+    if not _bound:
+        for name, (res, args) in GRAPH_SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _bound = True
+    return L
+
+
+class Graph:
+    def __init__(self, param_path: str, bin_path: str, batch: int, device: int = -1, cuda_graph: bool = True,
+                 fuse_residual: bool = True):
+        flags = (0 if cuda_graph else NO_CUDA_GRAPH) | (0 if fuse_residual else NO_RESIDUAL_FUSION)
+        L = _lib()
+        h = L.lotus_graph_create(param_path.encode(), bin_path.encode(), int(batch), int(device), flags)
+        if not h:
+            raise LotusError(-1, abi.last_error())
+        self._h = ctypes.c_void_p(h)
+        self.batch = batch
+        self.input_shape = self._shape(L.lotus_graph_input_shape)
+        self.output_shape = self._shape(L.lotus_graph_output_shape)
+
+    def _shape(self, fn) -> tuple:
+        dims = (ctypes.c_int64 * 8)()
+        nd = ctypes.c_int()
+        abi.check(fn(self._h, dims, ctypes.byref(nd)))
+        return tuple(int(dims[i]) for i in range(nd.value))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib().lotus_graph_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---------------------------------------------------------------- data
+    @property
+    def stream(self) -> int:
+        return int(_lib().lotus_graph_stream(self._h) or 0)
+
+    @property
+    def input_ptr(self) -> int:
+        return int(_lib().lotus_graph_input_ptr(self._h))
+
+    @property
+    def output_ptr(self) -> int:
+        return int(_lib().lotus_graph_output_ptr(self._h))
+
+    def set_input(self, host: np.ndarray, stream: Optional[int] = None) -> None:
+        assert host.dtype == np.float32 and host.flags["C_CONTIGUOUS"] and host.shape == self.input_shape
+        abi.check(_lib().lotus_graph_set_input(self._h, ctypes.c_void_p(host.ctypes.data), host.size,
+                                               ctypes.c_void_p(stream) if stream else None))
+
+    def set_input_ptr(self, host_ptr: int, count: int, stream: Optional[int] = None) -> None:
+        abi.check(_lib().lotus_graph_set_input(self._h, ctypes.c_void_p(host_ptr), count,
+                                               ctypes.c_void_p(stream) if stream else None))
+
+    def get_output_into(self, host_ptr: int, count: int, stream: Optional[int] = None) -> None:
+        abi.check(_lib().lotus_graph_get_output(self._h, ctypes.c_void_p(host_ptr), count,
+                                                ctypes.c_void_p(stream) if stream else None))
+
+    def forward(self, stream: Optional[int] = None) -> None:
+        abi.check(_lib().lotus_graph_forward(self._h, ctypes.c_void_p(stream) if stream else None))
+
+    def forward_sync(self) -> None:
+        abi.check(_lib().lotus_graph_forward_sync(self._h))
+
+    def get_output(self) -> np.ndarray:
+        """Synchronous copy of the NCHW fp32 output (waits for the graph stream)."""
+        out = np.empty(self.output_shape, np.float32)
+        abi.check(_lib().lotus_graph_get_output(self._h, ctypes.c_void_p(out.ctypes.data), out.size, None))
+        self.synchronize()
+        return out
+
+    def synchronize(self) -> None:
+        abi.check(_lib().lotus_graph_synchronize(self._h))
+
+    def run(self, x: np.ndarray) -> np.ndarray:
+        """Reference-style one-shot inference: input, Forward(), Output()."""
+        self.set_input(np.ascontiguousarray(x, np.float32))
+        self.forward()
+        return self.get_output()
+
+    # ---------------------------------------------------------------- introspection
+    def layers(self) -> List[dict]:
+        L = _lib()
+        out = []
+        for i in range(L.lotus_graph_layer_count(self._h)):
+            out.append({"name": L.lotus_graph_layer_name(self._h, i).decode(),
+                        "type": L.lotus_graph_layer_type(self._h, i).decode(),
+                        "flops": float(L.lotus_graph_layer_flops(self._h, i)),
+                        "bytes": float(L.lotus_graph_layer_bytes(self._h, i))})
+        return out
+
+    def launches_per_forward(self) -> int:
+        return int(_lib().lotus_graph_launches_per_forward(self._h))
+
+    def profile_layers(self, reps: int = 5) -> List[float]:
+        n = _lib().lotus_graph_layer_count(self._h)
+        ms = (ctypes.c_float * n)()
+        abi.check(_lib().lotus_graph_profile_layers(self._h, int(reps), ms))
+        return [float(v) for v in ms]
