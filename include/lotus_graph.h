@@ -62,6 +62,12 @@ const char* lotus_graph_layer_type(const lotus_graph* g, int i);
 double lotus_graph_layer_flops(const lotus_graph* g, int i);
 double lotus_graph_layer_bytes(const lotus_graph* g, int i);
 int lotus_graph_launches_per_forward(const lotus_graph* g);
+/* Device pointer, storage format (0 NCHW fp32, 1 NHWC fp16 with channel
+ * stride roundup(C, 8)) and logical NCHW shape of a named operand; NULL if
+ * the operand does not exist or was folded away. */
+const void* lotus_graph_operand(const lotus_graph* g, const char* name, int* format, int64_t* dims, int* ndim);
+/* Device pointer and size of layer i's prepacked weight (NULL if it has none). */
+const void* lotus_graph_layer_weight(const lotus_graph* g, int i, size_t* bytes);
 /* Mean device milliseconds per layer over `reps` eager runs into ms[layer_count]. */
 int lotus_graph_profile_layers(lotus_graph* g, int reps, float* ms);
 

@@ -54,6 +54,11 @@ class Graph {
   uint32_t Batch() const { return batch_; }
   // Mean device milliseconds of each layer over `reps` eager runs.
   std::vector<float> ProfileLayers(int reps);
+  // Operand by name (nullptr if absent).
+  std::shared_ptr<Operand> FindOperand(const std::string& name) const {
+    auto it = operands_.find(name);
+    return it == operands_.end() ? nullptr : it->second;
+  }
   // Library kernel launches per Forward.
   int LaunchesPerForward() const;
 

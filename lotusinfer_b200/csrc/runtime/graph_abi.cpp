@@ -135,6 +135,20 @@ double lotus_graph_layer_bytes(const lotus_graph* g, int i) {
   return g->g->Layers()[i]->Bytes();
 }
 
+const void* lotus_graph_operand(const lotus_graph* g, const char* name, int* format, int64_t* dims, int* ndim) {
+  if (!g || !name) return nullptr;
+  auto o = g->g->FindOperand(name);
+  if (!o || o->tensor_.Empty()) return nullptr;
+  if (format) *format = o->tensor_.Fmt() == lotus::Format::kNHWC_F16 ? 1 : 0;
+  if (dims && ndim) fill_shape(o->tensor_, dims, ndim);
+  return o->tensor_.Data();
+}
+
+const void* lotus_graph_layer_weight(const lotus_graph* g, int i, size_t* bytes) {
+  if (!g || i < 0 || i >= static_cast<int>(g->g->Layers().size())) return nullptr;
+  return g->g->Layers()[i]->Weight(bytes);
+}
+
 int lotus_graph_launches_per_forward(const lotus_graph* g) { return g ? g->g->LaunchesPerForward() : -1; }
 
 int lotus_graph_profile_layers(lotus_graph* g, int reps, float* ms) {

@@ -14,16 +14,22 @@ static std::shared_ptr<void> device_buffer(size_t bytes) {
   return std::shared_ptr<void>(p, [](void* q) { cudaFree(q); });
 }
 
-// Uploads an fp32 attribute; returns an empty pointer when the attribute is absent.
-static std::shared_ptr<void> upload_f32(const pnnx::Operator& op, const std::string& key, size_t expect_elems) {
+// Uploads an fp32 attribute on `stream` and waits for it; returns an empty
+// pointer when the attribute is absent.  The copy must be ordered before the
+// prepack kernel on the same (non-blocking) stream: a plain cudaMemcpy from
+// pageable memory may return before its DMA lands and runs on the legacy
+// stream, which a non-blocking stream does not wait for.
+static std::shared_ptr<void> upload_f32(const pnnx::Operator& op, const std::string& key, size_t expect_elems,
+                                        cudaStream_t stream) {
   auto it = op.attrs.find(key);
   if (it == op.attrs.end() || it->second.data.empty()) return nullptr;
   if (it->second.type != "f32") throw std::runtime_error(op.name + "." + key + ": only f32 weights are supported");
   if (it->second.data.size() != expect_elems * 4)
     throw std::runtime_error(op.name + "." + key + ": unexpected size");
   auto buf = device_buffer(it->second.data.size());
-  CudaCheck(cudaMemcpy(buf.get(), it->second.data.data(), it->second.data.size(), cudaMemcpyHostToDevice),
+  CudaCheck(cudaMemcpyAsync(buf.get(), it->second.data.data(), it->second.data.size(), cudaMemcpyHostToDevice, stream),
             "weight upload");
+  CudaCheck(cudaStreamSynchronize(stream), "weight upload");
   return buf;
 }
 
@@ -104,12 +110,13 @@ Conv2dLayer::Conv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, 
   desc_.n = 1;
   desc_.h = kh;
   desc_.w = kw;
-  auto w32 = upload_f32(op, "weight", static_cast<size_t>(c_out) * c_in * kh * kw);
+  auto w32 = upload_f32(op, "weight", static_cast<size_t>(c_out) * c_in * kh * kw, stream);
   if (!w32) throw std::runtime_error(name_ + ": missing weight");
-  w_packed_ = device_buffer(lotus_conv2d_packed_weight_bytes(&desc_));
+  w_bytes_ = lotus_conv2d_packed_weight_bytes(&desc_);
+  w_packed_ = device_buffer(w_bytes_);
   LotusCheck(lotus_conv2d_prepack(static_cast<const float*>(w32.get()), w_packed_.get(), &desc_, stream), name_);
   CudaCheck(cudaStreamSynchronize(stream), "prepack sync");
-  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", c_out);
+  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", c_out, stream);
 }
 
 void Conv2dLayer::Bind(const OperandMap& operands) {
@@ -154,12 +161,13 @@ TransposedConv2dLayer::TransposedConv2dLayer(const pnnx::Operator& op, int c_in,
   outputs_name_ = {op.outputs.at(0)};
   desc_ = lotus_tconv2d_desc{1, c_in, kh, kw, c_out, kh, kw, sh, sw, ph, pw, oph, opw, 0};
   desc_.h = desc_.w = 4;  // any valid size for the prepack validation
-  auto w32 = upload_f32(op, "weight", static_cast<size_t>(c_in) * c_out * kh * kw);
+  auto w32 = upload_f32(op, "weight", static_cast<size_t>(c_in) * c_out * kh * kw, stream);
   if (!w32) throw std::runtime_error(name_ + ": missing weight");
-  w_packed_ = device_buffer(lotus_tconv2d_packed_weight_bytes(&desc_));
+  w_bytes_ = lotus_tconv2d_packed_weight_bytes(&desc_);
+  w_packed_ = device_buffer(w_bytes_);
   LotusCheck(lotus_tconv2d_prepack(static_cast<const float*>(w32.get()), w_packed_.get(), &desc_, stream), name_);
   CudaCheck(cudaStreamSynchronize(stream), "prepack sync");
-  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", c_out);
+  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", c_out, stream);
 }
 
 void TransposedConv2dLayer::Bind(const OperandMap& operands) {
@@ -201,14 +209,15 @@ LinearLayer::LinearLayer(const pnnx::Operator& op, int in_f, int out_f, int fc_c
   type_ = op.type;
   inputs_name_ = {op.inputs.at(0)};
   outputs_name_ = {op.outputs.at(0)};
-  auto w32 = upload_f32(op, "weight", static_cast<size_t>(in_f) * out_f);
+  auto w32 = upload_f32(op, "weight", static_cast<size_t>(in_f) * out_f, stream);
   if (!w32) throw std::runtime_error(name_ + ": missing weight");
-  w_packed_ = device_buffer(lotus_linear_packed_weight_bytes(in_f, out_f));
+  w_bytes_ = lotus_linear_packed_weight_bytes(in_f, out_f);
+  w_packed_ = device_buffer(w_bytes_);
   LotusCheck(lotus_linear_prepack(static_cast<const float*>(w32.get()), w_packed_.get(), in_f, out_f, fc_c, fc_h, fc_w,
                                   stream),
              name_);
   CudaCheck(cudaStreamSynchronize(stream), "prepack sync");
-  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", out_f);
+  if (param_bool(op, "bias", true)) bias_ = upload_f32(op, "bias", out_f, stream);
 }
 
 void LinearLayer::Bind(const OperandMap& operands) {

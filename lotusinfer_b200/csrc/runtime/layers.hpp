@@ -53,6 +53,11 @@ class Layer {
   virtual double Bytes() const;
   // Number of library kernel launches one Forward issues.
   virtual int Launches() const { return 1; }
+  // Prepacked weight (device) and its size; null when the layer has none.
+  virtual const void* Weight(size_t* bytes) const {
+    if (bytes) *bytes = 0;
+    return nullptr;
+  }
 
  protected:
   std::string name_, type_;
@@ -89,8 +94,13 @@ class Conv2dLayer : public Layer {
   void Forward(cudaStream_t stream) override;
   double Flops() const override;
   lotus_conv2d_desc Desc() const { return desc_; }
+  const void* Weight(size_t* bytes) const override {
+    if (bytes) *bytes = w_bytes_;
+    return w_packed_.get();
+  }
 
  private:
+  size_t w_bytes_ = 0;
   std::shared_ptr<void> w_packed_;
   std::shared_ptr<void> bias_;
   std::string residual_name_;
@@ -105,8 +115,13 @@ class TransposedConv2dLayer : public Layer {
   void Forward(cudaStream_t stream) override;
   double Flops() const override;
   int Launches() const override;
+  const void* Weight(size_t* bytes) const override {
+    if (bytes) *bytes = w_bytes_;
+    return w_packed_.get();
+  }
 
  private:
+  size_t w_bytes_ = 0;
   std::shared_ptr<void> w_packed_;
   std::shared_ptr<void> bias_;
   lotus_tconv2d_desc desc_{};
@@ -120,8 +135,13 @@ class LinearLayer : public Layer {
   void Bind(const OperandMap& operands) override;
   void Forward(cudaStream_t stream) override;
   double Flops() const override;
+  const void* Weight(size_t* bytes) const override {
+    if (bytes) *bytes = w_bytes_;
+    return w_packed_.get();
+  }
 
  private:
+  size_t w_bytes_ = 0;
   std::shared_ptr<void> w_packed_;
   std::shared_ptr<void> bias_;
   int in_f_ = 0, out_f_ = 0, m_ = 0;

@@ -36,12 +36,16 @@ Tensor::Tensor(const std::vector<uint32_t>& shape, const std::vector<char>& data
   if (data.size() != bytes_) throw std::runtime_error("Tensor: data size does not match shape");
   data_ = device_alloc(bytes_);
   CudaCheck(cudaMemcpy(data_.get(), data.data(), bytes_, cudaMemcpyHostToDevice), "Tensor upload");
+  // a pageable-host cudaMemcpy may return before its DMA lands; kernels on
+  // non-blocking streams must not read the buffer before it does
+  CudaCheck(cudaDeviceSynchronize(), "Tensor upload");
 }
 
 void Tensor::AssignData(const std::vector<float>& data) {
   if (fmt_ != Format::kNCHW_F32) throw std::runtime_error("AssignData needs an fp32 NCHW tensor");
   if (data.size() * 4 != bytes_) throw std::runtime_error("AssignData: size mismatch");
   CudaCheck(cudaMemcpy(Data(), data.data(), bytes_, cudaMemcpyHostToDevice), "AssignData");
+  CudaCheck(cudaDeviceSynchronize(), "AssignData");
 }
 
 void Tensor::Reshape(const std::vector<uint32_t>& shape) {

@@ -43,6 +43,8 @@ GRAPH_SIGNATURES = {
     "lotus_graph_layer_bytes": (_D, [_V, _I]),
     "lotus_graph_launches_per_forward": (_I, [_V]),
     "lotus_graph_profile_layers": (_I, [_V, _I, _FP]),
+    "lotus_graph_operand": (_V, [_V, ctypes.c_char_p, _IP, _I64P, _IP]),
+    "lotus_graph_layer_weight": (_V, [_V, _I, ctypes.POINTER(ctypes.c_size_t)]),
 }
 
 NO_CUDA_GRAPH = 1
@@ -61,6 +63,16 @@ def _lib():
             fn.argtypes = args
         _bound = True
     return L
+
+
+def _cuda_copy(dst: int, src: int, nbytes: int) -> None:
+    """Device copy through the CUDA runtime torch has already loaded (test/debug helper)."""
+    import torch  # noqa: F401  (ensures libcudart is loaded)
+    rt = ctypes.CDLL("libcudart.so.12")
+    rt.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    err = rt.cudaMemcpy(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes, 4)  # cudaMemcpyDefault
+    if err != 0:
+        raise RuntimeError(f"cudaMemcpy failed with {err}")
 
 
 class Graph:
@@ -151,6 +163,47 @@ class Graph:
                         "flops": float(L.lotus_graph_layer_flops(self._h, i)),
                         "bytes": float(L.lotus_graph_layer_bytes(self._h, i))})
         return out
+
+    def operand(self, name: str):
+        """(device pointer, format, logical NCHW shape) of an operand, or None."""
+        fmt = ctypes.c_int()
+        dims = (ctypes.c_int64 * 8)()
+        nd = ctypes.c_int()
+        ptr = _lib().lotus_graph_operand(self._h, name.encode(), ctypes.byref(fmt), dims, ctypes.byref(nd))
+        if not ptr:
+            return None
+        return int(ptr), int(fmt.value), tuple(int(dims[i]) for i in range(nd.value))
+
+    def operand_array(self, name: str) -> "np.ndarray":
+        """Copy of an operand as NCHW fp32 numpy (synchronises the graph stream)."""
+        import torch
+        ptr, fmt, shape = self.operand(name)
+        self.synchronize()
+        from . import kernels
+        if fmt == 0:
+            n = int(np.prod(shape))
+            t = torch.empty(n, dtype=torch.float32, device="cuda")
+            _cuda_copy(t.data_ptr(), ptr, n * 4)
+            return t.view(shape).cpu().numpy()
+        c = shape[1]
+        sp = shape[2:] if len(shape) == 4 else (1, 1)
+        cs = abi.channel_stride(c)
+        n = shape[0] * sp[0] * sp[1] * cs
+        t = torch.empty(n, dtype=torch.float16, device="cuda")
+        _cuda_copy(t.data_ptr(), ptr, n * 2)
+        return kernels.from_nhwc(t.view(shape[0], sp[0], sp[1], cs), c).reshape(shape).cpu().numpy()
+
+    def layer_weight(self, i: int):
+        """Copy of layer i's prepacked fp16 weight as a 1-D numpy array (or None)."""
+        import torch
+        nb = ctypes.c_size_t()
+        ptr = _lib().lotus_graph_layer_weight(self._h, int(i), ctypes.byref(nb))
+        if not ptr:
+            return None
+        self.synchronize()
+        t = torch.empty(nb.value // 2, dtype=torch.float16, device="cuda")
+        _cuda_copy(t.data_ptr(), int(ptr), nb.value)
+        return t.cpu().numpy()
 
     def launches_per_forward(self) -> int:
         return int(_lib().lotus_graph_launches_per_forward(self._h))

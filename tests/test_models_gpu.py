@@ -101,3 +101,33 @@ def test_alexnet_matches_oracle(model_dir, batch):
     assert rel_l2(got, want) <= NET_REL_L2, rel_l2(got, want)
     _top1_check(got, want)
     g.close()
+
+
+@pytest.mark.parametrize("name", ["resnet18", "unet", "alexnet"])
+def test_graph_packed_weights_equal_standalone_prepack(model_dir, name):
+    """Every layer's packed weights inside the runtime equal the standalone
+    prepack of the same archive entry (guards the upload -> prepack ordering)."""
+    import torch
+    from lotusinfer_b200 import kernels as K
+    from oracle import pnnx_text
+    g, param, binp = _graph(name, model_dir, 1)
+    pg = pnnx_text.load(param)
+    W = pnnx_text.shaped_weights(pg, pnnx_text.read_weights(binp))
+    chw = {}
+    if name == "alexnet":
+        chw["classifier.1"] = (256, 6, 6)
+    for i, layer in enumerate(g.layers()):
+        w = g.layer_weight(i)
+        if w is None:
+            continue
+        n = layer["name"]
+        wt = torch.from_numpy(W[n + ".weight"]).cuda()
+        if layer["type"] == "nn.ConvTranspose2d":
+            ref = K.tconv2d_prepack(wt)
+        elif layer["type"] == "nn.Linear":
+            ref = K.linear_prepack(wt, chw.get(n))
+        else:
+            ref = K.conv2d_prepack(wt, wt.shape[1])
+        ref = ref.cpu().numpy().ravel()
+        assert np.array_equal(w.view(np.uint16), ref.view(np.uint16)), n
+    g.close()
