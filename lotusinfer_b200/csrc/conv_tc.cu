@@ -4,21 +4,28 @@
 //   M = N*OH*OW output pixels, N_gemm = Cout, K = kh*kw*Cs_in ordered (r, s, c).
 //   A[m, k] = x[n, oh*sh - ph + r, ow*sw - pw + s, c]   (zero outside the image)
 //   B[co, k] = prepacked weight row co (K-major fp16, K padded to 64).
-//   D[m, co] accumulates in TMEM (fp32), M tile = 128 lanes, N tile = BLOCK_N columns.
+//   D[m, co] accumulates in TMEM (fp32): 128 lanes x BLOCK_N columns per tile.
 //
-// One CTA computes one 128 x BLOCK_N output tile with 6 warps:
-//   warps 0-3  A producers: gather the im2col rows with 16-byte cp.async
-//              (zero-fill for padding) into the 128B-swizzled K-major layout,
-//              then become the epilogue (TMEM -> registers -> bias, residual,
-//              activation -> fp16/fp32 global stores);
-//   warp 4     B producer: one elected thread issues TMA tiled loads of the
-//              weight tile;
-//   warp 5     allocates TMEM; one elected thread issues tcgen05.mma
-//              (M=128, N=BLOCK_N, K=16) and commits stage releases.
-// Stages are guarded by full/empty mbarriers; all waits are bounded.
+// Persistent, warp-specialised kernel, one CTA per SM walking the output
+// tiles (tile = m_tile * n_tiles + n_tile, so the N tiles of one pixel block
+// run on neighbouring SMs and share the A rows through L2):
+//   warps 0-3  epilogue: TMEM -> registers -> bias, residual, activation ->
+//              fp16 NHWC / fp32 rows / transposed-conv scatter stores;
+//   warp 4     allocates 2 x BLOCK_N TMEM columns (double-buffered
+//              accumulator); one thread issues tcgen05.mma (M=128, N=BLOCK_N,
+//              K=16) and commits stage / accumulator releases;
+//   warp 5     one thread issues the TMA loads: the weight tile always, and
+//              the activation tile in im2col mode (AMODE 1: 3x3 / strided
+//              convs with Cs_in % 64 == 0) or tiled mode (AMODE 2: 1x1 stride-1
+//              convs and Linear, a plain [M, Cs_in] matrix);
+//   warps 6-9  (AMODE 0 only) gather the im2col rows with 16-byte cp.async
+//              for channel counts that are not a multiple of 64 (stem, U-Net
+//              level 1), using a per-CTA table of (r, s, c) per 8-channel chunk.
+// The epilogue of tile i overlaps the main loop of tile i+1.  Every wait is
+// bounded; an expired wait records an error code and the CTA drains and exits.
 //
 // The same kernel runs the Linear GEMM (a 1x1 "image") and the stride==kernel
-// transposed convolution (a 1x1 conv over Cin with N_gemm = kh*kw*Cout, whose
+// transposed convolution (a 1x1 conv over Cin with N_gemm = kh*kw*Cout whose
 // epilogue scatters each column to its (ky, kx) output pixel).
 //
 // Reference counterparts: source/operator/conv2d.cu:17-187 (fp32 SIMT conv,
@@ -35,10 +42,11 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
-#include "ptx.cuh"
 #include "kernels.h"
+#include "ptx.cuh"
 
 namespace lotus_impl {
 
@@ -47,8 +55,8 @@ using namespace lotus_dev;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;                     // fp16 elements = one 128-byte swizzle row
 constexpr int kABytes = kBlockM * kBlockK * 2;  // 16 KB per stage
-constexpr int kThreads = 192;
-constexpr int kLag = 2;                         // cp.async groups a producer keeps in flight
+constexpr int kLag = 2;                         // cp.async groups a gather thread keeps in flight
+constexpr int kMaxTable = 8192;                 // gather-table entries (8-channel chunks)
 
 struct ConvTcParams {
   const __half* x;
@@ -58,26 +66,30 @@ struct ConvTcParams {
   int H, W, Cs_in;
   int OH, OW;
   int kh, kw, sh, sw, ph, pw;
-  int Cout;      // columns with real outputs (N_gemm)
+  int Cout;      // GEMM N (columns with real outputs)
   int Cs_out;    // pixel stride of the NHWC fp16 output
   int M;
   int KB;        // number of 64-wide K blocks
   int act;
   int out_kind;  // 0 NHWC fp16, 1 fp32 rows, 2 transposed-conv scatter (NHWC fp16)
+  int n_tiles;   // N tiles per M tile
+  int tiles;     // total tiles
   // transposed-conv scatter geometry
   int t_oh, t_ow, t_sh, t_sw, t_ph, t_pw, t_kw, t_cout;
 };
 
-template <int BN, int STAGES>
-struct SmemLayout {
+template <int BN, int STAGES, int AMODE>
+struct Cfg {
+  static constexpr int kThreads = AMODE == 0 ? 320 : 192;
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kAOff = 0;
   static constexpr int kBOff = STAGES * kABytes;
   static constexpr int kBarOff = kBOff + STAGES * kBBytes;
-  static constexpr int kMiscOff = kBarOff + (2 * STAGES + 1) * 8;
+  static constexpr int kNumBars = 2 * STAGES + 5;  // full, empty, tfull[2], tempty[2], mma_done
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kTableOff = (kMiscOff + 16 + 15) & ~15;
-  // +1024 for manual alignment of the dynamic smem base
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
+  static constexpr uint32_t kTmemCols = 2 * BN;
 };
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
@@ -85,42 +97,135 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int BN, int STAGES, bool FAST>
-__global__ void __launch_bounds__(kThreads, 1)
-conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const ConvTcParams p) {
-  using L = SmemLayout<BN, STAGES>;
+// Epilogue of one 32-column chunk of one accumulator row.
+__device__ __forceinline__ void epilogue_chunk(const ConvTcParams& p, const uint32_t (&v)[32], int em, int colbase,
+                                               const uint4* res, int sc_n, int sc_iy, int sc_ix) {
+  if (p.out_kind == 0) {
+    __half* yrow = reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em) * p.Cs_out;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int cg = colbase + g * 8;
+      if (cg >= p.Cs_out) break;
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(v[g * 8 + j]);
+      if (res) {
+        const __half2* rh = reinterpret_cast<const __half2*>(&res[g]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 rf = __half22float2(rh[j]);
+          f[2 * j] += rf.x;
+          f[2 * j + 1] += rf.y;
+        }
+      }
+      uint32_t packed[4];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const int c_a = cg + j, c_b = cg + j + 1;
+        float a = 0.f, b = 0.f;
+        if (c_a < p.Cout) a = apply_act(f[j] + (p.bias ? __ldg(p.bias + c_a) : 0.f), p.act);
+        if (c_b < p.Cout) b = apply_act(f[j + 1] + (p.bias ? __ldg(p.bias + c_b) : 0.f), p.act);
+        packed[j / 2] = pack_half2(a, b);
+      }
+      *reinterpret_cast<uint4*>(yrow + cg) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+  } else if (p.out_kind == 1) {
+    float* yrow = reinterpret_cast<float*>(p.y) + static_cast<int64_t>(em) * p.Cout;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int col = colbase + j;
+      if (col < p.Cout)
+        yrow[col] = apply_act(__uint_as_float(v[j]) + (p.bias ? __ldg(p.bias + col) : 0.f), p.act);
+    }
+  } else {
+    // transposed conv: column -> (tap, co) -> output pixel
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int cg = colbase + g * 8;
+      if (cg >= p.Cout) break;
+      if ((p.t_cout & 7) == 0) {
+        const int tap = cg / p.t_cout;
+        const int co = cg - tap * p.t_cout;
+        const int ky = tap / p.t_kw, kx = tap - ky * p.t_kw;
+        const int oy = sc_iy * p.t_sh + ky - p.t_ph;
+        const int ox = sc_ix * p.t_sw + kx - p.t_pw;
+        if ((unsigned)oy >= (unsigned)p.t_oh || (unsigned)ox >= (unsigned)p.t_ow) continue;
+        __half* ypix = reinterpret_cast<__half*>(p.y) +
+                       ((static_cast<int64_t>(sc_n) * p.t_oh + oy) * p.t_ow + ox) * p.Cs_out;
+        uint32_t packed[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          const float a =
+              apply_act(__uint_as_float(v[g * 8 + j]) + (p.bias ? __ldg(p.bias + co + j) : 0.f), p.act);
+          const float b =
+              apply_act(__uint_as_float(v[g * 8 + j + 1]) + (p.bias ? __ldg(p.bias + co + j + 1) : 0.f), p.act);
+          packed[j / 2] = pack_half2(a, b);
+        }
+        *reinterpret_cast<uint4*>(ypix + co) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      } else {
+        for (int j = 0; j < 8; ++j) {
+          const int col = cg + j;
+          if (col >= p.Cout) break;
+          const int tp = col / p.t_cout;
+          const int c2 = col - tp * p.t_cout;
+          const int ky2 = tp / p.t_kw, kx2 = tp - ky2 * p.t_kw;
+          const int oy2 = sc_iy * p.t_sh + ky2 - p.t_ph;
+          const int ox2 = sc_ix * p.t_sw + kx2 - p.t_pw;
+          if ((unsigned)oy2 >= (unsigned)p.t_oh || (unsigned)ox2 >= (unsigned)p.t_ow) continue;
+          __half* yp = reinterpret_cast<__half*>(p.y) +
+                       ((static_cast<int64_t>(sc_n) * p.t_oh + oy2) * p.t_ow + ox2) * p.Cs_out;
+          yp[c2] = __float2half_rn(
+              apply_act(__uint_as_float(v[g * 8 + j]) + (p.bias ? __ldg(p.bias + c2) : 0.f), p.act));
+        }
+      }
+    }
+  }
+}
+
+template <int BN, int STAGES, int AMODE>
+__global__ void __launch_bounds__(Cfg<BN, STAGES, AMODE>::kThreads, 1)
+conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+               const ConvTcParams p) {
+  using C = Cfg<BN, STAGES, AMODE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem + L::kAOff;
-  uint8_t* sB = smem + L::kBOff;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint8_t* sA = smem + C::kAOff;
+  uint8_t* sB = smem + C::kBOff;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
-  uint32_t* ktable = reinterpret_cast<uint32_t*>(smem + L::kTableOff);
+  uint64_t* tfull = empty + STAGES;   // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;       // [2] accumulator drained by the epilogue
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
+  uint32_t* ktable = reinterpret_cast<uint32_t*>(smem + C::kTableOff);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int m0 = blockIdx.x * kBlockM;
-  const int n0 = blockIdx.y * BN;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 128 + 1);
+      mbar_init(&full[s], AMODE == 0 ? 128 + 1 : 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) tma_prefetch_desc(&tmap_w);
-  if (!FAST) {
+  if (warp == 5 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    if (AMODE != 0) tma_prefetch_desc(&tmap_a);
+  }
+  if (AMODE == 0) {
     // K-chunk table: one entry per 8-channel chunk, (r, s, c) or invalid.
     const int nchunks = p.KB * 8;
     const int taps = p.kh * p.kw;
-    for (int kc = tid; kc < nchunks; kc += kThreads) {
+    for (int kc = tid; kc < nchunks; kc += C::kThreads) {
       const int k = kc * 8;
       const int tap = k / p.Cs_in;
       uint32_t e = 0xFFFFFFFFu;
@@ -133,294 +238,312 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const ConvTcParams p)
       ktable[kc] = e;
     }
   }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, BN);
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int ohw = p.OH * p.OW;
 
   if (warp < 4) {
-    // ------------------------------------------------------------ A producer
-    const int row = tid;  // 0..127
-    const int m = m0 + row;
-    const bool mvalid = m < p.M;
-    const int ohw = p.OH * p.OW;
-    int n_img = 0, oh = 0, ow = 0;
-    if (mvalid) {
-      n_img = m / ohw;
-      const int rem = m - n_img * ohw;
-      oh = rem / p.OW;
-      ow = rem - oh * p.OW;
-    }
-    const int ih0 = oh * p.sh - p.ph;
-    const int iw0 = ow * p.sw - p.pw;
-    const __half* xb = p.x + static_cast<int64_t>(n_img) * p.H * p.W * p.Cs_in;
-    const uint32_t swz = row & 7;
-    const uint32_t a_row = smem_u32(sA) + row * 128;
-    int r = 0, s = 0, c0 = 0;
-    bool ok_run = true;
-    for (int kb = 0; kb < p.KB; ++kb) {
-      const int st = kb % STAGES;
-      const uint32_t it = kb / STAGES;
-      if (kb >= STAGES) {
-        if (*abort_flag || !mbar_wait(&empty[st], (it - 1) & 1, kErrWaitEmpty)) {
-          *abort_flag = 1;
-          ok_run = false;
-          break;
-        }
-      }
-      const uint32_t dst = a_row + st * kABytes;
-      if (FAST) {
-        const int ih = ih0 + r, iw = iw0 + s;
-        const bool ok = mvalid && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W;
-        const __half* src = ok ? xb + (static_cast<int64_t>(ih) * p.W + iw) * p.Cs_in + c0 : p.x;
-        const uint32_t nb = ok ? 16u : 0u;
+    // ================================================================ epilogue
+    const int erow = warp * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
+    constexpr int kResVecs = BN <= 128 ? BN / 8 : 4;
+    int lt = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
+      const int m0 = (t / p.n_tiles) * kBlockM;
+      const int n0 = (t % p.n_tiles) * BN;
+      const int ab = lt & 1;
+      const int em = m0 + erow;
+      const bool rvalid = em < p.M;
+      const bool has_res = p.residual != nullptr && p.out_kind == 0;
+      const uint4* rrow =
+          has_res ? reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out) : nullptr;
+      // residual rows do not depend on the accumulator: issue their loads before waiting
+      uint4 res[kResVecs];
+      if (BN <= 128 && has_res && rvalid) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) cp_async_16(dst + ((j ^ swz) << 4), ok ? src + j * 8 : src, nb);
-        c0 += kBlockK;
-        if (c0 == p.Cs_in) {
-          c0 = 0;
-          if (++s == p.kw) {
-            s = 0;
-            ++r;
+        for (int i = 0; i < kResVecs; ++i)
+          res[i] = (n0 + i * 8 < p.Cs_out) ? __ldg(rrow + n0 / 8 + i) : make_uint4(0, 0, 0, 0);
+      }
+      int sc_n = 0, sc_iy = 0, sc_ix = 0;
+      if (p.out_kind == 2 && rvalid) {
+        sc_n = em / ohw;
+        const int rem = em - sc_n * ohw;
+        sc_iy = rem / p.OW;
+        sc_ix = rem - sc_iy * p.OW;
+      }
+      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt >> 1) & 1, kErrWaitAccum);
+      if (!ok) *abort_flag = 1;
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * BN + cc * 32, v);  // warp-collective
+        tmem_ld_wait();
+        if (!ok || !rvalid) continue;
+        const uint4* rp = nullptr;
+        uint4 rtmp[4];
+        if (has_res) {
+          if (BN <= 128) {
+            rp = &res[cc * 4];
+          } else {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int cg = n0 + cc * 32 + g * 8;
+              rtmp[g] = cg < p.Cs_out ? __ldg(rrow + cg / 8) : make_uint4(0, 0, 0, 0);
+            }
+            rp = rtmp;
           }
         }
-      } else {
+        epilogue_chunk(p, v, em, n0 + cc * 32, rp, sc_n, sc_iy, sc_ix);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[ab]);
+      if (!ok) break;
+    }
+  } else if (warp == 4) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16_m128(BN);
+      uint32_t it = 0;
+      int lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++lt) {
+        const int ab = lt & 1;
+        if (*abort_flag || !mbar_wait(&tempty[ab], ((lt >> 1) & 1) ^ 1, kErrWaitAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * BN;
+        for (int kb = 0; kb < p.KB; ++kb, ++it) {
+          const int st = it % STAGES;
+          if (*abort_flag || !mbar_wait(&full[st], (it / STAGES) & 1, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + st * kABytes);
+          const uint32_t b_base = smem_u32(sB + st * C::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k) {
+            umma_f16(d_tmem, make_sdesc_sw128(a_base + k * 32), make_sdesc_sw128(b_base + k * 32), idesc,
+                     (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[ab]);
+      }
+      if (!ok) *abort_flag = 1;
+      // every MMA this thread issued has completed once mma_done fires
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, kErrWaitFull);
+    }
+  } else if (warp == 5) {
+    // ================================================================ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      constexpr uint32_t kTx = C::kBBytes + (AMODE != 0 ? kABytes : 0);
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        const int m0 = (t / p.n_tiles) * kBlockM;
+        const int n0 = (t % p.n_tiles) * BN;
+        int wst = 0, hst = 0, nimg = 0;
+        if (AMODE == 1) {
+          nimg = m0 / ohw;
+          const int rem = m0 - nimg * ohw;
+          const int oh = rem / p.OW;
+          const int ow = rem - oh * p.OW;
+          wst = ow * p.sw - p.pw;
+          hst = oh * p.sh - p.ph;
+        }
+        int r = 0, s = 0, c0 = 0;
+        for (int kb = 0; kb < p.KB; ++kb, ++it) {
+          const int st = it % STAGES;
+          if (*abort_flag || !mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], kTx);
+          tma_load_2d(sB + st * C::kBBytes, &tmap_w, &full[st], kb * kBlockK, n0);
+          if (AMODE == 1) {
+            tma_load_im2col_4d(sA + st * kABytes, &tmap_a, &full[st], c0, wst, hst, nimg, static_cast<uint16_t>(s),
+                               static_cast<uint16_t>(r));
+            c0 += kBlockK;
+            if (c0 == p.Cs_in) {
+              c0 = 0;
+              if (++s == p.kw) {
+                s = 0;
+                ++r;
+              }
+            }
+          } else if (AMODE == 2) {
+            tma_load_2d(sA + st * kABytes, &tmap_a, &full[st], kb * kBlockK, m0);
+          }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (AMODE == 0) {
+    // ================================================================ A gather (cp.async)
+    const int row = tid - 192;  // 0..127
+    const uint32_t swz = row & 7;
+    const uint32_t a_row = smem_u32(sA) + row * 128;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      const int m = (t / p.n_tiles) * kBlockM + row;
+      const bool mvalid = m < p.M;
+      int n_img = 0, oh = 0, ow = 0;
+      if (mvalid) {
+        n_img = m / ohw;
+        const int rem = m - n_img * ohw;
+        oh = rem / p.OW;
+        ow = rem - oh * p.OW;
+      }
+      const int ih0 = oh * p.sh - p.ph;
+      const int iw0 = ow * p.sw - p.pw;
+      const __half* xb = p.x + static_cast<int64_t>(n_img) * p.H * p.W * p.Cs_in;
+      for (int kb = 0; kb < p.KB; ++kb, ++it) {
+        const int st = it % STAGES;
+        if (*abort_flag || !mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, kErrWaitEmpty)) {
+          ok = false;
+          break;
+        }
+        const uint32_t dst = a_row + st * kABytes;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t e = ktable[kb * 8 + j];
           const int rr = int(e >> 24), ss = int((e >> 16) & 0xFF), cc = int(e & 0xFFFF);
           const int ih = ih0 + rr, iw = iw0 + ss;
-          const bool ok = (e != 0xFFFFFFFFu) && mvalid && (unsigned)ih < (unsigned)p.H &&
-                          (unsigned)iw < (unsigned)p.W;
-          const __half* src = ok ? xb + (static_cast<int64_t>(ih) * p.W + iw) * p.Cs_in + cc : p.x;
-          cp_async_16(dst + ((j ^ swz) << 4), src, ok ? 16u : 0u);
+          const bool okc =
+              (e != 0xFFFFFFFFu) && mvalid && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W;
+          const __half* src = okc ? xb + (static_cast<int64_t>(ih) * p.W + iw) * p.Cs_in + cc : p.x;
+          cp_async_16(dst + ((j ^ swz) << 4), src, okc ? 16u : 0u);
         }
-      }
-      cp_async_commit();
-      if (kb >= kLag) {
-        cp_async_wait<kLag>();
-        fence_proxy_async_smem();
-        mbar_arrive(&full[(kb - kLag) % STAGES]);
+        cp_async_commit();
+        if (it >= kLag) {
+          cp_async_wait<kLag>();
+          fence_proxy_async_smem();
+          mbar_arrive(&full[(it - kLag) % STAGES]);
+        }
       }
     }
     cp_async_wait_all();
     fence_proxy_async_smem();
-    if (ok_run) {
-      const int first = p.KB > kLag ? p.KB - kLag : 0;
-      for (int kb = first; kb < p.KB; ++kb) mbar_arrive(&full[kb % STAGES]);
-    }
-
-    // ------------------------------------------------------------ epilogue
-    __syncwarp();
-    bool acc_ok = false;
-    if (!*abort_flag) acc_ok = mbar_wait(accf, 0, kErrWaitAccum);
-    if (!acc_ok) *abort_flag = 1;
-    tc_fence_after();
-    const int erow = warp * 32 + lane;
-    const int em = m0 + erow;
-    const bool evalid = acc_ok && em < p.M;
-    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
-
-    // scatter geometry for out_kind 2
-    int sc_n = 0, sc_iy = 0, sc_ix = 0;
-    if (p.out_kind == 2 && evalid) {
-      const int hw = p.OH * p.OW;  // the GEMM "output" grid is the tconv input grid
-      sc_n = em / hw;
-      const int rem = em - sc_n * hw;
-      sc_iy = rem / p.OW;
-      sc_ix = rem - sc_iy * p.OW;
-    }
-
-#pragma unroll 1
-    for (int cc = 0; cc < BN / 32; ++cc) {
-      uint32_t v[32];
-      __syncwarp();
-      tmem_ld_32x32b_x32(t_lane + cc * 32, v);  // warp-collective: every lane executes it
-      tmem_ld_wait();
-      if (!evalid) continue;
-      const int colbase = n0 + cc * 32;
-      if (p.out_kind == 0) {
-        __half* yrow = reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em) * p.Cs_out;
-        const __half* rrow = p.residual ? p.residual + static_cast<int64_t>(em) * p.Cs_out : nullptr;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int cg = colbase + g * 8;
-          if (cg >= p.Cs_out) break;
-          float f[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(v[g * 8 + j]);
-          if (rrow) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(rrow + cg);
-            const __half2* rh = reinterpret_cast<const __half2*>(&rv);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 rf = __half22float2(rh[j]);
-              f[2 * j] += rf.x;
-              f[2 * j + 1] += rf.y;
-            }
-          }
-          uint32_t packed[4];
-#pragma unroll
-          for (int j = 0; j < 8; j += 2) {
-            const int c_a = cg + j, c_b = cg + j + 1;
-            float a = 0.f, b = 0.f;
-            if (c_a < p.Cout) a = apply_act(f[j] + (p.bias ? __ldg(p.bias + c_a) : 0.f), p.act);
-            if (c_b < p.Cout) b = apply_act(f[j + 1] + (p.bias ? __ldg(p.bias + c_b) : 0.f), p.act);
-            packed[j / 2] = pack_half2(a, b);
-          }
-          *reinterpret_cast<uint4*>(yrow + cg) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        }
-      } else if (p.out_kind == 1) {
-        float* yrow = reinterpret_cast<float*>(p.y) + static_cast<int64_t>(em) * p.Cout;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int col = colbase + j;
-          if (col < p.Cout)
-            yrow[col] = apply_act(__uint_as_float(v[j]) + (p.bias ? __ldg(p.bias + col) : 0.f), p.act);
-        }
-      } else {
-        // transposed conv: column -> (tap, co) -> output pixel
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int cg = colbase + g * 8;
-          if (cg >= p.Cout) break;
-          const int tap = cg / p.t_cout;
-          const int co = cg - tap * p.t_cout;
-          const int ky = tap / p.t_kw, kx = tap - ky * p.t_kw;
-          const int oy = sc_iy * p.t_sh + ky - p.t_ph;
-          const int ox = sc_ix * p.t_sw + kx - p.t_pw;
-          if ((unsigned)oy >= (unsigned)p.t_oh || (unsigned)ox >= (unsigned)p.t_ow) continue;
-          __half* ypix = reinterpret_cast<__half*>(p.y) +
-                         ((static_cast<int64_t>(sc_n) * p.t_oh + oy) * p.t_ow + ox) * p.Cs_out;
-          if ((p.t_cout & 7) == 0) {
-            uint32_t packed[4];
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-              const float a = apply_act(__uint_as_float(v[g * 8 + j]) + (p.bias ? __ldg(p.bias + co + j) : 0.f), p.act);
-              const float b =
-                  apply_act(__uint_as_float(v[g * 8 + j + 1]) + (p.bias ? __ldg(p.bias + co + j + 1) : 0.f), p.act);
-              packed[j / 2] = pack_half2(a, b);
-            }
-            *reinterpret_cast<uint4*>(ypix + co) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-          } else {
-            for (int j = 0; j < 8; ++j) {
-              const int col = cg + j;
-              if (col >= p.Cout) break;
-              const int tp = col / p.t_cout;
-              const int c2 = col - tp * p.t_cout;
-              const int ky2 = tp / p.t_kw, kx2 = tp - ky2 * p.t_kw;
-              const int oy2 = sc_iy * p.t_sh + ky2 - p.t_ph;
-              const int ox2 = sc_ix * p.t_sw + kx2 - p.t_pw;
-              if ((unsigned)oy2 >= (unsigned)p.t_oh || (unsigned)ox2 >= (unsigned)p.t_ow) continue;
-              __half* yp = reinterpret_cast<__half*>(p.y) +
-                           ((static_cast<int64_t>(sc_n) * p.t_oh + oy2) * p.t_ow + ox2) * p.Cs_out;
-              yp[c2] = __float2half_rn(
-                  apply_act(__uint_as_float(v[g * 8 + j]) + (p.bias ? __ldg(p.bias + c2) : 0.f), p.act));
-            }
-          }
-        }
-      }
-    }
-  } else if (warp == 4) {
-    // ------------------------------------------------------------ B producer (TMA)
-    if (lane == 0) {
-      for (int kb = 0; kb < p.KB; ++kb) {
-        const int st = kb % STAGES;
-        const uint32_t it = kb / STAGES;
-        if (kb >= STAGES) {
-          if (*abort_flag || !mbar_wait(&empty[st], (it - 1) & 1, kErrWaitEmpty)) {
-            *abort_flag = 1;
-            break;
-          }
-        }
-        mbar_arrive_expect_tx(&full[st], L::kBBytes);
-        tma_load_2d(sB + st * L::kBBytes, &tmap_w, &full[st], kb * kBlockK, n0);
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16_m128(BN);
-      bool ok_run = true;
-      for (int kb = 0; kb < p.KB; ++kb) {
-        const int st = kb % STAGES;
-        const uint32_t it = kb / STAGES;
-        if (*abort_flag || !mbar_wait(&full[st], it & 1, kErrWaitFull)) {
-          *abort_flag = 1;
-          ok_run = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + st * kABytes);
-        const uint32_t b_base = smem_u32(sB + st * L::kBBytes);
-#pragma unroll
-        for (int k = 0; k < kBlockK / 16; ++k) {
-          umma_f16(tmem_base, make_sdesc_sw128(a_base + k * 32), make_sdesc_sw128(b_base + k * 32), idesc,
-                   (kb | k) != 0 ? 1u : 0u);
-        }
-        umma_commit(&empty[st]);
-      }
-      // Signal the epilogue even on abort so that it does not wait out its
-      // own limit; it checks the abort flag before reading TMEM.
-      umma_commit(accf);
-      (void)ok_run;
+    if (ok) {
+      for (uint32_t j = it > kLag ? it - kLag : 0; j < it; ++j) mbar_arrive(&full[j % STAGES]);
+    } else {
+      *abort_flag = 1;
     }
   }
 
-  // All MMAs have completed once the epilogue has passed accf (or the CTA
-  // aborted); TMEM can be released after everyone is done with it.
+  // TMEM is released after every warp is done with it (the MMA thread has
+  // waited for all of its MMAs, the epilogue for all of its loads).
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 4) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, BN);
+    tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 
 // ---------------------------------------------------------------- host side
 
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+static void* driver_fn(const char* name) {
+  cudaDriverEntryPointQueryResult q;
+  void* ptr = nullptr;
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+    return ptr;
+  return nullptr;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void* ptr = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(driver_fn("cuTensorMapEncodeTiled"));
   });
   return fn;
 }
 
-// 2-D map over the packed weight [rows, k_pad] fp16, box {64, bn}, 128B swizzle.
-static int make_weight_tmap(CUtensorMap* map, const void* w, int rows, int k_pad, int bn) {
-  auto enc = get_encode_fn();
+static PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(driver_fn("cuTensorMapEncodeIm2col"));
+  });
+  return fn;
+}
+
+// 2-D map over a row-major fp16 matrix [rows, cols] (row stride ld elements),
+// box {64, box_rows}, 128B swizzle.  Columns past `cols` read as zero.
+static int make_tmap_2d(CUtensorMap* map, const void* base, int rows, int cols, int ld, int box_rows) {
+  auto enc = encode_tiled();
   if (!enc) return -1;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k_pad), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k_pad) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(bn)};
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(w), dims, strides, box, estr,
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-template <int BN, int STAGES, bool FAST>
-static cudaError_t launch_impl(const CUtensorMap& map, const ConvTcParams& p, int n_rows, cudaStream_t stream) {
-  using L = SmemLayout<BN, STAGES>;
-  const int table = FAST ? 0 : p.KB * 8;
-  const int smem = L::bytes(table);
-  auto kern = conv_tc_kernel<BN, STAGES, FAST>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid((p.M + kBlockM - 1) / kBlockM, (n_rows + BN - 1) / BN);
-  kern<<<grid, kThreads, smem, stream>>>(map, p);
+// im2col map over the NHWC activation [N, H, W, Cs]: 128 pixels x 64 channels
+// per load, bounding box [-pad, dim - 1 + pad - (k - 1)], traversal = stride.
+static int make_tmap_im2col(CUtensorMap* map, const ConvTcArgs& a, int n_img) {
+  auto enc = encode_im2col();
+  if (!enc) return -1;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Cs_in), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
+                        static_cast<cuuint64_t>(n_img)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.Cs_in) * 2, static_cast<cuuint64_t>(a.W) * a.Cs_in * 2,
+                           static_cast<cuuint64_t>(a.H) * a.W * a.Cs_in * 2};
+  int lower[2] = {-a.pw, -a.ph};
+  int upper[2] = {a.pw - (a.kw - 1), a.ph - (a.kh - 1)};
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(a.sw), static_cast<cuuint32_t>(a.sh), 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, lower, upper,
+                   kBlockK, kBlockM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int STAGES, int AMODE>
+static cudaError_t launch_impl(const CUtensorMap& mw, const CUtensorMap& ma, const ConvTcParams& p,
+                               cudaStream_t stream) {
+  using C = Cfg<BN, STAGES, AMODE>;
+  const int smem = C::bytes(AMODE == 0 ? p.KB * 8 : 0);
+  auto kern = conv_tc_kernel<BN, STAGES, AMODE>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::bytes(AMODE == 0 ? kMaxTable : 0));
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const int grid = p.tiles < num_sms() ? p.tiles : num_sms();
+  kern<<<grid, C::kThreads, smem, stream>>>(mw, ma, p);
   note_launch();
   return cudaGetLastError();
 }
@@ -457,30 +580,66 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   p.t_kw = a.t_kw;
   p.t_cout = a.t_cout;
 
-  const bool fast = (a.Cs_in % kBlockK) == 0;
-  if (!fast && p.KB * 8 > 8192) {
-    *err = "conv: K too large for the general gather path";
+  int bn = a.block_n;
+  if (bn == 0) {
+    const char* env = std::getenv("LOTUS_CONV_BN");
+    bn = env ? std::atoi(env) : 0;
+  }
+  if (bn != 64 && bn != 128 && bn != 256) bn = a.n_cols <= 64 ? 64 : 128;
+  p.n_tiles = (a.n_cols + bn - 1) / bn;
+  const long m_tiles = (static_cast<long>(a.M) + kBlockM - 1) / kBlockM;
+  if (m_tiles * p.n_tiles > 0x7FFFFFFFL) {
+    *err = "conv: too many tiles";
     return -2;
   }
-  int bn = a.block_n;
-  if (bn == 0) bn = a.n_cols <= 64 ? 64 : (a.n_cols <= 128 ? 128 : 128);
-  CUtensorMap map;
-  if (make_weight_tmap(&map, a.w_packed, a.n_cols, a.k_pad, bn) != 0) {
-    *err = "conv: cuTensorMapEncodeTiled failed (driver entry point or arguments)";
+  p.tiles = static_cast<int>(m_tiles * p.n_tiles);
+
+  // A operand: plain-GEMM tiles by 2-D TMA, im2col TMA for 64-channel-aligned
+  // inputs, otherwise the cp.async gather.  Small inputs (< 128 KB) stay on
+  // the gather path: the im2col map is only used on activation tensors at
+  // least that large.
+  const bool plain_gemm = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
+  const int n_img = a.M / (a.OH * a.OW);
+  const size_t x_bytes = static_cast<size_t>(n_img) * a.H * a.W * a.Cs_in * 2;
+  int amode = 0;
+  if (plain_gemm)
+    amode = 2;
+  else if (a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10))
+    amode = 1;
+  const char* force = std::getenv("LOTUS_CONV_AMODE");
+  if (force && std::atoi(force) == 0) amode = 0;
+  if (amode == 0 && p.KB * 8 > kMaxTable) {
+    *err = "conv: K too large for the gather path";
+    return -2;
+  }
+
+  CUtensorMap mw, ma;
+  if (make_tmap_2d(&mw, a.w_packed, a.n_cols, a.k_pad, a.k_pad, bn) != 0) {
+    *err = "conv: weight tensor map encoding failed";
     return -3;
   }
-  cudaError_t e;
+  ma = mw;  // unused by the gather path
+  if (amode == 1 && make_tmap_im2col(&ma, a, n_img) != 0) {
+    *err = "conv: im2col tensor map encoding failed";
+    return -3;
+  }
+  if (amode == 2 && make_tmap_2d(&ma, a.x, a.M, a.Cs_in, a.Cs_in, kBlockM) != 0) {
+    *err = "conv: activation tensor map encoding failed";
+    return -3;
+  }
+
+  cudaError_t e = cudaErrorInvalidValue;
   if (bn == 64) {
-    e = fast ? launch_impl<64, 4, true>(map, p, a.n_cols, stream) : launch_impl<64, 4, false>(map, p, a.n_cols, stream);
+    e = amode == 0 ? launch_impl<64, 8, 0>(mw, ma, p, stream)
+                   : (amode == 1 ? launch_impl<64, 8, 1>(mw, ma, p, stream) : launch_impl<64, 8, 2>(mw, ma, p, stream));
   } else if (bn == 128) {
-    e = fast ? launch_impl<128, 3, true>(map, p, a.n_cols, stream)
-             : launch_impl<128, 3, false>(map, p, a.n_cols, stream);
-  } else if (bn == 256) {
-    e = fast ? launch_impl<256, 4, true>(map, p, a.n_cols, stream)
-             : launch_impl<256, 4, false>(map, p, a.n_cols, stream);
+    e = amode == 0 ? launch_impl<128, 6, 0>(mw, ma, p, stream)
+                   : (amode == 1 ? launch_impl<128, 6, 1>(mw, ma, p, stream)
+                                 : launch_impl<128, 6, 2>(mw, ma, p, stream));
   } else {
-    *err = "conv: unsupported block_n";
-    return -2;
+    e = amode == 0 ? launch_impl<256, 4, 0>(mw, ma, p, stream)
+                   : (amode == 1 ? launch_impl<256, 4, 1>(mw, ma, p, stream)
+                                 : launch_impl<256, 4, 2>(mw, ma, p, stream));
   }
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);
