@@ -9,16 +9,18 @@
 // Persistent, warp-specialised kernel, one CTA per SM walking the output
 // tiles (tile = m_tile * n_tiles + n_tile, so the N tiles of one pixel block
 // run on neighbouring SMs and share the A rows through L2):
-//   warps 0-3  epilogue: TMEM -> registers -> bias, residual, activation ->
-//              fp16 NHWC / fp32 rows / transposed-conv scatter stores;
-//   warp 4     allocates 2 x BLOCK_N TMEM columns (double-buffered
+//   warps 0-7  epilogue (two warps per TMEM lane quarter, one per column
+//              half): TMEM -> registers -> bias (staged in shared memory per
+//              tile), residual, activation -> fp16 NHWC / fp32 rows /
+//              transposed-conv scatter stores;
+//   warp 8     allocates 2 x BLOCK_N TMEM columns (double-buffered
 //              accumulator); one thread issues tcgen05.mma (M=128, N=BLOCK_N,
 //              K=16) and commits stage / accumulator releases;
-//   warp 5     one thread issues the TMA loads: the weight tile always, and
+//   warp 9     one thread issues the TMA loads: the weight tile always, and
 //              the activation tile in im2col mode (AMODE 1: 3x3 / strided
 //              convs with Cs_in % 64 == 0) or tiled mode (AMODE 2: 1x1 stride-1
 //              convs and Linear, a plain [M, Cs_in] matrix);
-//   warps 6-9  (AMODE 0 only) gather the im2col rows with 16-byte cp.async
+//   warps 10-13 (AMODE 0 only) gather the im2col rows with 16-byte cp.async
 //              for channel counts that are not a multiple of 64 (stem, U-Net
 //              level 1), using a per-CTA table of (r, s, c) per 8-channel chunk.
 // The epilogue of tile i overlaps the main loop of tile i+1.  Every wait is
@@ -80,14 +82,19 @@ struct ConvTcParams {
 
 template <int BN, int STAGES, int AMODE>
 struct Cfg {
-  static constexpr int kThreads = AMODE == 0 ? 320 : 192;
+  static constexpr int kEpiWarps = 8;                      // 2 per TMEM lane quarter
+  static constexpr int kMmaWarp = 8;
+  static constexpr int kTmaWarp = 9;
+  static constexpr int kGatherWarp0 = 10;                  // AMODE 0: warps 10-13
+  static constexpr int kThreads = AMODE == 0 ? 448 : 320;
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kAOff = 0;
   static constexpr int kBOff = STAGES * kABytes;
   static constexpr int kBarOff = kBOff + STAGES * kBBytes;
   static constexpr int kNumBars = 2 * STAGES + 5;  // full, empty, tfull[2], tempty[2], mma_done
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kTableOff = (kMiscOff + 16 + 15) & ~15;
+  static constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
+  static constexpr int kTableOff = kBiasOff + BN * 4;
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
   static constexpr uint32_t kTmemCols = 2 * BN;
 };
@@ -97,18 +104,36 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Epilogue of one 32-column chunk of one accumulator row.
-__device__ __forceinline__ void epilogue_chunk(const ConvTcParams& p, const uint32_t (&v)[32], int em, int colbase,
-                                               const uint4* res, int sc_n, int sc_iy, int sc_ix) {
-  if (p.out_kind == 0) {
-    __half* yrow = reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em) * p.Cs_out;
+template <int ACT>
+__device__ __forceinline__ float act_t(float v) {
+  if (ACT == 1) return fmaxf(v, 0.0f);
+  if (ACT == 2) return 1.0f / (1.0f + expf(-v));
+  return v;
+}
+
+// Named barrier over the epilogue warps only (ids 1.., 0 is __syncthreads).
+__device__ __forceinline__ void epi_bar(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Epilogue of one 32-column chunk of one accumulator row.  `cl` is the
+// chunk's first column inside the tile, `sb` the tile's bias slice in shared
+// memory (zero past Cout), `full` whether every column of the tile is < Cout.
+template <int OUT, int ACT>
+__device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t (&v)[32], int em, int n0, int cl,
+                                          const float* sb, bool full, const uint4* res, int sc_n, int sc_iy,
+                                          int sc_ix) {
+  if (OUT == 0) {
+    __half* yrow = reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em) * p.Cs_out + n0;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const int cg = colbase + g * 8;
-      if (cg >= p.Cs_out) break;
-      float f[8];
+      const int c = cl + g * 8;  // column inside the tile
+      if (!full && n0 + c >= p.Cs_out) break;
+      const float4 b0 = *reinterpret_cast<const float4*>(sb + c);
+      const float4 b1 = *reinterpret_cast<const float4*>(sb + c + 4);
+      float f[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(v[g * 8 + j]);
+      for (int j = 0; j < 8; ++j) f[j] += __uint_as_float(v[g * 8 + j]);
       if (res) {
         const __half2* rh = reinterpret_cast<const __half2*>(&res[g]);
 #pragma unroll
@@ -118,30 +143,39 @@ __device__ __forceinline__ void epilogue_chunk(const ConvTcParams& p, const uint
           f[2 * j + 1] += rf.y;
         }
       }
-      uint32_t packed[4];
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        const int c_a = cg + j, c_b = cg + j + 1;
-        float a = 0.f, b = 0.f;
-        if (c_a < p.Cout) a = apply_act(f[j] + (p.bias ? __ldg(p.bias + c_a) : 0.f), p.act);
-        if (c_b < p.Cout) b = apply_act(f[j + 1] + (p.bias ? __ldg(p.bias + c_b) : 0.f), p.act);
-        packed[j / 2] = pack_half2(a, b);
+      for (int j = 0; j < 8; ++j) f[j] = act_t<ACT>(f[j]);
+      if (!full) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (n0 + c + j >= p.Cout) f[j] = 0.f;  // pad channels stay zero
       }
-      *reinterpret_cast<uint4*>(yrow + cg) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      *reinterpret_cast<uint4*>(yrow + c) = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]),
+                                                       pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
     }
-  } else if (p.out_kind == 1) {
-    float* yrow = reinterpret_cast<float*>(p.y) + static_cast<int64_t>(em) * p.Cout;
+  } else if (OUT == 1) {
+    float* yrow = reinterpret_cast<float*>(p.y) + static_cast<int64_t>(em) * p.Cout + n0;
+    if (full && (p.Cout & 3) == 0) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int col = colbase + j;
-      if (col < p.Cout)
-        yrow[col] = apply_act(__uint_as_float(v[j]) + (p.bias ? __ldg(p.bias + col) : 0.f), p.act);
+      for (int j = 0; j < 32; j += 4) {
+        const float4 b = *reinterpret_cast<const float4*>(sb + cl + j);
+        float4 o;
+        o.x = act_t<ACT>(__uint_as_float(v[j]) + b.x);
+        o.y = act_t<ACT>(__uint_as_float(v[j + 1]) + b.y);
+        o.z = act_t<ACT>(__uint_as_float(v[j + 2]) + b.z);
+        o.w = act_t<ACT>(__uint_as_float(v[j + 3]) + b.w);
+        *reinterpret_cast<float4*>(yrow + cl + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + cl + j < p.Cout) yrow[cl + j] = act_t<ACT>(__uint_as_float(v[j]) + sb[cl + j]);
     }
   } else {
-    // transposed conv: column -> (tap, co) -> output pixel
+    // transposed conv: GEMM column -> (tap, co) -> output pixel; sb holds bias[col % t_cout]
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const int cg = colbase + g * 8;
+      const int cg = n0 + cl + g * 8;
       if (cg >= p.Cout) break;
       if ((p.t_cout & 7) == 0) {
         const int tap = cg / p.t_cout;
@@ -152,16 +186,11 @@ __device__ __forceinline__ void epilogue_chunk(const ConvTcParams& p, const uint
         if ((unsigned)oy >= (unsigned)p.t_oh || (unsigned)ox >= (unsigned)p.t_ow) continue;
         __half* ypix = reinterpret_cast<__half*>(p.y) +
                        ((static_cast<int64_t>(sc_n) * p.t_oh + oy) * p.t_ow + ox) * p.Cs_out;
-        uint32_t packed[4];
+        float f[8];
 #pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-          const float a =
-              apply_act(__uint_as_float(v[g * 8 + j]) + (p.bias ? __ldg(p.bias + co + j) : 0.f), p.act);
-          const float b =
-              apply_act(__uint_as_float(v[g * 8 + j + 1]) + (p.bias ? __ldg(p.bias + co + j + 1) : 0.f), p.act);
-          packed[j / 2] = pack_half2(a, b);
-        }
-        *reinterpret_cast<uint4*>(ypix + co) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        for (int j = 0; j < 8; ++j) f[j] = act_t<ACT>(__uint_as_float(v[g * 8 + j]) + sb[cl + g * 8 + j]);
+        *reinterpret_cast<uint4*>(ypix + co) = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]),
+                                                          pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
       } else {
         for (int j = 0; j < 8; ++j) {
           const int col = cg + j;
@@ -174,12 +203,23 @@ __device__ __forceinline__ void epilogue_chunk(const ConvTcParams& p, const uint
           if ((unsigned)oy2 >= (unsigned)p.t_oh || (unsigned)ox2 >= (unsigned)p.t_ow) continue;
           __half* yp = reinterpret_cast<__half*>(p.y) +
                        ((static_cast<int64_t>(sc_n) * p.t_oh + oy2) * p.t_ow + ox2) * p.Cs_out;
-          yp[c2] = __float2half_rn(
-              apply_act(__uint_as_float(v[g * 8 + j]) + (p.bias ? __ldg(p.bias + c2) : 0.f), p.act));
+          yp[c2] = __float2half_rn(act_t<ACT>(__uint_as_float(v[g * 8 + j]) + sb[cl + g * 8 + j]));
         }
       }
     }
   }
+}
+
+template <int OUT>
+__device__ __forceinline__ void epi_chunk_act(const ConvTcParams& p, const uint32_t (&v)[32], int em, int n0, int cl,
+                                              const float* sb, bool full, const uint4* res, int sc_n, int sc_iy,
+                                              int sc_ix) {
+  if (p.act == 1)
+    epi_chunk<OUT, 1>(p, v, em, n0, cl, sb, full, res, sc_n, sc_iy, sc_ix);
+  else if (p.act == 0)
+    epi_chunk<OUT, 0>(p, v, em, n0, cl, sb, full, res, sc_n, sc_iy, sc_ix);
+  else
+    epi_chunk<OUT, 2>(p, v, em, n0, cl, sb, full, res, sc_n, sc_iy, sc_ix);
 }
 
 template <int BN, int STAGES, int AMODE>
@@ -198,6 +238,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   uint64_t* mma_done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
+  float* s_bias = reinterpret_cast<float*>(smem + C::kBiasOff);
   uint32_t* ktable = reinterpret_cast<uint32_t*>(smem + C::kTableOff);
 
   const int tid = threadIdx.x;
@@ -211,13 +252,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], C::kEpiWarps);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5 && lane == 0) {
+  if (warp == C::kTmaWarp && lane == 0) {
     tma_prefetch_desc(&tmap_w);
     if (AMODE != 0) tma_prefetch_desc(&tmap_a);
   }
@@ -238,7 +279,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       ktable[kc] = e;
     }
   }
-  if (warp == 4) {
+  if (warp == C::kMmaWarp) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
@@ -248,11 +289,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   const uint32_t tmem_base = *tmem_slot;
   const int ohw = p.OH * p.OW;
 
-  if (warp < 4) {
+  if (warp < C::kEpiWarps) {
     // ================================================================ epilogue
-    const int erow = warp * 32 + lane;
-    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
-    constexpr int kResVecs = BN <= 128 ? BN / 8 : 4;
+    // warp w reads TMEM lanes 32*(w%4).. (its hardware lane quarter) and the
+    // columns of tile half w/4.
+    constexpr int kHalf = BN / 2;
+    constexpr int kResVecs = kHalf / 8;
+    const int q = warp & 3;
+    const int hcol = (warp >> 2) * kHalf;
+    const int erow = q * 32 + lane;
+    const int etid = warp * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    const bool has_res = p.residual != nullptr && p.out_kind == 0;
     int lt = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
       const int m0 = (t / p.n_tiles) * kBlockM;
@@ -260,16 +308,23 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const int ab = lt & 1;
       const int em = m0 + erow;
       const bool rvalid = em < p.M;
-      const bool has_res = p.residual != nullptr && p.out_kind == 0;
-      const uint4* rrow =
-          has_res ? reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out) : nullptr;
-      // residual rows do not depend on the accumulator: issue their loads before waiting
+      const bool tile_full = n0 + BN <= p.Cout;
+      // residual rows and bias do not depend on the accumulator: fetch them first
       uint4 res[kResVecs];
-      if (BN <= 128 && has_res && rvalid) {
+      if (has_res && rvalid) {
+        const uint4* rrow = reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out + n0 + hcol);
 #pragma unroll
         for (int i = 0; i < kResVecs; ++i)
-          res[i] = (n0 + i * 8 < p.Cs_out) ? __ldg(rrow + n0 / 8 + i) : make_uint4(0, 0, 0, 0);
+          res[i] = (n0 + hcol + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
       }
+      epi_bar(C::kEpiWarps * 32);  // previous tile's bias readers are done
+      for (int i = etid; i < BN; i += C::kEpiWarps * 32) {
+        const int col = n0 + i;
+        float b = 0.f;
+        if (p.bias && col < p.Cout) b = __ldg(p.bias + (p.out_kind == 2 ? col % p.t_cout : col));
+        s_bias[i] = b;
+      }
+      epi_bar(C::kEpiWarps * 32);
       int sc_n = 0, sc_iy = 0, sc_ix = 0;
       if (p.out_kind == 2 && rvalid) {
         sc_n = em / ohw;
@@ -281,34 +336,28 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       if (!ok) *abort_flag = 1;
       tc_fence_after();
 #pragma unroll
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = 0; cc < kHalf / 32; ++cc) {
         uint32_t v[32];
+        const int cl = hcol + cc * 32;
         __syncwarp();
-        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * BN + cc * 32, v);  // warp-collective
+        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * BN + cl, v);  // warp-collective
         tmem_ld_wait();
         if (!ok || !rvalid) continue;
-        const uint4* rp = nullptr;
-        uint4 rtmp[4];
-        if (has_res) {
-          if (BN <= 128) {
-            rp = &res[cc * 4];
-          } else {
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int cg = n0 + cc * 32 + g * 8;
-              rtmp[g] = cg < p.Cs_out ? __ldg(rrow + cg / 8) : make_uint4(0, 0, 0, 0);
-            }
-            rp = rtmp;
-          }
-        }
-        epilogue_chunk(p, v, em, n0 + cc * 32, rp, sc_n, sc_iy, sc_ix);
+        const uint4* rp = has_res ? &res[cc * 4] : nullptr;
+        if (p.out_kind == 0)
+          epi_chunk_act<0>(p, v, em, n0, cl, s_bias, tile_full, rp, sc_n, sc_iy, sc_ix);
+        else if (p.out_kind == 1)
+          epi_chunk_act<1>(p, v, em, n0, cl, s_bias, tile_full, rp, sc_n, sc_iy, sc_ix);
+        else
+          epi_chunk_act<2>(p, v, em, n0, cl, s_bias, tile_full, rp, sc_n, sc_iy, sc_ix);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);
-      if (!ok) break;
+      // an aborted warp keeps walking the tiles (skipping the waits) so that
+      // every epilogue warp reaches the same number of named barriers
     }
-  } else if (warp == 4) {
+  } else if (warp == C::kMmaWarp) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16_m128(BN);
@@ -347,7 +396,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, kErrWaitFull);
     }
-  } else if (warp == 5) {
+  } else if (warp == C::kTmaWarp) {
     // ================================================================ TMA producer
     if (lane == 0) {
       uint32_t it = 0;
@@ -394,7 +443,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   } else if (AMODE == 0) {
     // ================================================================ A gather (cp.async)
-    const int row = tid - 192;  // 0..127
+    const int row = tid - C::kGatherWarp0 * 32;  // 0..127
     const uint32_t swz = row & 7;
     const uint32_t a_row = smem_u32(sA) + row * 128;
     uint32_t it = 0;
@@ -450,7 +499,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // waited for all of its MMAs, the epilogue for all of its loads).
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == C::kMmaWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
@@ -585,7 +634,7 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     const char* env = std::getenv("LOTUS_CONV_BN");
     bn = env ? std::atoi(env) : 0;
   }
-  if (bn != 64 && bn != 128 && bn != 256) bn = a.n_cols <= 64 ? 64 : 128;
+  if (bn != 64 && bn != 128) bn = a.n_cols <= 64 ? 64 : 128;
   p.n_tiles = (a.n_cols + bn - 1) / bn;
   const long m_tiles = (static_cast<long>(a.M) + kBlockM - 1) / kBlockM;
   if (m_tiles * p.n_tiles > 0x7FFFFFFFL) {
@@ -632,14 +681,10 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   if (bn == 64) {
     e = amode == 0 ? launch_impl<64, 8, 0>(mw, ma, p, stream)
                    : (amode == 1 ? launch_impl<64, 8, 1>(mw, ma, p, stream) : launch_impl<64, 8, 2>(mw, ma, p, stream));
-  } else if (bn == 128) {
+  } else {
     e = amode == 0 ? launch_impl<128, 6, 0>(mw, ma, p, stream)
                    : (amode == 1 ? launch_impl<128, 6, 1>(mw, ma, p, stream)
                                  : launch_impl<128, 6, 2>(mw, ma, p, stream));
-  } else {
-    e = amode == 0 ? launch_impl<256, 4, 0>(mw, ma, p, stream)
-                   : (amode == 1 ? launch_impl<256, 4, 1>(mw, ma, p, stream)
-                                 : launch_impl<256, 4, 2>(mw, ma, p, stream));
   }
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);
