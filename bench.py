@@ -272,6 +272,7 @@ def main():
             traffic = None
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if peak else None, "traffic": traffic,
+                "scope": "the 20 conv launches of one forward: FLOPs and DRAM bytes summed over them",
                 "kernel": "conv_tc_kernel (tcgen05 implicit GEMM, fp16 x fp16 -> fp32)",
                 "peak_source": f"{peak_src} bf16/fp16 dense burst", "frac_of_sustained": achieved / peak_sus if peak_sus else None,
                 "conv_ms_per_forward": conv_ms, "conv_gflop_per_forward": conv_flops / 1e9,

@@ -8,6 +8,10 @@ operators in the reference's graph order (source/graph.cpp:84-109, Kahn order
 of source/graph.cpp:5-40) with the fusion rules of the reference layers
 (ReLU / sigmoid folded into the producing conv or linear,
 source/layer/layer_conv2d.cu:129-141).
+
+Parity unpinned: no golden vectors of the reference exist and the reference
+cannot run here; see the header of lotus_oracle.c for what the restatements
+are checked against instead.
 """
 from __future__ import annotations
 
