@@ -5,11 +5,13 @@
  * calls this file; only tests/, __graft_entry__.smoke() and bench.py's CPU
  * baseline legs do, and only as the checker.
  *
- * Parity unpinned: the reference commits no golden vectors and its tests and
- * host runtime cannot run here (xtensor / Eigen / glog are absent), so these
- * restatements are checked against hand-computed answers, the reference GEMM
- * test's deterministic inputs, the reference test shapes and torch CPU, not
- * against outputs of the reference itself.
+ * Pinned against the reference itself: the reference's own operator kernels,
+ * compiled from its sources by oracle/ref/Makefile and run on a GPU by
+ * tests/golden/make_golden.py, produced tests/golden/ref_ops.npz;
+ * tests/test_golden_cpu.py requires these functions to reproduce those
+ * outputs (bit for bit on integer-valued and fp16-exact inputs).  Also
+ * checked against hand-computed answers, the reference GEMM test's
+ * deterministic inputs and torch CPU.
  *
  * Plain C restatements (fp32 NCHW, OpenMP over the outermost independent
  * loop) of the host-side reference loops the reference's per-operator tests

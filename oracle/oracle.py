@@ -9,9 +9,8 @@ of source/graph.cpp:5-40) with the fusion rules of the reference layers
 (ReLU / sigmoid folded into the producing conv or linear,
 source/layer/layer_conv2d.cu:129-141).
 
-Parity unpinned: no golden vectors of the reference exist and the reference
-cannot run here; see the header of lotus_oracle.c for what the restatements
-are checked against instead.
+Pinned: tests/test_golden_cpu.py checks these functions against outputs of
+the reference's own kernels (tests/golden/ref_ops.npz, see lotus_oracle.c).
 """
 from __future__ import annotations
 
