@@ -161,6 +161,16 @@ int lotus_concat_channels_fwd(const void* a, int ca, const void* b, int cb, void
 int lotus_nchw_f32_to_nhwc_f16(const float* x, void* y, int n, int c, int h, int w, cudaStream_t stream);
 int lotus_nhwc_f16_to_nchw_f32(const void* x, float* y, int n, int c, int h, int w, cudaStream_t stream);
 
+/* Space-to-depth of a zero-padded NCHW fp32 batch into NHWC fp16:
+ * y[n, i, j, (a*factor + b)*c + ch] = x[n, ch, factor*i + a - pad_h, factor*j + b - pad_w]
+ * (zero outside the image), for i < out_h, j < out_w; channel stride
+ * Cs(c*factor^2).  A stride-`factor` conv with kernel k on x equals a
+ * stride-1 conv with kernel ceil(k/factor) on y; the graph uses this for
+ * 3-channel strided stem convs.  No reference counterpart (the reference runs
+ * the stem as a direct conv, source/operator/conv2d.cu:17-187). */
+int lotus_space_to_depth_f16(const float* x, void* y, int n, int c, int h, int w, int factor, int pad_h, int pad_w,
+                             int out_h, int out_w, cudaStream_t stream);
+
 /* Last error of the calling thread, "" if none. */
 const char* lotus_last_error_string(void);
 

@@ -409,6 +409,16 @@ int lotus_nchw_f32_to_nhwc_f16(const float* x, void* y, int n, int c, int h, int
   return cuda_status(launch_nchw_to_nhwc(x, y, n, c, h, w, cs_of(c), stream), "nchw_to_nhwc");
 }
 
+int lotus_space_to_depth_f16(const float* x, void* y, int n, int c, int h, int w, int factor, int pad_h, int pad_w,
+                             int out_h, int out_w, cudaStream_t stream) {
+  if (!x || !y || !aligned16(y)) return fail(LOTUS_ERR_INVALID, "space_to_depth: bad pointer");
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0 || factor <= 0 || pad_h < 0 || pad_w < 0 || out_h <= 0 || out_w <= 0)
+    return fail(LOTUS_ERR_INVALID, "space_to_depth: bad sizes");
+  return cuda_status(launch_space_to_depth(x, y, n, c, h, w, factor, pad_h, pad_w, out_h, out_w,
+                                           cs_of(c * factor * factor), stream),
+                     "space_to_depth");
+}
+
 int lotus_nhwc_f16_to_nchw_f32(const void* x, float* y, int n, int c, int h, int w, cudaStream_t stream) {
   if (!x || !y || !aligned16(x)) return fail(LOTUS_ERR_INVALID, "nhwc_to_nchw: bad pointer");
   if (n <= 0 || c <= 0 || h <= 0 || w <= 0) return fail(LOTUS_ERR_INVALID, "nhwc_to_nchw: bad sizes");

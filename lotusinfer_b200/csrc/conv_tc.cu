@@ -57,8 +57,8 @@ using namespace lotus_dev;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;                     // fp16 elements = one 128-byte swizzle row
 constexpr int kABytes = kBlockM * kBlockK * 2;  // 16 KB per stage
-constexpr int kLag = 2;                         // cp.async groups a gather thread keeps in flight
-constexpr int kMaxTable = 8192;                 // gather-table entries (8-channel chunks)
+constexpr int kMaxTable = 4096;                 // gather-table entries (8-channel chunks)
+constexpr int kBiasMax = 4096;                  // bias entries staged in shared memory
 
 struct ConvTcParams {
   const __half* x;
@@ -76,12 +76,16 @@ struct ConvTcParams {
   int out_kind;  // 0 NHWC fp16, 1 fp32 rows, 2 transposed-conv scatter (NHWC fp16)
   int n_tiles;   // N tiles per M tile
   int tiles;     // total tiles
+  int bias_smem; // 1: bias staged in shared memory (<= kBiasMax columns), 0: read from global
   // transposed-conv scatter geometry
   int t_oh, t_ow, t_sh, t_sw, t_ph, t_pw, t_kw, t_cout;
 };
 
 template <int BN, int STAGES, int AMODE>
 struct Cfg {
+  // cp.async groups a gather thread keeps in flight before it signals a
+  // stage (must stay below STAGES; two stages stay free for the tensor core)
+  static constexpr int kLag = STAGES - 2;
   static constexpr int kEpiWarps = 8;                      // 2 per TMEM lane quarter
   static constexpr int kMmaWarp = 8;
   static constexpr int kTmaWarp = 9;
@@ -94,7 +98,7 @@ struct Cfg {
   static constexpr int kNumBars = 2 * STAGES + 5;  // full, empty, tfull[2], tempty[2], mma_done
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
-  static constexpr int kTableOff = kBiasOff + BN * 4;
+  static constexpr int kTableOff = kBiasOff + kBiasMax * 4;
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
   static constexpr uint32_t kTmemCols = 2 * BN;
 };
@@ -111,14 +115,18 @@ __device__ __forceinline__ float act_t(float v) {
   return v;
 }
 
-// Named barrier over the epilogue warps only (ids 1.., 0 is __syncthreads).
-__device__ __forceinline__ void epi_bar(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+// Bias of column `c` of the tile (OUT 0/1) or of output channel `c` (OUT 2).
+__device__ __forceinline__ float bias_of(const ConvTcParams& p, const float* sb, int n0, int c) {
+  if (p.bias_smem) return sb[c];
+  const int col = p.out_kind == 2 ? c : n0 + c;
+  const int lim = p.out_kind == 2 ? p.t_cout : p.Cout;
+  return (p.bias != nullptr && col < lim) ? __ldg(p.bias + col) : 0.f;
 }
 
 // Epilogue of one 32-column chunk of one accumulator row.  `cl` is the
-// chunk's first column inside the tile, `sb` the tile's bias slice in shared
-// memory (zero past Cout), `full` whether every column of the tile is < Cout.
+// chunk's first column inside the tile; `sb` points at the bias of the tile's
+// first column (OUT 0/1, zero past Cout) or at bias[0] (OUT 2, indexed by the
+// output channel); `full` says every column of the tile is < Cout.
 template <int OUT, int ACT>
 __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t (&v)[32], int em, int n0, int cl,
                                           const float* sb, bool full, const uint4* res, int sc_n, int sc_iy,
@@ -129,9 +137,16 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
     for (int g = 0; g < 4; ++g) {
       const int c = cl + g * 8;  // column inside the tile
       if (!full && n0 + c >= p.Cs_out) break;
-      const float4 b0 = *reinterpret_cast<const float4*>(sb + c);
-      const float4 b1 = *reinterpret_cast<const float4*>(sb + c + 4);
-      float f[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float f[8];
+      if (p.bias_smem) {
+        const float4 b0 = *reinterpret_cast<const float4*>(sb + c);
+        const float4 b1 = *reinterpret_cast<const float4*>(sb + c + 4);
+        f[0] = b0.x; f[1] = b0.y; f[2] = b0.z; f[3] = b0.w;
+        f[4] = b1.x; f[5] = b1.y; f[6] = b1.z; f[7] = b1.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = bias_of(p, sb, n0, c + j);
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) f[j] += __uint_as_float(v[g * 8 + j]);
       if (res) {
@@ -155,7 +170,7 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
     }
   } else if (OUT == 1) {
     float* yrow = reinterpret_cast<float*>(p.y) + static_cast<int64_t>(em) * p.Cout + n0;
-    if (full && (p.Cout & 3) == 0) {
+    if (full && (p.Cout & 3) == 0 && p.bias_smem) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
         const float4 b = *reinterpret_cast<const float4*>(sb + cl + j);
@@ -169,7 +184,7 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (n0 + cl + j < p.Cout) yrow[cl + j] = act_t<ACT>(__uint_as_float(v[j]) + sb[cl + j]);
+        if (n0 + cl + j < p.Cout) yrow[cl + j] = act_t<ACT>(__uint_as_float(v[j]) + bias_of(p, sb, n0, cl + j));
     }
   } else {
     // transposed conv: GEMM column -> (tap, co) -> output pixel; sb holds bias[col % t_cout]
@@ -188,7 +203,7 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
                        ((static_cast<int64_t>(sc_n) * p.t_oh + oy) * p.t_ow + ox) * p.Cs_out;
         float f[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = act_t<ACT>(__uint_as_float(v[g * 8 + j]) + sb[cl + g * 8 + j]);
+        for (int j = 0; j < 8; ++j) f[j] = act_t<ACT>(__uint_as_float(v[g * 8 + j]) + bias_of(p, sb, n0, co + j));
         *reinterpret_cast<uint4*>(ypix + co) = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]),
                                                           pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
       } else {
@@ -203,7 +218,7 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
           if ((unsigned)oy2 >= (unsigned)p.t_oh || (unsigned)ox2 >= (unsigned)p.t_ow) continue;
           __half* yp = reinterpret_cast<__half*>(p.y) +
                        ((static_cast<int64_t>(sc_n) * p.t_oh + oy2) * p.t_ow + ox2) * p.Cs_out;
-          yp[c2] = __float2half_rn(act_t<ACT>(__uint_as_float(v[g * 8 + j]) + sb[cl + g * 8 + j]));
+          yp[c2] = __float2half_rn(act_t<ACT>(__uint_as_float(v[g * 8 + j]) + bias_of(p, sb, n0, c2)));
         }
       }
     }
@@ -279,6 +294,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       ktable[kc] = e;
     }
   }
+  // bias, once per CTA: columns [0, bias_len) (tconv: output channels), zero
+  // past the real bias so float4 reads of a whole tile stay defined
+  const int bias_len = p.out_kind == 2 ? p.t_cout : p.n_tiles * BN;
+  for (int i = tid; p.bias_smem && i < bias_len; i += C::kThreads) {
+    const int lim = p.out_kind == 2 ? p.t_cout : p.Cout;
+    s_bias[i] = (p.bias != nullptr && i < lim) ? __ldg(p.bias + i) : 0.f;
+  }
   if (warp == C::kMmaWarp) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
@@ -298,7 +320,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     const int q = warp & 3;
     const int hcol = (warp >> 2) * kHalf;
     const int erow = q * 32 + lane;
-    const int etid = warp * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
     const bool has_res = p.residual != nullptr && p.out_kind == 0;
     int lt = 0;
@@ -309,7 +330,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const int em = m0 + erow;
       const bool rvalid = em < p.M;
       const bool tile_full = n0 + BN <= p.Cout;
-      // residual rows and bias do not depend on the accumulator: fetch them first
+      // residual rows do not depend on the accumulator: fetch them first
       uint4 res[kResVecs];
       if (has_res && rvalid) {
         const uint4* rrow = reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out + n0 + hcol);
@@ -317,14 +338,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         for (int i = 0; i < kResVecs; ++i)
           res[i] = (n0 + hcol + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
       }
-      epi_bar(C::kEpiWarps * 32);  // previous tile's bias readers are done
-      for (int i = etid; i < BN; i += C::kEpiWarps * 32) {
-        const int col = n0 + i;
-        float b = 0.f;
-        if (p.bias && col < p.Cout) b = __ldg(p.bias + (p.out_kind == 2 ? col % p.t_cout : col));
-        s_bias[i] = b;
-      }
-      epi_bar(C::kEpiWarps * 32);
       int sc_n = 0, sc_iy = 0, sc_ix = 0;
       if (p.out_kind == 2 && rvalid) {
         sc_n = em / ohw;
@@ -335,27 +348,32 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt >> 1) & 1, kErrWaitAccum);
       if (!ok) *abort_flag = 1;
       tc_fence_after();
+      // drain this warp's share of the accumulator into registers, then hand
+      // the TMEM buffer back to the MMA warp before the math and the stores
+      uint32_t v[kHalf / 32][32];
 #pragma unroll
       for (int cc = 0; cc < kHalf / 32; ++cc) {
-        uint32_t v[32];
-        const int cl = hcol + cc * 32;
         __syncwarp();
-        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * BN + cl, v);  // warp-collective
-        tmem_ld_wait();
-        if (!ok || !rvalid) continue;
-        const uint4* rp = has_res ? &res[cc * 4] : nullptr;
-        if (p.out_kind == 0)
-          epi_chunk_act<0>(p, v, em, n0, cl, s_bias, tile_full, rp, sc_n, sc_iy, sc_ix);
-        else if (p.out_kind == 1)
-          epi_chunk_act<1>(p, v, em, n0, cl, s_bias, tile_full, rp, sc_n, sc_iy, sc_ix);
-        else
-          epi_chunk_act<2>(p, v, em, n0, cl, s_bias, tile_full, rp, sc_n, sc_iy, sc_ix);
+        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * BN + hcol + cc * 32, v[cc]);  // warp-collective
       }
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);
-      // an aborted warp keeps walking the tiles (skipping the waits) so that
-      // every epilogue warp reaches the same number of named barriers
+      if (ok && rvalid) {
+        const float* sb = p.out_kind == 2 ? s_bias : s_bias + n0;
+#pragma unroll
+        for (int cc = 0; cc < kHalf / 32; ++cc) {
+          const int cl = hcol + cc * 32;
+          const uint4* rp = has_res ? &res[cc * 4] : nullptr;
+          if (p.out_kind == 0)
+            epi_chunk_act<0>(p, v[cc], em, n0, cl, sb, tile_full, rp, sc_n, sc_iy, sc_ix);
+          else if (p.out_kind == 1)
+            epi_chunk_act<1>(p, v[cc], em, n0, cl, sb, tile_full, rp, sc_n, sc_iy, sc_ix);
+          else
+            epi_chunk_act<2>(p, v[cc], em, n0, cl, sb, tile_full, rp, sc_n, sc_iy, sc_ix);
+        }
+      }
     }
   } else if (warp == C::kMmaWarp) {
     // ================================================================ MMA issuer
@@ -443,53 +461,66 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   } else if (AMODE == 0) {
     // ================================================================ A gather (cp.async)
-    const int row = tid - C::kGatherWarp0 * 32;  // 0..127
-    const uint32_t swz = row & 7;
-    const uint32_t a_row = smem_u32(sA) + row * 128;
+    // Lane l of gather warp gw copies 16-byte chunk (l % 8) of rows
+    // gw*32 + l/8 + 4*i (i = 0..7): one warp instruction moves four whole
+    // 128-byte rows, which are contiguous in global memory whenever a K block
+    // is one run of channels (or of space-to-depth taps).
+    const int gt = tid - C::kGatherWarp0 * 32;  // 0..127
+    const int gw = gt >> 5, gl = gt & 31;
+    const int j = gl & 7;
+    const int rbase = gw * 32 + (gl >> 3);
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-      const int m = (t / p.n_tiles) * kBlockM + row;
-      const bool mvalid = m < p.M;
-      int n_img = 0, oh = 0, ow = 0;
-      if (mvalid) {
-        n_img = m / ohw;
-        const int rem = m - n_img * ohw;
-        oh = rem / p.OW;
-        ow = rem - oh * p.OW;
+      const int m0 = (t / p.n_tiles) * kBlockM;
+      int ih0[8], iw0[8];
+      const __half* xb[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = m0 + rbase + 4 * i;
+        ih0[i] = -(1 << 28);  // rows past M never pass the bounds check
+        iw0[i] = 0;
+        xb[i] = p.x;
+        if (m < p.M) {
+          const int n_img = m / ohw;
+          const int rem = m - n_img * ohw;
+          const int oh = rem / p.OW;
+          const int ow = rem - oh * p.OW;
+          ih0[i] = oh * p.sh - p.ph;
+          iw0[i] = ow * p.sw - p.pw;
+          xb[i] = p.x + static_cast<int64_t>(n_img) * p.H * p.W * p.Cs_in;
+        }
       }
-      const int ih0 = oh * p.sh - p.ph;
-      const int iw0 = ow * p.sw - p.pw;
-      const __half* xb = p.x + static_cast<int64_t>(n_img) * p.H * p.W * p.Cs_in;
       for (int kb = 0; kb < p.KB; ++kb, ++it) {
         const int st = it % STAGES;
         if (*abort_flag || !mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, kErrWaitEmpty)) {
           ok = false;
           break;
         }
-        const uint32_t dst = a_row + st * kABytes;
+        const uint32_t e = ktable[kb * 8 + j];
+        const bool ek = e != 0xFFFFFFFFu;
+        const int rr = int(e >> 24), ss = int((e >> 16) & 0xFF), cc = int(e & 0xFFFF);
+        const uint32_t stage = smem_u32(sA) + st * kABytes;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t e = ktable[kb * 8 + j];
-          const int rr = int(e >> 24), ss = int((e >> 16) & 0xFF), cc = int(e & 0xFFFF);
-          const int ih = ih0 + rr, iw = iw0 + ss;
-          const bool okc =
-              (e != 0xFFFFFFFFu) && mvalid && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W;
-          const __half* src = okc ? xb + (static_cast<int64_t>(ih) * p.W + iw) * p.Cs_in + cc : p.x;
-          cp_async_16(dst + ((j ^ swz) << 4), src, okc ? 16u : 0u);
+        for (int i = 0; i < 8; ++i) {
+          const int row = rbase + 4 * i;
+          const int ih = ih0[i] + rr, iw = iw0[i] + ss;
+          const bool okc = ek && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W;
+          const __half* src = okc ? xb[i] + (static_cast<int64_t>(ih) * p.W + iw) * p.Cs_in + cc : p.x;
+          cp_async_16(stage + row * 128 + ((j ^ (row & 7)) << 4), src, okc ? 16u : 0u);
         }
         cp_async_commit();
-        if (it >= kLag) {
-          cp_async_wait<kLag>();
+        if (it >= C::kLag) {
+          cp_async_wait<C::kLag>();
           fence_proxy_async_smem();
-          mbar_arrive(&full[(it - kLag) % STAGES]);
+          mbar_arrive(&full[(it - C::kLag) % STAGES]);
         }
       }
     }
     cp_async_wait_all();
     fence_proxy_async_smem();
     if (ok) {
-      for (uint32_t j = it > kLag ? it - kLag : 0; j < it; ++j) mbar_arrive(&full[j % STAGES]);
+      for (uint32_t j = it > C::kLag ? it - C::kLag : 0; j < it; ++j) mbar_arrive(&full[j % STAGES]);
     } else {
       *abort_flag = 1;
     }
@@ -642,6 +673,7 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     return -2;
   }
   p.tiles = static_cast<int>(m_tiles * p.n_tiles);
+  p.bias_smem = (a.out_kind == 2 ? a.t_cout : p.n_tiles * bn) <= kBiasMax ? 1 : 0;
 
   // A operand: plain-GEMM tiles by 2-D TMA, im2col TMA for 64-channel-aligned
   // inputs, otherwise the cp.async gather.  Small inputs (< 128 KB) stay on

@@ -42,6 +42,8 @@ cudaError_t launch_tconv_prepack(const float* w, void* wp, int cin, int cout, in
 cudaError_t launch_linear_prepack(const float* w, void* wp, int in_f, int out_f, int k_pad, int fc_c, int fc_h,
                                   int fc_w, cudaStream_t s);
 cudaError_t launch_nchw_to_nhwc(const float* x, void* y, int n, int c, int h, int w, int cs, cudaStream_t s);
+cudaError_t launch_space_to_depth(const float* x, void* y, int n, int c, int h, int w, int f, int pad_h, int pad_w,
+                                  int oh, int ow, int cs, cudaStream_t s);
 cudaError_t launch_nhwc_to_nchw(const void* x, float* y, int n, int c, int h, int w, int cs, cudaStream_t s);
 
 // pool.cu

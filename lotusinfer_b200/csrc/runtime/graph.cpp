@@ -94,8 +94,24 @@ void Graph::Build(const std::string& param_path, const std::string& bin_path) {
       const auto& st = need(op, "stride");
       const auto& pd = need(op, "padding");
       if (pd.type == 4) throw std::runtime_error(op.name + ": string padding is not supported");
-      layer = std::make_shared<Conv2dLayer>(op, need(op, "in_channels").i, need(op, "out_channels").i, pair0(ks),
-                                            pair1(ks), pair0(st), pair1(st), pair0(pd), pair1(pd), stream_);
+      const int cin = need(op, "in_channels").i;
+      int s2d = 1;
+      // stem rewrite: a strided conv on the graph input with few channels becomes
+      // a stride-1 conv over the space-to-depth input (K = Cin*f^2*ceil(k/f)^2
+      // instead of roundup(Cin,8)*k^2, contiguous 128-byte K rows)
+      if (opt_.s2d_stem && op.inputs.at(0) == input_operand_ && g.operands.at(input_operand_).consumers.size() == 1 &&
+          pair0(st) == pair1(st) && pair0(st) >= 2 && pair0(st) <= 8 && cin * pair0(st) * pair0(st) <= 64 &&
+          shapes.at(op.outputs.at(0)).size() == 4) {
+        s2d = pair0(st);
+        const auto& os = shapes.at(op.outputs.at(0));
+        stem_s2d_ = s2d;
+        stem_pad_h_ = pair0(pd);
+        stem_pad_w_ = pair1(pd);
+        stem_shape_ = {os[0], static_cast<uint32_t>(cin * s2d * s2d), os[2] + (pair0(ks) + s2d - 1) / s2d - 1,
+                       os[3] + (pair1(ks) + s2d - 1) / s2d - 1};
+      }
+      layer = std::make_shared<Conv2dLayer>(op, cin, need(op, "out_channels").i, pair0(ks), pair1(ks), pair0(st),
+                                            pair1(st), pair0(pd), pair1(pd), stream_, s2d);
     } else if (t == "nn.ConvTranspose2d") {
       if (need(op, "groups").i != 1) throw std::runtime_error(op.name + ": only groups=1 is supported");
       const auto& dil = need(op, "dilation");
@@ -223,10 +239,11 @@ void Graph::Build(const std::string& param_path, const std::string& bin_path) {
       if (n == input_operand_) n = in_nhwc;
   {
     auto l = std::make_shared<InputConvertLayer>(input_operand_, in_nhwc);
+    if (stem_s2d_ > 1) l->SetSpaceToDepth(stem_s2d_, stem_pad_h_, stem_pad_w_);
     layers_[l->Name()] = l;
     layer_order_.insert(layer_order_.begin(), l->Name());
   }
-  shapes[in_nhwc] = shapes.at(input_operand_);
+  shapes[in_nhwc] = stem_s2d_ > 1 ? stem_shape_ : shapes.at(input_operand_);
 
   // output: Linear and 1x1 adaptive pooling write fp32 rows directly, others convert
   auto out_prod = producer_of(output_operand_);

@@ -30,6 +30,7 @@ class Graph {
     int device = -1;             // -1: the current device
     bool cuda_graph = true;      // replay Forward from a CUDA graph after the first run
     bool fuse_residual = true;   // fold conv -> add (-> ReLU) into the conv epilogue
+    bool s2d_stem = true;        // run a strided few-channel stem conv over the space-to-depth input
   };
 
   Graph(const std::string& param_path, const std::string& bin_path, uint32_t batch_size);
@@ -78,6 +79,9 @@ class Graph {
   cudaStream_t stream_ = nullptr;
   cudaGraphExec_t exec_ = nullptr;
   int eager_runs_ = 0;
+  // space-to-depth stem rewrite (factor 1 = none)
+  int stem_s2d_ = 1, stem_pad_h_ = 0, stem_pad_w_ = 0;
+  std::vector<uint32_t> stem_shape_;
 };
 
 }  // namespace lotus

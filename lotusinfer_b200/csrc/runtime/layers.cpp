@@ -33,6 +33,13 @@ static std::shared_ptr<void> upload_f32(const pnnx::Operator& op, const std::str
   return buf;
 }
 
+static std::shared_ptr<void> upload_host(const std::vector<float>& v, cudaStream_t stream) {
+  auto buf = device_buffer(v.size() * 4);
+  CudaCheck(cudaMemcpyAsync(buf.get(), v.data(), v.size() * 4, cudaMemcpyHostToDevice, stream), "weight upload");
+  CudaCheck(cudaStreamSynchronize(stream), "weight upload");
+  return buf;
+}
+
 static bool param_bool(const pnnx::Operator& op, const std::string& k, bool dflt) {
   auto it = op.params.find(k);
   return it == op.params.end() ? dflt : it->second.b;
@@ -70,6 +77,13 @@ InputConvertLayer::InputConvertLayer(const std::string& in, const std::string& o
 
 void InputConvertLayer::Forward(cudaStream_t stream) {
   const Tensor& x = inputs_[0]->tensor_;
+  if (s2d_ > 1) {
+    const Tensor& y = outputs_[0]->tensor_;
+    LotusCheck(lotus_space_to_depth_f16(x.DataF32(), y.Data(), x.Dim(0), x.Dim(1), x.Dim(2), x.Dim(3), s2d_, pad_h_,
+                                        pad_w_, y.Dim(2), y.Dim(3), stream),
+               name_);
+    return;
+  }
   LotusCheck(lotus_nchw_f32_to_nhwc_f16(x.DataF32(), outputs_[0]->tensor_.Data(), x.Dim(0), x.Dim(1), x.Dim(2),
                                         x.Dim(3), stream),
              name_);
@@ -92,11 +106,41 @@ void OutputConvertLayer::Forward(cudaStream_t stream) {
 
 // ------------------------------------------------------------------ conv
 Conv2dLayer::Conv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, int kw, int sh, int sw, int ph,
-                         int pw, cudaStream_t stream) {
+                         int pw, cudaStream_t stream, int s2d) {
   name_ = op.name;
   type_ = op.type;
   inputs_name_ = {op.inputs.at(0)};
   outputs_name_ = {op.outputs.at(0)};
+  flops_per_pixel_ = 2.0 * c_out * c_in * kh * kw;
+  const size_t w_elems = static_cast<size_t>(c_out) * c_in * kh * kw;
+  std::shared_ptr<void> w32;
+  if (s2d > 1) {
+    // W'[co][(a*f + b)*Cin + c][r'][s'] = W[co][c][f*r' + a][f*s' + b] (0 past the kernel)
+    auto it = op.attrs.find("weight");
+    if (it == op.attrs.end() || it->second.data.size() != w_elems * 4)
+      throw std::runtime_error(name_ + ": missing or mis-sized weight");
+    const float* w = reinterpret_cast<const float*>(it->second.data.data());
+    const int f = s2d, kh2 = (kh + f - 1) / f, kw2 = (kw + f - 1) / f, c2 = c_in * f * f;
+    std::vector<float> w2(static_cast<size_t>(c_out) * c2 * kh2 * kw2, 0.f);
+    for (int co = 0; co < c_out; ++co)
+      for (int c = 0; c < c_in; ++c)
+        for (int r = 0; r < kh; ++r)
+          for (int q = 0; q < kw; ++q) {
+            const int a = r % f, r2 = r / f, b = q % f, q2 = q / f;
+            const int cc = (a * f + b) * c_in + c;
+            w2[((static_cast<size_t>(co) * c2 + cc) * kh2 + r2) * kw2 + q2] =
+                w[((static_cast<size_t>(co) * c_in + c) * kh + r) * kw + q];
+          }
+    w32 = upload_host(w2, stream);
+    c_in = c2;
+    kh = kh2;
+    kw = kw2;
+    sh = sw = 1;
+    ph = pw = 0;
+  } else {
+    w32 = upload_f32(op, "weight", w_elems, stream);
+    if (!w32) throw std::runtime_error(name_ + ": missing weight");
+  }
   desc_.c_in = c_in;
   desc_.c_out = c_out;
   desc_.kh = kh;
@@ -110,8 +154,6 @@ Conv2dLayer::Conv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, 
   desc_.n = 1;
   desc_.h = kh;
   desc_.w = kw;
-  auto w32 = upload_f32(op, "weight", static_cast<size_t>(c_out) * c_in * kh * kw, stream);
-  if (!w32) throw std::runtime_error(name_ + ": missing weight");
   w_bytes_ = lotus_conv2d_packed_weight_bytes(&desc_);
   w_packed_ = device_buffer(w_bytes_);
   LotusCheck(lotus_conv2d_prepack(static_cast<const float*>(w32.get()), w_packed_.get(), &desc_, stream), name_);
@@ -149,7 +191,7 @@ void Conv2dLayer::Forward(cudaStream_t stream) {
 double Conv2dLayer::Flops() const {
   int oh = 0, ow = 0;
   lotus_conv2d_out_hw(&desc_, &oh, &ow);
-  return 2.0 * desc_.n * oh * ow * static_cast<double>(desc_.c_out) * desc_.c_in * desc_.kh * desc_.kw;
+  return static_cast<double>(desc_.n) * oh * ow * flops_per_pixel_;
 }
 
 // ------------------------------------------------------------------ tconv

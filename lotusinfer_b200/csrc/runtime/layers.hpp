@@ -67,11 +67,20 @@ class Layer {
   friend class Graph;
 };
 
-// NCHW fp32 graph input -> NHWC fp16 activation.
+// NCHW fp32 graph input -> NHWC fp16 activation, optionally as the
+// space-to-depth (factor f, zero padding) of the input for a rewritten stem.
 class InputConvertLayer : public Layer {
  public:
   InputConvertLayer(const std::string& in, const std::string& out);
+  void SetSpaceToDepth(int factor, int pad_h, int pad_w) {
+    s2d_ = factor;
+    pad_h_ = pad_h;
+    pad_w_ = pad_w;
+  }
   void Forward(cudaStream_t stream) override;
+
+ private:
+  int s2d_ = 1, pad_h_ = 0, pad_w_ = 0;
 };
 
 // NHWC fp16 activation -> NCHW fp32 graph output.
@@ -83,8 +92,11 @@ class OutputConvertLayer : public Layer {
 
 class Conv2dLayer : public Layer {
  public:
+  // s2d > 1 rewrites a stride-s2d conv as a stride-1 conv over the
+  // space-to-depth input: Cin*s2d^2 channels, kernel ceil(k/s2d), no padding
+  // (the padding moves into the input conversion).
   Conv2dLayer(const pnnx::Operator& op, int c_in, int c_out, int kh, int kw, int sh, int sw, int ph, int pw,
-              cudaStream_t stream);
+              cudaStream_t stream, int s2d = 1);
   void SetResidual(const std::string& operand) {
     residual_name_ = operand;
     inputs_name_.push_back(operand);
@@ -100,6 +112,7 @@ class Conv2dLayer : public Layer {
   }
 
  private:
+  double flops_per_pixel_ = 0.0;  // 2*Cout*Cin*kh*kw of the model's own conv
   size_t w_bytes_ = 0;
   std::shared_ptr<void> w_packed_;
   std::shared_ptr<void> bias_;

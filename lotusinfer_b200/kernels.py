@@ -41,6 +41,16 @@ def to_nhwc(x: torch.Tensor) -> torch.Tensor:
     return y
 
 
+def space_to_depth(x: torch.Tensor, factor: int, pad: int, out_hw) -> torch.Tensor:
+    """NCHW fp32 (cuda) -> NHWC fp16 [N, OH, OW, Cs(C*f*f)] space-to-depth of the padded image."""
+    x = x.contiguous()
+    n, c, h, w = x.shape
+    oh, ow = out_hw
+    y = torch.empty((n, oh, ow, channel_stride(c * factor * factor)), dtype=torch.float16, device=x.device)
+    check(abi.lib().lotus_space_to_depth_f16(_ptr(x), _ptr(y), n, c, h, w, factor, pad, pad, oh, ow, _stream()))
+    return y
+
+
 def from_nhwc(y: torch.Tensor, c: int) -> torch.Tensor:
     """NHWC fp16 [N, H, W, Cs] -> NCHW fp32 with c channels."""
     n, h, w, cs = y.shape

@@ -103,6 +103,34 @@ def test_alexnet_matches_oracle(model_dir, batch):
     g.close()
 
 
+S2D_STEM = {"resnet18": 2, "alexnet": 4}  # stem stride = space-to-depth factor
+
+
+def _s2d_weight(w, f):
+    """W'[co, (a*f+b)*C + c, r', s'] = W[co, c, f*r' + a, f*s' + b] (zero past the kernel)."""
+    co, c, kh, kw = w.shape
+    kh2, kw2 = -(-kh // f), -(-kw // f)
+    out = np.zeros((co, c * f * f, kh2, kw2), np.float32)
+    for r in range(kh):
+        for q in range(kw):
+            a, b = r % f, q % f
+            out[:, (a * f + b) * c:(a * f + b + 1) * c, r // f, q // f] = w[:, :, r, q]
+    return out
+
+
+def test_s2d_stem_matches_direct_stem(model_dir):
+    """The space-to-depth stem rewrite leaves ResNet-18 and AlexNet outputs unchanged up to fp16 rounding."""
+    from lotusinfer_b200 import synth
+    for name in ("resnet18", "alexnet"):
+        x = synth.synthetic_input(name, 2, seed=3)
+        g1, _, _ = _graph(name, model_dir, 2)
+        g2, _, _ = _graph(name, model_dir, 2, s2d_stem=False)
+        a, b = g1.run(x), g2.run(x)
+        assert rel_l2(a, b) < 2e-3, (name, rel_l2(a, b))
+        g1.close()
+        g2.close()
+
+
 @pytest.mark.parametrize("name", ["resnet18", "unet", "alexnet"])
 def test_graph_packed_weights_equal_standalone_prepack(model_dir, name):
     """Every layer's packed weights inside the runtime equal the standalone
@@ -121,7 +149,10 @@ def test_graph_packed_weights_equal_standalone_prepack(model_dir, name):
         if w is None:
             continue
         n = layer["name"]
-        wt = torch.from_numpy(W[n + ".weight"]).cuda()
+        w_np = W[n + ".weight"]
+        if i == 1 and layer["type"] == "nn.Conv2d" and name in S2D_STEM:
+            w_np = _s2d_weight(w_np, S2D_STEM[name])  # the stem runs over the space-to-depth input
+        wt = torch.from_numpy(w_np).cuda()
         if layer["type"] == "nn.ConvTranspose2d":
             ref = K.tconv2d_prepack(wt)
         elif layer["type"] == "nn.Linear":

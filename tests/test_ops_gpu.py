@@ -102,6 +102,23 @@ def test_conv2d_repeatable_and_no_bias():
     assert_close(K.from_nhwc(a, 128).cpu().numpy(), oracle.conv2d(x, wt, None, (1, 1), (1, 1)))
 
 
+@pytest.mark.parametrize("case", [(2, 3, 224, 224, 2, 3, 112 + 3, 112 + 3), (1, 3, 224, 224, 4, 2, 57, 57),
+                                  (1, 5, 17, 13, 3, 1, 7, 6)])
+def test_space_to_depth_exact(case):
+    K = _k()
+    n, c, h, w, f, p, oh, ow = case
+    x = _f16(_rng(13).normal(0, 1, (n, c, h, w)))
+    xp = np.zeros((n, c, f * oh + f, f * ow + f), np.float32)
+    hh, ww = min(h, f * oh - p), min(w, f * ow - p)
+    xp[:, :, p:p + hh, p:p + ww] = x[:, :, :hh, :ww]
+    want = np.zeros((n, oh, ow, K.channel_stride(c * f * f)), np.float32)
+    for a in range(f):
+        for b in range(f):
+            want[..., (a * f + b) * c:(a * f + b + 1) * c] = xp[:, :, a:a + f * oh:f, b:b + f * ow:f].transpose(0, 2, 3, 1)
+    got = K.space_to_depth(_gpu(x), f, p, (oh, ow)).float().cpu().numpy()
+    np.testing.assert_array_equal(got, want)
+
+
 def test_layout_round_trip_exact_for_fp16_values():
     K = _k()
     x = _f16(_rng(12).normal(0, 3, (3, 13, 9, 7)))
