@@ -172,6 +172,7 @@ def main():
     from datetime import timedelta
 
     from lotusinfer_b200 import abi, synth
+    from lotusinfer_b200.dist import gather_outputs
     from lotusinfer_b200.graph import Graph
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -182,6 +183,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
 
     B = args.batch
+    if rank == 0:
+        synth.make_model("resnet18", MODEL_DIR, seed=0)
+    if world > 1:
+        dist.barrier()
     param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
     g = Graph(param, binp, B, device=local)
     gstream = torch.cuda.ExternalStream(g.stream, device=torch.device("cuda", local))
@@ -195,7 +200,7 @@ def main():
         if world > 1:
             g.get_output_into(logits_dev.data_ptr(), logits_dev.numel(), stream=g.stream)
             with torch.cuda.stream(gstream):
-                dist.all_gather_into_tensor(gathered, logits_dev)
+                gather_outputs(logits_dev, gathered)
 
     def barrier():
         torch.cuda.synchronize()

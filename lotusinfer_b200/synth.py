@@ -243,7 +243,7 @@ def random_weights(g: ParamWriter, seed: int) -> Dict[str, np.ndarray]:
 
 def write_bin(path: str, weights: Dict[str, np.ndarray]) -> None:
     """Stored (uncompressed) zip with one raw fp32 entry per attribute."""
-    tmp = path + ".tmp"
+    tmp = f"{path}.{os.getpid()}.tmp"  # concurrent writers (one per rank) never share a temporary
     with zipfile.ZipFile(tmp, "w", compression=zipfile.ZIP_STORED, allowZip64=True) as z:
         for key in sorted(weights):
             z.writestr(zipfile.ZipInfo(key), np.ascontiguousarray(weights[key], "<f4").tobytes())
@@ -258,9 +258,10 @@ def make_model(name: str, out_dir: str, seed: int = 0) -> Tuple[str, str]:
     binp = os.path.join(out_dir, f"{name}_s{seed}.pnnx.bin")
     text = g.text()
     if not os.path.exists(param) or open(param).read() != text:
-        with open(param + ".tmp", "w") as f:
+        tmp = f"{param}.{os.getpid()}.tmp"
+        with open(tmp, "w") as f:
             f.write(text)
-        os.replace(param + ".tmp", param)
+        os.replace(tmp, param)
     if not os.path.exists(binp):
         write_bin(binp, random_weights(g, seed))
     return param, binp
