@@ -120,17 +120,18 @@ __global__ void nhwc_to_nchw_kernel(const __half* __restrict__ x, float* __restr
 // y[n, i, j, (a*f + b)*c + ch] = xpad[n, ch, f*i + a, f*j + b] with
 // xpad[.., u, v] = x[.., u - pad_h, v - pad_w] inside the image, 0 outside;
 // channels c*f*f .. cs-1 are zero.  One thread per output pixel.
+template <typename IT>
 __global__ void space_to_depth_kernel(const float* __restrict__ x, __half* __restrict__ y, int n, int c, int h, int w,
                                       int f, int pad_h, int pad_w, int oh, int ow, int cs) {
-  const size_t pixels = static_cast<size_t>(n) * oh * ow;
-  const size_t plane = static_cast<size_t>(h) * w;
-  for (size_t p = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; p < pixels;
-       p += static_cast<size_t>(gridDim.x) * blockDim.x) {
+  const IT pixels = static_cast<IT>(n) * oh * ow;
+  const IT plane = static_cast<IT>(h) * w;
+  for (IT p = blockIdx.x * static_cast<IT>(blockDim.x) + threadIdx.x; p < pixels;
+       p += static_cast<IT>(gridDim.x) * blockDim.x) {
     const int j = static_cast<int>(p % ow);
-    const size_t t = p / ow;
+    const IT t = p / ow;
     const int i = static_cast<int>(t % oh);
     const int img = static_cast<int>(t / oh);
-    const float* xb = x + static_cast<size_t>(img) * c * plane;
+    const float* xb = x + static_cast<IT>(img) * c * plane;
     uint4* yd = reinterpret_cast<uint4*>(y + p * cs);
     // channel order (a, b, ch): consecutive threads (consecutive j) read
     // consecutive f-wide runs of one input row, so each warp load coalesces
@@ -142,7 +143,7 @@ __global__ void space_to_depth_kernel(const float* __restrict__ x, __half* __res
       for (int b = 0; b < f; ++b) {
         const int col = f * j + b - pad_w;
         const bool ok = row_ok && col >= 0 && col < w;
-        const float* src = xb + static_cast<size_t>(u) * w + col;
+        const float* src = xb + static_cast<IT>(u) * w + col;
         for (int ch = 0; ch < c; ++ch) {
           v[q++] = ok ? __ldg(src + ch * plane) : 0.f;
           if (q == 8) {
@@ -164,8 +165,12 @@ __global__ void space_to_depth_kernel(const float* __restrict__ x, __half* __res
 cudaError_t launch_space_to_depth(const float* x, void* y, int n, int c, int h, int w, int f, int pad_h, int pad_w,
                                   int oh, int ow, int cs, cudaStream_t s) {
   const size_t pixels = static_cast<size_t>(n) * oh * ow;
-  space_to_depth_kernel<<<grid_for(pixels, 256), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w, f, pad_h, pad_w,
-                                                              oh, ow, cs);
+  if (static_cast<size_t>(n) * c * h * w < (1u << 31) && pixels * cs < (1u << 31))
+    space_to_depth_kernel<int><<<grid_for(pixels, 256, 32), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w, f,
+                                                                         pad_h, pad_w, oh, ow, cs);
+  else
+    space_to_depth_kernel<size_t><<<grid_for(pixels, 256), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w, f,
+                                                                        pad_h, pad_w, oh, ow, cs);
   note_launch();
   return cudaGetLastError();
 }

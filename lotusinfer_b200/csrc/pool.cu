@@ -20,23 +20,26 @@ namespace lotus_impl {
 
 using namespace lotus_dev;
 
+// IT is the index type: 32-bit when every element offset fits (the common
+// case; 64-bit division in the grid-stride loop dominated the kernel), else 64-bit.
+template <typename IT>
 __global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __restrict__ y, int n, int c, int cs, int h,
                                     int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int act) {
   const int groups = cs / 8;
-  const size_t total = static_cast<size_t>(n) * oh * ow * groups;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+  const IT total = static_cast<IT>(n) * oh * ow * groups;
+  for (IT i = blockIdx.x * static_cast<IT>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<IT>(gridDim.x) * blockDim.x) {
     const int g = static_cast<int>(i % groups);
-    const size_t pix = i / groups;
+    const IT pix = i / groups;
     const int ox = static_cast<int>(pix % ow);
-    const size_t t = pix / ow;
+    const IT t = pix / ow;
     const int oy = static_cast<int>(t % oh);
     const int img = static_cast<int>(t / oh);
     float m[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) m[j] = -INFINITY;
     const int y0 = oy * sh - ph, x0 = ox * sw - pw;
-    const __half* xb = x + static_cast<size_t>(img) * h * w * cs + g * 8;
+    const __half* xb = x + static_cast<IT>(img) * h * w * cs + g * 8;
     for (int r = 0; r < kh; ++r) {
       const int iy = y0 + r;
       if (iy < 0 || iy >= h) continue;
@@ -44,7 +47,7 @@ __global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __rest
         const int ix = x0 + s;
         if (ix < 0 || ix >= w) continue;
         float f[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (static_cast<size_t>(iy) * w + ix) * cs)), f);
+        unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (static_cast<IT>(iy) * w + ix) * cs)), f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], f[j]);
       }
@@ -96,8 +99,13 @@ __global__ void adaptive_avgpool_nhwc_kernel(const __half* __restrict__ x, void*
 cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow, int kh, int kw,
                            int sh, int sw, int ph, int pw, int act, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
-  maxpool_nhwc_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y), n,
-                                                           c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
+  const bool small = static_cast<size_t>(n) * h * w * cs < (1u << 31) && total < (1u << 31);
+  if (small)
+    maxpool_nhwc_kernel<int><<<grid_for(total, 256, 32), 256, 0, s>>>(
+        static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
+  else
+    maxpool_nhwc_kernel<size_t><<<grid_for(total, 256), 256, 0, s>>>(
+        static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
   note_launch();
   return cudaGetLastError();
 }
