@@ -23,6 +23,20 @@
 //   warps 10-13 (AMODE 0 only) gather the im2col rows with 16-byte cp.async
 //              for channel counts that are not a multiple of 64 (stem, U-Net
 //              level 1), using a per-CTA table of (r, s, c) per 8-channel chunk.
+//
+// Resident-weight halo mode (AMODE 3): stride-1 convs with Cs_in of 16, 32 or
+// 64 channels whose whole weight matrix fits in shared memory next to two or
+// more activation buffers (the space-to-depth stem, ResNet stage 1, U-Net
+// level 1-2).  The weights are loaded once per CTA.  The M axis of one image
+// runs over positions q = oy * Wp + ox of the zero-padded input width
+// Wp = W + 2*pw (columns ox >= OW are computed and dropped).  Output q under
+// tap (r, s) reads padded input pixel q + r*Wp + s, so one tiled TMA box of R
+// whole padded rows (Cs_in channels a row, swizzled at the row's width) holds
+// the A operand of every tap of a 128-position tile: tap (r, s) is the same
+// buffer with the descriptor start moved by (q0 % Wp + r*Wp + s) rows.  The
+// swizzle is a function of the shared-memory address, so a start moved by
+// whole rows reads what the TMA wrote.  The MMA thread waits once per tile
+// instead of once per 64-wide K block.
 // The epilogue of tile i overlaps the main loop of tile i+1.  Every wait is
 // bounded; an expired wait records an error code and the CTA drains and exits.
 //
@@ -45,6 +59,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <mutex>
 
 #include "kernels.h"
@@ -79,7 +94,19 @@ struct ConvTcParams {
   int bias_smem; // 1: bias staged in shared memory (<= kBiasMax columns), 0: read from global
   // transposed-conv scatter geometry
   int t_oh, t_ow, t_sh, t_sw, t_ph, t_pw, t_kw, t_cout;
+  // resident-weight halo mode geometry (AMODE 3)
+  int Wp;           // padded input width W + 2*pw
+  int tpi;          // 128-position tiles per image
+  int halo_off;     // byte offset of the first halo buffer (after the weights)
+  int halo_stride;  // bytes per halo buffer (multiple of 1024)
+  int halo_slots;   // halo buffers in the ring (2..kHaloSlotsMax)
+  int halo_bytes;   // bytes one halo box writes
+  int a_rowbytes;   // Cs_in * 2: 32, 64 or 128
+  int a_layout;     // tcgen05 descriptor swizzle code of that row width
 };
+
+constexpr int kHaloSlotsMax = 4;
+constexpr int kHaloRegion = 200 * 1024;  // weights + halo ring (AMODE 3)
 
 template <int BN, int STAGES, int AMODE>
 struct Cfg {
@@ -93,15 +120,30 @@ struct Cfg {
   static constexpr int kThreads = AMODE == 0 ? 448 : 320;
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kAOff = 0;
-  static constexpr int kBOff = STAGES * kABytes;
-  static constexpr int kBarOff = kBOff + STAGES * kBBytes;
-  static constexpr int kNumBars = 2 * STAGES + 5;  // full, empty, tfull[2], tempty[2], mma_done
+  // AMODE 3 keeps resident weights and the halo ring in one region at 0
+  static constexpr int kBOff = AMODE == 3 ? kHaloRegion : STAGES * kABytes;
+  static constexpr int kBarOff = kBOff + (AMODE == 3 ? 0 : STAGES * kBBytes);
+  // full, empty, tfull[2], tempty[2], mma_done, hfull[kHaloSlotsMax], hempty[kHaloSlotsMax]
+  static constexpr int kNumBars = 2 * STAGES + 5 + 2 * kHaloSlotsMax;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
   static constexpr int kTableOff = kBiasOff + kBiasMax * 4;
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
   static constexpr uint32_t kTmemCols = 2 * BN;
 };
+
+// K-major shared-memory descriptor for rows of `rowbytes` (32/64/128) bytes
+// under the matching swizzle (`layout` 6/4/2); 8-row groups are 8*rowbytes
+// apart.  LBO is unused: one MMA's K=16 slice lies inside one swizzle row.
+__device__ __forceinline__ uint64_t make_sdesc_rows(uint32_t smem_addr, uint32_t rowbytes, uint32_t layout) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>((8u * rowbytes) >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(layout) << 61;
+  return d;
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
@@ -251,6 +293,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   uint64_t* tfull = empty + STAGES;   // [2] accumulator ready for the epilogue
   uint64_t* tempty = tfull + 2;       // [2] accumulator drained by the epilogue
   uint64_t* mma_done = tempty + 2;
+  uint64_t* hfull = mma_done + 1;            // [kHaloSlotsMax] AMODE 3: halo buffer loaded
+  uint64_t* hempty = hfull + kHaloSlotsMax;  // [kHaloSlotsMax] AMODE 3: halo buffer consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   float* s_bias = reinterpret_cast<float*>(smem + C::kBiasOff);
@@ -270,6 +314,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       mbar_init(&tempty[b], C::kEpiWarps);
     }
     mbar_init(mma_done, 1);
+    for (int h = 0; h < kHaloSlotsMax; ++h) {
+      mbar_init(&hfull[h], 1);
+      mbar_init(&hempty[h], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -327,8 +375,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const int m0 = (t / p.n_tiles) * kBlockM;
       const int n0 = (t % p.n_tiles) * BN;
       const int ab = lt & 1;
-      const int em = m0 + erow;
-      const bool rvalid = em < p.M;
+      int em = m0 + erow;
+      bool rvalid = em < p.M;
+      if (AMODE == 3) {
+        // position q of the padded-width grid -> output pixel
+        const int mt = t / p.n_tiles;
+        const int img = mt / p.tpi;
+        const int q = (mt - img * p.tpi) * kBlockM + erow;
+        const int oy = q / p.Wp;
+        const int ox = q - oy * p.Wp;
+        rvalid = oy < p.OH && ox < p.OW;
+        em = (img * p.OH + oy) * p.OW + ox;
+      }
       const bool tile_full = n0 + BN <= p.Cout;
       // residual rows do not depend on the accumulator: fetch them first
       uint4 res[kResVecs];
@@ -382,17 +440,50 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       uint32_t it = 0;
       int lt = 0;
       bool ok = true;
+      // AMODE 3: the resident weights land once, on full[0]
+      if (AMODE == 3 && p.tiles > static_cast<int>(blockIdx.x)) ok = mbar_wait_relaxed(&full[0], 0, kErrWaitFull);
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++lt) {
         const int ab = lt & 1;
-        if (*abort_flag || !mbar_wait(&tempty[ab], ((lt >> 1) & 1) ^ 1, kErrWaitAccum)) {
+        // the abort flag is read once per tile only: a shared-memory load
+        // here would wait for the MMAs already queued (the waits are relaxed
+        // for the same reason); a stalled peer still ends this loop through
+        // the bounded waits
+        if (*abort_flag || !mbar_wait_relaxed(&tempty[ab], ((lt >> 1) & 1) ^ 1, kErrWaitAccum)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * BN;
+        if (AMODE == 3) {
+          const int hs = lt % p.halo_slots;
+          if (!mbar_wait_relaxed(&hfull[hs], (lt / p.halo_slots) & 1, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int q0 = ((t / p.n_tiles) % p.tpi) * kBlockM;
+          const uint32_t rb = static_cast<uint32_t>(p.a_rowbytes);
+          const uint32_t a0 = smem_u32(sA) + p.halo_off + hs * p.halo_stride + static_cast<uint32_t>(q0 % p.Wp) * rb;
+          const uint32_t b0 = smem_u32(sA);
+          const int csub = p.Cs_in >> 4;  // K=16 slices per tap
+          int k0 = 0;
+          for (int r = 0; r < p.kh; ++r) {
+            for (int sx = 0; sx < p.kw; ++sx) {
+              const uint32_t a_tap = a0 + static_cast<uint32_t>(r * p.Wp + sx) * rb;
+              for (int c = 0; c < csub; ++c, k0 += 16) {
+                const uint32_t b_addr = b0 + (k0 >> 6) * C::kBBytes + (k0 & 63) * 2;
+                umma_f16(d_tmem, make_sdesc_rows(a_tap + c * 32, rb, p.a_layout), make_sdesc_sw128(b_addr), idesc,
+                         k0 != 0 ? 1u : 0u);
+              }
+            }
+          }
+          umma_commit(&hempty[hs]);
+          umma_commit(&tfull[ab]);
+          continue;
+        }
         for (int kb = 0; kb < p.KB; ++kb, ++it) {
           const int st = it % STAGES;
-          if (*abort_flag || !mbar_wait(&full[st], (it / STAGES) & 1, kErrWaitFull)) {
+          if (!mbar_wait_relaxed(&full[st], (it / STAGES) & 1, kErrWaitFull)) {
             ok = false;
             break;
           }
@@ -420,7 +511,25 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       uint32_t it = 0;
       constexpr uint32_t kTx = C::kBBytes + (AMODE != 0 ? kABytes : 0);
       bool ok = true;
-      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      if (AMODE == 3 && p.tiles > static_cast<int>(blockIdx.x)) {
+        // resident weights: every 64-wide K block of the (single) N tile
+        mbar_arrive_expect_tx(&full[0], static_cast<uint32_t>(p.KB) * C::kBBytes);
+        for (int kb = 0; kb < p.KB; ++kb) tma_load_2d(sA + kb * C::kBBytes, &tmap_w, &full[0], kb * kBlockK, 0);
+        int lt = 0;
+        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
+          const int hs = lt % p.halo_slots;
+          if (*abort_flag || !mbar_wait(&hempty[hs], ((lt / p.halo_slots) & 1) ^ 1, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const int mt = t / p.n_tiles;
+          const int img = mt / p.tpi;
+          const int q0 = (mt - img * p.tpi) * kBlockM;
+          mbar_arrive_expect_tx(&hfull[hs], static_cast<uint32_t>(p.halo_bytes));
+          tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], 0, -p.pw, q0 / p.Wp - p.ph, img);
+        }
+      }
+      for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3; t += gridDim.x) {
         const int m0 = (t / p.n_tiles) * kBlockM;
         const int n0 = (t % p.n_tiles) * BN;
         int wst = 0, hst = 0, nimg = 0;
@@ -598,6 +707,61 @@ static int make_tmap_im2col(CUtensorMap* map, const ConvTcArgs& a, int n_img) {
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// Halo map over the NHWC activation [N, H, W, Cs]: box of Cs channels x Wp
+// pixels x R rows of one image, swizzled at the row width (Cs * 2 bytes); the
+// kernel starts each box at pixel -pw so that its rows are whole zero-padded
+// input rows.
+static int make_tmap_halo(CUtensorMap* map, const ConvTcArgs& a, int n_img, int wp, int rows) {
+  auto enc = encode_tiled();
+  if (!enc) return -1;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Cs_in), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
+                        static_cast<cuuint64_t>(n_img)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.Cs_in) * 2, static_cast<cuuint64_t>(a.W) * a.Cs_in * 2,
+                           static_cast<cuuint64_t>(a.H) * a.W * a.Cs_in * 2};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(a.Cs_in), static_cast<cuuint32_t>(wp), static_cast<cuuint32_t>(rows), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle sw = a.Cs_in == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                : a.Cs_in == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+// Resident-weight halo plan of a conv at block width `bn`: fills the AMODE 3
+// fields of `p` and returns the fraction of computed positions that are real
+// outputs, or 0 when the layer does not fit the mode (stride 1, Cs_in of 16,
+// 32 or 64, one N tile, weights plus two halo buffers within kHaloRegion).
+static double halo_plan(const ConvTcArgs& a, int bn, ConvTcParams* p) {
+  const int wp = a.W + 2 * a.pw;
+  if (a.sh != 1 || a.sw != 1 || a.out_kind == 2 || a.n_cols > bn) return 0.0;
+  if (a.Cs_in != 16 && a.Cs_in != 32 && a.Cs_in != 64) return 0.0;
+  if (wp > 256 || a.OW != wp - a.kw + 1 || a.k_pad % kBlockK != 0) return 0.0;
+  const long q = static_cast<long>(a.OH) * wp;
+  const int tpi = static_cast<int>((q + kBlockM - 1) / kBlockM);
+  int max_off = 0;
+  for (int j = 0; j < tpi; ++j) max_off = std::max(max_off, (j * kBlockM) % wp);
+  const int rows = (max_off + (a.kh - 1) * wp + (a.kw - 1) + kBlockM - 1) / wp + 1;
+  if (rows > 256) return 0.0;
+  const int rb = a.Cs_in * 2;
+  const int w_bytes = (a.k_pad / kBlockK) * bn * kBlockK * 2;
+  const int halo_bytes = rb * wp * rows;
+  const int stride = (halo_bytes + 1023) & ~1023;
+  if (w_bytes >= kHaloRegion) return 0.0;
+  const int slots = std::min(kHaloSlotsMax, (kHaloRegion - w_bytes) / stride);
+  if (slots < 2) return 0.0;
+  p->Wp = wp;
+  p->tpi = tpi;
+  p->halo_off = w_bytes;
+  p->halo_stride = stride;
+  p->halo_slots = slots;
+  p->halo_bytes = halo_bytes;
+  p->a_rowbytes = rb;
+  p->a_layout = rb == 32 ? 6 : (rb == 64 ? 4 : 2);
+  return static_cast<double>(a.OH) * a.OW / (static_cast<double>(tpi) * kBlockM);
+}
+
 static int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -687,8 +851,13 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     amode = 2;
   else if (a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10))
     amode = 1;
+  // resident-weight halo mode where at least 70% of the computed positions are
+  // real outputs (the padding columns and each image's last tile are waste)
+  if (!plain_gemm && halo_plan(a, bn, &p) >= 0.70) amode = 3;
   const char* force = std::getenv("LOTUS_CONV_AMODE");
   if (force && std::atoi(force) == 0) amode = 0;
+  if (force && std::atoi(force) == 1 && amode == 3) amode = a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10) ? 1 : 0;
+  if (amode == 3) p.tiles = static_cast<int>(static_cast<long>(n_img) * p.tpi);
   if (amode == 0 && p.KB * 8 > kMaxTable) {
     *err = "conv: K too large for the gather path";
     return -2;
@@ -704,6 +873,10 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     *err = "conv: im2col tensor map encoding failed";
     return -3;
   }
+  if (amode == 3 && make_tmap_halo(&ma, a, n_img, p.Wp, p.halo_bytes / (p.a_rowbytes * p.Wp)) != 0) {
+    *err = "conv: halo tensor map encoding failed";
+    return -3;
+  }
   if (amode == 2 && make_tmap_2d(&ma, a.x, a.M, a.Cs_in, a.Cs_in, kBlockM) != 0) {
     *err = "conv: activation tensor map encoding failed";
     return -3;
@@ -711,12 +884,19 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
 
   cudaError_t e = cudaErrorInvalidValue;
   if (bn == 64) {
-    e = amode == 0 ? launch_impl<64, 8, 0>(mw, ma, p, stream)
-                   : (amode == 1 ? launch_impl<64, 8, 1>(mw, ma, p, stream) : launch_impl<64, 8, 2>(mw, ma, p, stream));
+    switch (amode) {
+      case 0: e = launch_impl<64, 8, 0>(mw, ma, p, stream); break;
+      case 1: e = launch_impl<64, 8, 1>(mw, ma, p, stream); break;
+      case 2: e = launch_impl<64, 8, 2>(mw, ma, p, stream); break;
+      default: e = launch_impl<64, 2, 3>(mw, ma, p, stream); break;
+    }
   } else {
-    e = amode == 0 ? launch_impl<128, 6, 0>(mw, ma, p, stream)
-                   : (amode == 1 ? launch_impl<128, 6, 1>(mw, ma, p, stream)
-                                 : launch_impl<128, 6, 2>(mw, ma, p, stream));
+    switch (amode) {
+      case 0: e = launch_impl<128, 6, 0>(mw, ma, p, stream); break;
+      case 1: e = launch_impl<128, 6, 1>(mw, ma, p, stream); break;
+      case 2: e = launch_impl<128, 6, 2>(mw, ma, p, stream); break;
+      default: e = launch_impl<128, 2, 3>(mw, ma, p, stream); break;
+    }
   }
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);

@@ -79,6 +79,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int er
   return false;
 }
 
+// Relaxed-semantics variant for the thread that issues tcgen05.mma.  An
+// acquiring try_wait (or any shared-memory load) issued behind queued MMAs
+// waits for them to drain, which serialises the tensor pipe stage by stage;
+// the relaxed form does not.  Callers follow it with
+// tcgen05.fence::after_thread_sync, which orders the MMAs they issue next
+// after the observed phase (the TMA bytes counted by that phase are in
+// shared memory once it completes).
+__device__ __forceinline__ bool mbar_try_wait_relaxed(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.relaxed.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_relaxed(uint64_t* bar, uint32_t parity, int err_code) {
+  for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
+    if (mbar_try_wait_relaxed(bar, parity)) return true;
+  }
+  atomicExch(&g_lotus_device_error, err_code);
+  return false;
+}
+
 // ---------------------------------------------------------------- cp.async
 // 16-byte global->shared copy; `src_bytes` = 0 writes 16 zero bytes.
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -111,6 +138,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 4-D tiled load (no multicast), coordinates innermost first.  The innermost
+// coordinate obeys the same 16-byte rule as tma_load_2d; the others may be
+// negative or past the end (those box elements read as zero).
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -57,6 +57,13 @@ CONV_CASES = [
     ("unet_1x1_sigmoid_cout1", 2, 32, 16, 16, 1, 1, 1, 0, 2, False),
     ("alexnet_11x11_s4", 1, 3, 63, 63, 64, 11, 4, 2, 1, False),
     ("5x5_cout192", 1, 64, 13, 13, 192, 5, 1, 2, 1, False),
+    # stride-1 layers with 16/32/64 channels and weights that fit in shared
+    # memory run the resident-weight halo path (32/64/128-byte swizzled rows)
+    ("halo_s2d_stem_like_cin12_4x4", 2, 12, 35, 35, 64, 4, 1, 0, 1, False),
+    ("halo_cin16_cout40", 2, 16, 30, 30, 40, 3, 1, 1, 0, False),
+    ("halo_stage1_residual", 4, 64, 56, 56, 64, 3, 1, 1, 1, True),
+    ("halo_cin32_cout128_sigmoid", 1, 32, 33, 31, 128, 3, 1, 1, 2, False),
+    ("halo_pad0_nonsquare", 2, 64, 34, 30, 64, 3, 1, 0, 1, False),
 ]
 
 
@@ -88,6 +95,17 @@ def test_conv2d_parity(case):
         got32 = y32.view(n, oh, ow, cout).permute(0, 3, 1, 2).cpu().numpy()
         assert_close(got32, want, what=case[0] + "/f32")
     _no_device_error()
+
+
+@pytest.mark.parametrize("amode", ["0", "1"])
+@pytest.mark.parametrize("case", [c for c in CONV_CASES if c[0] in (
+    "cfg1_64x56x56_3x3_relu", "halo_stage1_residual", "unet_32to64", "halo_s2d_stem_like_cin12_4x4")],
+    ids=lambda c: c[0])
+def test_conv2d_forced_paths(case, amode, monkeypatch):
+    """The cp.async gather (0) and im2col TMA (1) paths on layers that
+    default to the halo path give the same results."""
+    monkeypatch.setenv("LOTUS_CONV_AMODE", amode)
+    test_conv2d_parity(case)
 
 
 def test_conv2d_repeatable_and_no_bias():
