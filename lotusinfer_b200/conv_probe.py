@@ -4,6 +4,7 @@
 
 Layers (ResNet-18 at batch B, NHWC fp16, seeded random data):
   stem  3->64   7x7/2 on 224x224     s1   64->64   3x3/1 on 56x56 (+residual)
+  stem_s2d 12->64 4x4/1 on 115x115 (the stem after the graph's space-to-depth rewrite)
   s2d  64->128  3x3/2 on 56x56       s2  128->128  3x3/1 on 28x28
   s3  256->256  3x3/1 on 14x14       s4  512->512  3x3/1 on 7x7
   ds2  64->128  1x1/2 on 56x56
@@ -22,6 +23,7 @@ from . import kernels as K
 
 LAYERS = {
     "stem": (3, 224, 224, 64, 7, 2, 3, False),
+    "stem_s2d": (12, 115, 115, 64, 4, 1, 0, False),
     "s1": (64, 56, 56, 64, 3, 1, 1, True),
     "s2d": (64, 56, 56, 128, 3, 2, 1, False),
     "s2": (128, 28, 28, 128, 3, 1, 1, True),

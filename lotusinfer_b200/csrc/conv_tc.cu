@@ -13,8 +13,8 @@
 //              half): TMEM -> registers -> bias (staged in shared memory per
 //              tile), residual, activation -> fp16 NHWC / fp32 rows /
 //              transposed-conv scatter stores;
-//   warp 8     allocates 2 x BLOCK_N TMEM columns (double-buffered
-//              accumulator); one thread issues tcgen05.mma (M=128, N=BLOCK_N,
+//   warp 8     allocates all 512 TMEM columns as a ring of 512/BLOCK_N
+//              (at most 8) accumulators; one thread issues tcgen05.mma (M=128, N=BLOCK_N,
 //              K=16) and commits stage / accumulator releases;
 //   warp 9     one thread issues the TMA loads: the weight tile always, and
 //              the activation tile in im2col mode (AMODE 1: 3x3 / strided
@@ -37,7 +37,7 @@
 // swizzle is a function of the shared-memory address, so a start moved by
 // whole rows reads what the TMA wrote.  The MMA thread waits once per tile
 // instead of once per 64-wide K block.
-// The epilogue of tile i overlaps the main loop of tile i+1.  Every wait is
+// The epilogue of tile i overlaps the main loop of the tiles after it.  Every wait is
 // bounded; an expired wait records an error code and the CTA drains and exits.
 //
 // The same kernel runs the Linear GEMM (a 1x1 "image") and the stride==kernel
@@ -117,19 +117,28 @@ struct Cfg {
   static constexpr int kMmaWarp = 8;
   static constexpr int kTmaWarp = 9;
   static constexpr int kGatherWarp0 = 10;                  // AMODE 0: warps 10-13
-  static constexpr int kThreads = AMODE == 0 ? 448 : 320;
+  // AMODE 3: a second MMA-issuing warp (warp 10) takes every other tile; one
+  // thread issues at most one tcgen05.mma per ~80 cycles whatever N is, two
+  // issuing warps keep an N=128 accumulator at the tensor pipe's own rate
+  static constexpr int kMmaWarp2 = 10;
+  static constexpr int kMmaIssuers = AMODE == 3 ? 2 : 1;
+  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 352 : 320);
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kAOff = 0;
   // AMODE 3 keeps resident weights and the halo ring in one region at 0
   static constexpr int kBOff = AMODE == 3 ? kHaloRegion : STAGES * kABytes;
   static constexpr int kBarOff = kBOff + (AMODE == 3 ? 0 : STAGES * kBBytes);
-  // full, empty, tfull[2], tempty[2], mma_done, hfull[kHaloSlotsMax], hempty[kHaloSlotsMax]
-  static constexpr int kNumBars = 2 * STAGES + 5 + 2 * kHaloSlotsMax;
+  // TMEM accumulator ring: all 512 columns (one CTA per SM), at most 8 tiles,
+  // so the MMA runs several tiles ahead of the epilogue and the handoff
+  // latency of one accumulator (commit -> TMEM load -> release) stays hidden
+  static constexpr int kAccBufs = 512 / BN < 8 ? 512 / BN : 8;
+  // full, empty, tfull[kAccBufs], tempty[kAccBufs], mma_done, hfull[kHaloSlotsMax], hempty[kHaloSlotsMax]
+  static constexpr int kNumBars = 2 * STAGES + 2 * kAccBufs + 1 + 2 * kHaloSlotsMax;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
   static constexpr int kTableOff = kBiasOff + kBiasMax * 4;
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
-  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr uint32_t kTmemCols = kAccBufs * BN;
 };
 
 // K-major shared-memory descriptor for rows of `rowbytes` (32/64/128) bytes
@@ -290,9 +299,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   uint8_t* sB = smem + C::kBOff;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;   // [2] accumulator ready for the epilogue
-  uint64_t* tempty = tfull + 2;       // [2] accumulator drained by the epilogue
-  uint64_t* mma_done = tempty + 2;
+  uint64_t* tfull = empty + STAGES;        // [kAccBufs] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + C::kAccBufs;  // [kAccBufs] accumulator drained by the epilogue
+  uint64_t* mma_done = tempty + C::kAccBufs;
   uint64_t* hfull = mma_done + 1;            // [kHaloSlotsMax] AMODE 3: halo buffer loaded
   uint64_t* hempty = hfull + kHaloSlotsMax;  // [kHaloSlotsMax] AMODE 3: halo buffer consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
@@ -309,11 +318,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       mbar_init(&full[s], AMODE == 0 ? 128 + 1 : 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::kAccBufs; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], C::kEpiWarps);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, C::kMmaIssuers);
     for (int h = 0; h < kHaloSlotsMax; ++h) {
       mbar_init(&hfull[h], 1);
       mbar_init(&hempty[h], 1);
@@ -374,7 +383,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
       const int m0 = (t / p.n_tiles) * kBlockM;
       const int n0 = (t % p.n_tiles) * BN;
-      const int ab = lt & 1;
+      const int ab = lt % C::kAccBufs;
       int em = m0 + erow;
       bool rvalid = em < p.M;
       if (AMODE == 3) {
@@ -403,7 +412,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         sc_iy = rem / p.OW;
         sc_ix = rem - sc_iy * p.OW;
       }
-      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt >> 1) & 1, kErrWaitAccum);
+      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAccBufs) & 1, kErrWaitAccum);
       if (!ok) *abort_flag = 1;
       tc_fence_after();
       // drain this warp's share of the accumulator into registers, then hand
@@ -433,22 +442,24 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
       }
     }
-  } else if (warp == C::kMmaWarp) {
-    // ================================================================ MMA issuer
+  } else if (warp == C::kMmaWarp || (C::kMmaIssuers == 2 && warp == C::kMmaWarp2)) {
+    // ================================================================ MMA issuer(s)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16_m128(BN);
+      const int issuer = warp == C::kMmaWarp ? 0 : 1;  // AMODE 3: tiles with lt % 2 == issuer
       uint32_t it = 0;
       int lt = 0;
       bool ok = true;
       // AMODE 3: the resident weights land once, on full[0]
       if (AMODE == 3 && p.tiles > static_cast<int>(blockIdx.x)) ok = mbar_wait_relaxed(&full[0], 0, kErrWaitFull);
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++lt) {
-        const int ab = lt & 1;
+        if (C::kMmaIssuers == 2 && (lt & 1) != issuer) continue;
+        const int ab = lt % C::kAccBufs;
         // the abort flag is read once per tile only: a shared-memory load
         // here would wait for the MMAs already queued (the waits are relaxed
         // for the same reason); a stalled peer still ends this loop through
         // the bounded waits
-        if (*abort_flag || !mbar_wait_relaxed(&tempty[ab], ((lt >> 1) & 1) ^ 1, kErrWaitAccum)) {
+        if (*abort_flag || !mbar_wait_relaxed(&tempty[ab], ((lt / C::kAccBufs) & 1) ^ 1, kErrWaitAccum)) {
           ok = false;
           break;
         }
@@ -461,19 +472,23 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             break;
           }
           tc_fence_after();
+          // descriptors are built once per tile; a tap or K step only moves
+          // the start-address field (16-byte units in the low bits; every
+          // address stays below 232448 bytes, so the 14-bit field cannot carry)
           const int q0 = ((t / p.n_tiles) % p.tpi) * kBlockM;
           const uint32_t rb = static_cast<uint32_t>(p.a_rowbytes);
-          const uint32_t a0 = smem_u32(sA) + p.halo_off + hs * p.halo_stride + static_cast<uint32_t>(q0 % p.Wp) * rb;
-          const uint32_t b0 = smem_u32(sA);
+          const uint64_t a_desc = make_sdesc_rows(
+              smem_u32(sA) + p.halo_off + hs * p.halo_stride + static_cast<uint32_t>(q0 % p.Wp) * rb, rb, p.a_layout);
+          const uint64_t b_desc = make_sdesc_sw128(smem_u32(sA));
           const int csub = p.Cs_in >> 4;  // K=16 slices per tap
+          const uint32_t row16 = rb >> 4, wp16 = static_cast<uint32_t>(p.Wp) * row16;
           int k0 = 0;
           for (int r = 0; r < p.kh; ++r) {
             for (int sx = 0; sx < p.kw; ++sx) {
-              const uint32_t a_tap = a0 + static_cast<uint32_t>(r * p.Wp + sx) * rb;
+              const uint64_t a_tap = a_desc + static_cast<uint32_t>(r) * wp16 + static_cast<uint32_t>(sx) * row16;
               for (int c = 0; c < csub; ++c, k0 += 16) {
-                const uint32_t b_addr = b0 + (k0 >> 6) * C::kBBytes + (k0 & 63) * 2;
-                umma_f16(d_tmem, make_sdesc_rows(a_tap + c * 32, rb, p.a_layout), make_sdesc_sw128(b_addr), idesc,
-                         k0 != 0 ? 1u : 0u);
+                const uint32_t b_off16 = static_cast<uint32_t>((k0 >> 6) * (C::kBBytes >> 4) + ((k0 & 63) >> 3));
+                umma_f16(d_tmem, a_tap + 2u * c, b_desc + b_off16, idesc, k0 != 0 ? 1u : 0u);
               }
             }
           }
