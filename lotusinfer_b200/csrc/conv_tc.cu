@@ -16,6 +16,10 @@
 //   warp 8     allocates all 512 TMEM columns as a ring of 512/BLOCK_N
 //              (at most 8) accumulators; one thread issues tcgen05.mma (M=128, N=BLOCK_N,
 //              K=16) and commits stage / accumulator releases;
+//   warps 10/11 (AMODE 1/2) a second MMA issuer and TMA producer pair with its
+//              own half of the stages takes every other tile: one thread
+//              issues at most one tcgen05.mma per ~80 cycles, so a single
+//              issuer leaves the tensor pipe idle between MMAs;
 //   warp 9     one thread issues the TMA loads: the weight tile always, and
 //              the activation tile in im2col mode (AMODE 1: 3x3 / strided
 //              convs with Cs_in % 64 == 0) or tiled mode (AMODE 2: 1x1 stride-1
@@ -121,8 +125,14 @@ struct Cfg {
   // thread issues at most one tcgen05.mma per ~80 cycles whatever N is, two
   // issuing warps keep an N=128 accumulator at the tensor pipe's own rate
   static constexpr int kMmaWarp2 = 10;
-  static constexpr int kMmaIssuers = AMODE == 3 ? 2 : 1;
-  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 352 : 320);
+  // AMODE 1/2: two independent pipelines (producer warp 9 + MMA warp 8 and
+  // producer warp 11 + MMA warp 10), each with half of the stages, take
+  // alternate tiles and share the epilogue warps and the accumulator ring
+  static constexpr int kRings = (AMODE == 1 || AMODE == 2) ? 2 : 1;
+  static constexpr int kRingStages = STAGES / kRings;
+  static constexpr int kTmaWarp2 = 11;
+  static constexpr int kMmaIssuers = (AMODE == 3 || kRings == 2) ? 2 : 1;
+  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 352 : 384);
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kAOff = 0;
   // AMODE 3 keeps resident weights and the halo ring in one region at 0
@@ -446,7 +456,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // ================================================================ MMA issuer(s)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16_m128(BN);
-      const int issuer = warp == C::kMmaWarp ? 0 : 1;  // AMODE 3: tiles with lt % 2 == issuer
+      const int issuer = warp == C::kMmaWarp ? 0 : 1;  // two issuers: tiles with lt % 2 == issuer
       uint32_t it = 0;
       int lt = 0;
       bool ok = true;
@@ -497,8 +507,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           continue;
         }
         for (int kb = 0; kb < p.KB; ++kb, ++it) {
-          const int st = it % STAGES;
-          if (!mbar_wait_relaxed(&full[st], (it / STAGES) & 1, kErrWaitFull)) {
+          const int st = issuer * C::kRingStages + static_cast<int>(it % C::kRingStages);
+          if (!mbar_wait_relaxed(&full[st], (it / C::kRingStages) & 1, kErrWaitFull)) {
             ok = false;
             break;
           }
@@ -520,9 +530,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, kErrWaitFull);
     }
-  } else if (warp == C::kTmaWarp) {
-    // ================================================================ TMA producer
+  } else if (warp == C::kTmaWarp || (C::kRings == 2 && warp == C::kTmaWarp2)) {
+    // ================================================================ TMA producer(s)
     if (lane == 0) {
+      const int ring = warp == C::kTmaWarp ? 0 : 1;  // kRings == 2: tiles with lt % 2 == ring
       uint32_t it = 0;
       constexpr uint32_t kTx = C::kBBytes + (AMODE != 0 ? kABytes : 0);
       bool ok = true;
@@ -544,7 +555,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], 0, -p.pw, q0 / p.Wp - p.ph, img);
         }
       }
-      for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3; t += gridDim.x) {
+      int plt = 0;
+      for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3; t += gridDim.x, ++plt) {
+        if (C::kRings == 2 && (plt & 1) != ring) continue;
         const int m0 = (t / p.n_tiles) * kBlockM;
         const int n0 = (t % p.n_tiles) * BN;
         int wst = 0, hst = 0, nimg = 0;
@@ -558,8 +571,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
         int r = 0, s = 0, c0 = 0;
         for (int kb = 0; kb < p.KB; ++kb, ++it) {
-          const int st = it % STAGES;
-          if (*abort_flag || !mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, kErrWaitEmpty)) {
+          const int st = ring * C::kRingStages + static_cast<int>(it % C::kRingStages);
+          if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kRingStages) & 1) ^ 1, kErrWaitEmpty)) {
             ok = false;
             break;
           }
