@@ -109,8 +109,11 @@ struct ConvTcParams {
   int a_layout;     // tcgen05 descriptor swizzle code of that row width
 };
 
-constexpr int kHaloSlotsMax = 4;
-constexpr int kHaloRegion = 200 * 1024;  // weights + halo ring (AMODE 3)
+constexpr int kHaloSlotsMax = 8;
+// weights + halo ring (AMODE 3): what remains of the 227 KB of shared memory
+// after the barriers, a 1 KB bias area and the 1 KB alignment slack
+constexpr int kHaloRegion = 224 * 1024;
+constexpr int kHaloBiasMax = 256;  // AMODE 3 has one N tile of at most 128 columns
 
 template <int BN, int STAGES, int AMODE>
 struct Cfg {
@@ -146,7 +149,7 @@ struct Cfg {
   static constexpr int kNumBars = 2 * STAGES + 2 * kAccBufs + 1 + 2 * kHaloSlotsMax;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
-  static constexpr int kTableOff = kBiasOff + kBiasMax * 4;
+  static constexpr int kTableOff = kBiasOff + (AMODE == 3 ? kHaloBiasMax : kBiasMax) * 4;
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
   static constexpr uint32_t kTmemCols = kAccBufs * BN;
 };
@@ -465,11 +468,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++lt) {
         if (C::kMmaIssuers == 2 && (lt & 1) != issuer) continue;
         const int ab = lt % C::kAccBufs;
-        // the abort flag is read once per tile only: a shared-memory load
-        // here would wait for the MMAs already queued (the waits are relaxed
-        // for the same reason); a stalled peer still ends this loop through
-        // the bounded waits
-        if (*abort_flag || !mbar_wait_relaxed(&tempty[ab], ((lt / C::kAccBufs) & 1) ^ 1, kErrWaitAccum)) {
+        // no shared-memory loads (the abort flag included) in this loop: one
+        // issued behind queued MMAs waits for them to drain; the waits are
+        // relaxed for the same reason.  A stalled peer still ends the loop
+        // through the bounded waits.
+        if (!mbar_wait_relaxed(&tempty[ab], ((lt / C::kAccBufs) & 1) ^ 1, kErrWaitAccum)) {
           ok = false;
           break;
         }
@@ -513,12 +516,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + st * kABytes);
-          const uint32_t b_base = smem_u32(sB + st * C::kBBytes);
+          const uint64_t a_desc = make_sdesc_sw128(smem_u32(sA + st * kABytes));
+          const uint64_t b_desc = make_sdesc_sw128(smem_u32(sB + st * C::kBBytes));
 #pragma unroll
-          for (int k = 0; k < kBlockK / 16; ++k) {
-            umma_f16(d_tmem, make_sdesc_sw128(a_base + k * 32), make_sdesc_sw128(b_base + k * 32), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < kBlockK / 16; ++k) {  // K step = 32 bytes = 2 start-address units
+            umma_f16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[st]);
         }
@@ -805,6 +807,7 @@ template <int BN, int STAGES, int AMODE>
 static cudaError_t launch_impl(const CUtensorMap& mw, const CUtensorMap& ma, const ConvTcParams& p,
                                cudaStream_t stream) {
   using C = Cfg<BN, STAGES, AMODE>;
+  static_assert(C::bytes(AMODE == 0 ? kMaxTable : 0) <= 232448, "dynamic shared memory above 227 KB");
   const int smem = C::bytes(AMODE == 0 ? p.KB * 8 : 0);
   auto kern = conv_tc_kernel<BN, STAGES, AMODE>;
   static std::once_flag once;
