@@ -124,9 +124,10 @@ struct Cfg {
   static constexpr int kMmaWarp = 8;
   static constexpr int kTmaWarp = 9;
   static constexpr int kGatherWarp0 = 10;                  // AMODE 0: warps 10-13
-  // AMODE 3: a second MMA-issuing warp (warp 10) takes every other tile; one
-  // thread issues at most one tcgen05.mma per ~80 cycles whatever N is, two
-  // issuing warps keep an N=128 accumulator at the tensor pipe's own rate
+  // AMODE 3: four MMA-issuing warps (8, 10, 11, 12) take tiles round robin;
+  // one thread issues at most one tcgen05.mma per ~80 cycles whatever N is,
+  // plus the integer work between two issues, so the short tap loops of
+  // this mode need several issuers to keep the tensor pipe busy
   static constexpr int kMmaWarp2 = 10;
   // AMODE 1/2: two independent pipelines (producer warp 9 + MMA warp 8 and
   // producer warp 11 + MMA warp 10), each with half of the stages, take
@@ -134,8 +135,15 @@ struct Cfg {
   static constexpr int kRings = (AMODE == 1 || AMODE == 2) ? 2 : 1;
   static constexpr int kRingStages = STAGES / kRings;
   static constexpr int kTmaWarp2 = 11;
-  static constexpr int kMmaIssuers = (AMODE == 3 || kRings == 2) ? 2 : 1;
-  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 352 : 384);
+  static constexpr int kMmaIssuers = AMODE == 3 ? 4 : (kRings == 2 ? 2 : 1);
+  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 416 : 384);
+  // issuer index of a warp (-1: not an issuer): warp 8 is issuer 0, warps
+  // 10.. the others
+  static __device__ __forceinline__ int issuer_of(int warp) {
+    if (warp == kMmaWarp) return 0;
+    if (kMmaIssuers > 1 && warp >= kMmaWarp2 && warp < kMmaWarp2 + kMmaIssuers - 1) return warp - kMmaWarp2 + 1;
+    return -1;
+  }
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kAOff = 0;
   // AMODE 3 keeps resident weights and the halo ring in one region at 0
@@ -455,18 +463,22 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
       }
     }
-  } else if (warp == C::kMmaWarp || (C::kMmaIssuers == 2 && warp == C::kMmaWarp2)) {
+  } else if (C::issuer_of(warp) >= 0) {
     // ================================================================ MMA issuer(s)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16_m128(BN);
-      const int issuer = warp == C::kMmaWarp ? 0 : 1;  // two issuers: tiles with lt % 2 == issuer
+      const int issuer = C::issuer_of(warp);  // several issuers: tiles with lt % n_iss == issuer
+      // An issuer waiting on a halo buffer must never be two loads ahead of
+      // the producer (a parity wait would then match the previous phase), so
+      // AMODE 3 uses at most as many issuers as halo buffers; the others idle.
+      const int n_iss = AMODE == 3 ? (p.halo_slots < C::kMmaIssuers ? p.halo_slots : C::kMmaIssuers) : C::kMmaIssuers;
       uint32_t it = 0;
       int lt = 0;
       bool ok = true;
       // AMODE 3: the resident weights land once, on full[0]
       if (AMODE == 3 && p.tiles > static_cast<int>(blockIdx.x)) ok = mbar_wait_relaxed(&full[0], 0, kErrWaitFull);
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++lt) {
-        if (C::kMmaIssuers == 2 && (lt & 1) != issuer) continue;
+        if (C::kMmaIssuers > 1 && lt % n_iss != issuer) continue;
         const int ab = lt % C::kAccBufs;
         // no shared-memory loads (the abort flag included) in this loop: one
         // issued behind queued MMAs waits for them to drain; the waits are
@@ -556,6 +568,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           mbar_arrive_expect_tx(&hfull[hs], static_cast<uint32_t>(p.halo_bytes));
           tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], 0, -p.pw, q0 / p.Wp - p.ph, img);
         }
+        // before the CTA may exit (an abort included), every TMA load this
+        // thread issued has landed: the weights, and the last load of each
+        // halo buffer (earlier ones were waited for through hempty)
+        mbar_wait(&full[0], 0, kErrWaitFull);
+        for (int j = lt - 1; j >= 0 && j >= lt - p.halo_slots; --j)
+          mbar_wait(&hfull[j % p.halo_slots], (j / p.halo_slots) & 1, kErrWaitFull);
       }
       int plt = 0;
       for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3; t += gridDim.x, ++plt) {
@@ -597,6 +615,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
       }
       if (!ok) *abort_flag = 1;
+      if (AMODE == 1 || AMODE == 2) {
+        // every TMA load this thread issued has landed before the CTA may exit
+        // (the last kRingStages stages; earlier ones were waited for through
+        // their empty barriers)
+        for (int j = static_cast<int>(it) - 1; j >= 0 && j >= static_cast<int>(it) - C::kRingStages; --j)
+          mbar_wait(&full[ring * C::kRingStages + j % C::kRingStages], (j / C::kRingStages) & 1, kErrWaitFull);
+      }
     }
   } else if (AMODE == 0) {
     // ================================================================ A gather (cp.async)

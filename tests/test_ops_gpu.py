@@ -108,6 +108,34 @@ def test_conv2d_forced_paths(case, amode, monkeypatch):
     test_conv2d_parity(case)
 
 
+@pytest.mark.parametrize("case", [
+    # name, n, c, h, w, cout, k, pad, residual: 40-70 tiles per persistent CTA,
+    # so every halo buffer, accumulator and MMA issuer is reused many times
+    ("stem_s2d_like_n64", 64, 12, 115, 115, 64, 4, 0, False),
+    ("stage1_residual_n256", 256, 64, 56, 56, 64, 3, 1, True),
+    ("cin32_n128", 128, 32, 40, 40, 64, 3, 1, False),
+], ids=lambda c: c[0])
+def test_conv2d_halo_many_tiles_per_cta(case, monkeypatch):
+    """Full-size halo launches against the im2col / gather paths on the same
+    inputs (those paths are checked against the oracle on smaller cases)."""
+    K = _k()
+    _, n, c, h, w, cout, k, p, with_res = case
+    g = torch.Generator(device=DEV).manual_seed(zlib.crc32(case[0].encode()))
+    x = K.to_nhwc(torch.rand((n, c, h, w), device=DEV, generator=g) * 2 - 1)
+    wt = torch.randn((cout, c, k, k), device=DEV, generator=g) * (2.0 / (c * k * k)) ** 0.5
+    b = torch.rand(cout, device=DEV, generator=g) * 0.2 - 0.1
+    oh, ow = h + 2 * p - k + 1, w + 2 * p - k + 1
+    res = K.to_nhwc(torch.randn((n, cout, oh, ow), device=DEV, generator=g)) if with_res else None
+    wp = K.conv2d_prepack(wt, c)
+    y_halo = K.conv2d(x, c, wp, b, cout, k, 1, p, 1, residual=res)
+    y_again = K.conv2d(x, c, wp, b, cout, k, 1, p, 1, residual=res)
+    assert torch.equal(y_halo, y_again)
+    monkeypatch.setenv("LOTUS_CONV_AMODE", "1" if c % 64 == 0 else "0")
+    y_ref = K.conv2d(x, c, wp, b, cout, k, 1, p, 1, residual=res)
+    assert_close(K.from_nhwc(y_halo, cout).cpu().numpy(), K.from_nhwc(y_ref, cout).cpu().numpy(), what=case[0])
+    _no_device_error()
+
+
 def test_conv2d_repeatable_and_no_bias():
     K = _k()
     rng = _rng(11)
