@@ -41,6 +41,14 @@
 // swizzle is a function of the shared-memory address, so a start moved by
 // whole rows reads what the TMA wrote.  The MMA thread waits once per tile
 // instead of once per 64-wide K block.
+//
+// Streamed-weight halo mode (AMODE 4, selected with LOTUS_CONV_AMODE=4): the
+// same padded-row halo for stride-1
+// convs with Cs_in a multiple of 64 whose weights do not fit (ResNet stages
+// 2-3): one 64-channel halo box per (tile, channel chunk) serves the kh*kw
+// taps of that chunk, the weights stream per 64-wide K block in chunk-major
+// order (all taps of chunk 0, then chunk 1, ...).  Two producer/MMA pipelines
+// as in AMODE 1/2, each with its own weight stages and two halo buffers.
 // The epilogue of tile i overlaps the main loop of the tiles after it.  Every wait is
 // bounded; an expired wait records an error code and the CTA drains and exits.
 //
@@ -107,6 +115,7 @@ struct ConvTcParams {
   int halo_bytes;   // bytes one halo box writes
   int a_rowbytes;   // Cs_in * 2: 32, 64 or 128
   int a_layout;     // tcgen05 descriptor swizzle code of that row width
+  int cchunks;      // AMODE 4: 64-channel chunks per pixel (Cs_in / 64)
 };
 
 constexpr int kHaloSlotsMax = 8;
@@ -114,6 +123,10 @@ constexpr int kHaloSlotsMax = 8;
 // after the barriers, a 1 KB bias area and the 1 KB alignment slack
 constexpr int kHaloRegion = 224 * 1024;
 constexpr int kHaloBiasMax = 256;  // AMODE 3 has one N tile of at most 128 columns
+// AMODE 4: weight stages + 2 x kHalo4Slots halo buffers, bias of up to 512 columns
+constexpr int kHalo4Region = 220 * 1024;
+constexpr int kHalo4BiasMax = 512;
+constexpr int kHalo4Slots = 2;  // halo buffers per pipeline
 
 template <int BN, int STAGES, int AMODE>
 struct Cfg {
@@ -132,7 +145,7 @@ struct Cfg {
   // AMODE 1/2: two independent pipelines (producer warp 9 + MMA warp 8 and
   // producer warp 11 + MMA warp 10), each with half of the stages, take
   // alternate tiles and share the epilogue warps and the accumulator ring
-  static constexpr int kRings = (AMODE == 1 || AMODE == 2) ? 2 : 1;
+  static constexpr int kRings = (AMODE == 1 || AMODE == 2 || AMODE == 4) ? 2 : 1;
   static constexpr int kRingStages = STAGES / kRings;
   static constexpr int kTmaWarp2 = 11;
   static constexpr int kMmaIssuers = AMODE == 3 ? 4 : (kRings == 2 ? 2 : 1);
@@ -147,8 +160,10 @@ struct Cfg {
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kAOff = 0;
   // AMODE 3 keeps resident weights and the halo ring in one region at 0
-  static constexpr int kBOff = AMODE == 3 ? kHaloRegion : STAGES * kABytes;
-  static constexpr int kBarOff = kBOff + (AMODE == 3 ? 0 : STAGES * kBBytes);
+  // AMODE 4 puts the weight stages at 0 and the halo buffers after them
+  static constexpr int kBOff = AMODE == 3 ? kHaloRegion : (AMODE == 4 ? 0 : STAGES * kABytes);
+  static constexpr int kBarOff =
+      AMODE == 3 ? kHaloRegion : (AMODE == 4 ? kHalo4Region : kBOff + STAGES * kBBytes);
   // TMEM accumulator ring: all 512 columns (one CTA per SM), at most 8 tiles,
   // so the MMA runs several tiles ahead of the epilogue and the handoff
   // latency of one accumulator (commit -> TMEM load -> release) stays hidden
@@ -157,7 +172,8 @@ struct Cfg {
   static constexpr int kNumBars = 2 * STAGES + 2 * kAccBufs + 1 + 2 * kHaloSlotsMax;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
-  static constexpr int kTableOff = kBiasOff + (AMODE == 3 ? kHaloBiasMax : kBiasMax) * 4;
+  static constexpr int kTableOff =
+      kBiasOff + (AMODE == 3 ? kHaloBiasMax : (AMODE == 4 ? kHalo4BiasMax : kBiasMax)) * 4;
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
   static constexpr uint32_t kTmemCols = kAccBufs * BN;
 };
@@ -407,7 +423,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const int ab = lt % C::kAccBufs;
       int em = m0 + erow;
       bool rvalid = em < p.M;
-      if (AMODE == 3) {
+      if (AMODE == 3 || AMODE == 4) {
         // position q of the padded-width grid -> output pixel
         const int mt = t / p.n_tiles;
         const int img = mt / p.tpi;
@@ -472,7 +488,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       // the producer (a parity wait would then match the previous phase), so
       // AMODE 3 uses at most as many issuers as halo buffers; the others idle.
       const int n_iss = AMODE == 3 ? (p.halo_slots < C::kMmaIssuers ? p.halo_slots : C::kMmaIssuers) : C::kMmaIssuers;
-      uint32_t it = 0;
+      uint32_t it = 0, hc = 0;
       int lt = 0;
       bool ok = true;
       // AMODE 3: the resident weights land once, on full[0]
@@ -518,6 +534,42 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             }
           }
           umma_commit(&hempty[hs]);
+          umma_commit(&tfull[ab]);
+          continue;
+        }
+        if (AMODE == 4) {
+          const int q0 = ((t / p.n_tiles) % p.tpi) * kBlockM;
+          const uint32_t row0 = static_cast<uint32_t>(q0 % p.Wp) * 8;  // 128-byte rows in 16-byte units
+          const int taps = p.kh * p.kw;
+          for (int cc = 0; cc < p.cchunks && ok; ++cc, ++hc) {
+            const int hs = issuer * kHalo4Slots + static_cast<int>(hc % kHalo4Slots);
+            if (!mbar_wait_relaxed(&hfull[hs], (hc / kHalo4Slots) & 1, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            const uint64_t a_base = make_sdesc_sw128(smem_u32(sA) + p.halo_off + hs * p.halo_stride) + row0;
+            int r = 0, sx = 0;
+            for (int tap = 0; tap < taps; ++tap, ++it) {
+              const int st = issuer * C::kRingStages + static_cast<int>(it % C::kRingStages);
+              if (!mbar_wait_relaxed(&full[st], (it / C::kRingStages) & 1, kErrWaitFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t a_desc = a_base + static_cast<uint32_t>(r * p.Wp + sx) * 8u;
+              const uint64_t b_desc = make_sdesc_sw128(smem_u32(sB + st * C::kBBytes));
+#pragma unroll
+              for (int k = 0; k < kBlockK / 16; ++k)
+                umma_f16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (cc | tap | k) != 0 ? 1u : 0u);
+              umma_commit(&empty[st]);
+              if (++sx == p.kw) {
+                sx = 0;
+                ++r;
+              }
+            }
+            if (ok) umma_commit(&hempty[hs]);
+          }
+          if (!ok) break;
           umma_commit(&tfull[ab]);
           continue;
         }
@@ -575,8 +627,57 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         for (int j = lt - 1; j >= 0 && j >= lt - p.halo_slots; --j)
           mbar_wait(&hfull[j % p.halo_slots], (j / p.halo_slots) & 1, kErrWaitFull);
       }
+      if (AMODE == 4) {
+        // halo chunk h of this pipeline: tile lt = ring + 2 * (h / cchunks), chunk h % cchunks
+        const int gx = static_cast<int>(gridDim.x), bx = static_cast<int>(blockIdx.x);
+        const int my_tiles = p.tiles > bx ? (p.tiles - 1 - bx) / gx + 1 : 0;
+        const int ring_tiles = my_tiles > ring ? (my_tiles - 1 - ring) / 2 + 1 : 0;
+        const uint32_t n_h = static_cast<uint32_t>(ring_tiles) * p.cchunks;
+        uint32_t h_issued = 0;
+        auto issue_halo = [&](uint32_t h) -> bool {
+          const int t = bx + (ring + 2 * static_cast<int>(h / p.cchunks)) * gx;
+          const int cc = static_cast<int>(h % p.cchunks);
+          const int mt = t / p.n_tiles;
+          const int img = mt / p.tpi;
+          const int q0 = (mt - img * p.tpi) * kBlockM;
+          const int hs = ring * kHalo4Slots + static_cast<int>(h % kHalo4Slots);
+          if (*abort_flag || !mbar_wait(&hempty[hs], ((h / kHalo4Slots) & 1) ^ 1, kErrWaitEmpty)) return false;
+          mbar_arrive_expect_tx(&hfull[hs], static_cast<uint32_t>(p.halo_bytes));
+          tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], cc * kBlockK, -p.pw, q0 / p.Wp - p.ph,
+                      img);
+          ++h_issued;
+          return true;
+        };
+        uint32_t h = 0;
+        if (n_h > 0) ok = issue_halo(0);
+        const int taps = p.kh * p.kw;
+        for (int lt = ring; lt < my_tiles && ok; lt += 2) {
+          const int t = bx + lt * gx;
+          const int n0 = (t % p.n_tiles) * BN;
+          for (int cc = 0; cc < p.cchunks && ok; ++cc, ++h) {
+            for (int tap = 0; tap < taps; ++tap, ++it) {
+              const int st = ring * C::kRingStages + static_cast<int>(it % C::kRingStages);
+              if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kRingStages) & 1) ^ 1, kErrWaitEmpty)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(C::kBBytes));
+              tma_load_2d(sB + st * C::kBBytes, &tmap_w, &full[st], tap * p.Cs_in + cc * kBlockK, n0);
+              // the next chunk's halo goes out after this chunk's first weight
+              // block, a whole chunk ahead of its first MMA
+              if (tap == 0 && h + 1 < n_h && !issue_halo(h + 1)) {
+                ok = false;
+                break;
+              }
+            }
+          }
+        }
+        // the last halo loads of this pipeline have landed before the CTA may exit
+        for (int j = static_cast<int>(h_issued) - 1; j >= 0 && j >= static_cast<int>(h_issued) - kHalo4Slots; --j)
+          mbar_wait(&hfull[ring * kHalo4Slots + j % kHalo4Slots], (j / kHalo4Slots) & 1, kErrWaitFull);
+      }
       int plt = 0;
-      for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3; t += gridDim.x, ++plt) {
+      for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3 && AMODE != 4; t += gridDim.x, ++plt) {
         if (C::kRings == 2 && (plt & 1) != ring) continue;
         const int m0 = (t / p.n_tiles) * kBlockM;
         const int n0 = (t % p.n_tiles) * BN;
@@ -615,7 +716,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
       }
       if (!ok) *abort_flag = 1;
-      if (AMODE == 1 || AMODE == 2) {
+      if (AMODE == 1 || AMODE == 2 || AMODE == 4) {
         // every TMA load this thread issued has landed before the CTA may exit
         // (the last kRingStages stages; earlier ones were waited for through
         // their empty barriers)
@@ -762,22 +863,23 @@ static int make_tmap_im2col(CUtensorMap* map, const ConvTcArgs& a, int n_img) {
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-// Halo map over the NHWC activation [N, H, W, Cs]: box of Cs channels x Wp
-// pixels x R rows of one image, swizzled at the row width (Cs * 2 bytes); the
-// kernel starts each box at pixel -pw so that its rows are whole zero-padded
-// input rows.
+// Halo map over the NHWC activation [N, H, W, Cs]: box of min(Cs, 64)
+// channels x Wp pixels x R rows of one image, swizzled at the box row width;
+// the kernel starts each box at pixel -pw so that its rows are whole
+// zero-padded input rows (and at channel 64*chunk in AMODE 4).
 static int make_tmap_halo(CUtensorMap* map, const ConvTcArgs& a, int n_img, int wp, int rows) {
+  const int box_c = a.Cs_in < kBlockK ? a.Cs_in : kBlockK;
   auto enc = encode_tiled();
   if (!enc) return -1;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Cs_in), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
                         static_cast<cuuint64_t>(n_img)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.Cs_in) * 2, static_cast<cuuint64_t>(a.W) * a.Cs_in * 2,
                            static_cast<cuuint64_t>(a.H) * a.W * a.Cs_in * 2};
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(a.Cs_in), static_cast<cuuint32_t>(wp), static_cast<cuuint32_t>(rows), 1};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(box_c), static_cast<cuuint32_t>(wp), static_cast<cuuint32_t>(rows), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUtensorMapSwizzle sw = a.Cs_in == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
-                                : a.Cs_in == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                : CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMapSwizzle sw = box_c == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                : box_c == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -814,6 +916,38 @@ static double halo_plan(const ConvTcArgs& a, int bn, ConvTcParams* p) {
   p->halo_bytes = halo_bytes;
   p->a_rowbytes = rb;
   p->a_layout = rb == 32 ? 6 : (rb == 64 ? 4 : 2);
+  return static_cast<double>(a.OH) * a.OW / (static_cast<double>(tpi) * kBlockM);
+}
+
+// Streamed-weight halo plan (AMODE 4) at block width `bn` with `stages`
+// weight stages (split over the two pipelines): fills the halo fields of `p`
+// and returns the fraction of computed positions that are real outputs, or 0
+// when the layer does not fit (stride 1, Cs_in a multiple of 64, weight
+// stages plus 2 x kHalo4Slots halo buffers within kHalo4Region).
+static double halo4_plan(const ConvTcArgs& a, int bn, int stages, ConvTcParams* p) {
+  const int wp = a.W + 2 * a.pw;
+  if (a.sh != 1 || a.sw != 1 || a.out_kind == 2 || a.Cs_in % kBlockK != 0) return 0.0;
+  if (wp > 256 || a.OW != wp - a.kw + 1 || a.k_pad != a.kh * a.kw * a.Cs_in) return 0.0;
+  const long q = static_cast<long>(a.OH) * wp;
+  const int tpi = static_cast<int>((q + kBlockM - 1) / kBlockM);
+  int max_off = 0;
+  for (int j = 0; j < tpi; ++j) max_off = std::max(max_off, (j * kBlockM) % wp);
+  const int rows = (max_off + (a.kh - 1) * wp + (a.kw - 1) + kBlockM - 1) / wp + 1;
+  if (rows > 256) return 0.0;
+  const int halo_bytes = kBlockK * 2 * wp * rows;
+  const int stride = (halo_bytes + 1023) & ~1023;
+  const int w_bytes = stages * bn * kBlockK * 2;
+  if (w_bytes + 2 * kHalo4Slots * stride > kHalo4Region) return 0.0;
+  if ((a.out_kind == 2 ? a.t_cout : ((a.n_cols + bn - 1) / bn) * bn) > kHalo4BiasMax) return 0.0;
+  p->Wp = wp;
+  p->tpi = tpi;
+  p->halo_off = w_bytes;
+  p->halo_stride = stride;
+  p->halo_slots = kHalo4Slots;
+  p->halo_bytes = halo_bytes;
+  p->a_rowbytes = kBlockK * 2;
+  p->a_layout = 2;
+  p->cchunks = a.Cs_in / kBlockK;
   return static_cast<double>(a.OH) * a.OW / (static_cast<double>(tpi) * kBlockM);
 }
 
@@ -911,9 +1045,15 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   // real outputs (the padding columns and each image's last tile are waste)
   if (!plain_gemm && halo_plan(a, bn, &p) >= 0.70) amode = 3;
   const char* force = std::getenv("LOTUS_CONV_AMODE");
+  // AMODE 4 only on request: with three weight stages per pipeline the
+  // streamed weights, not the A bytes, bound these layers, and im2col is as
+  // fast or faster on ResNet stages 2-3
+  if (force && std::atoi(force) == 4 && amode == 1 && halo4_plan(a, bn, bn == 64 ? 8 : 6, &p) >= 0.70) amode = 4;
   if (force && std::atoi(force) == 0) amode = 0;
-  if (force && std::atoi(force) == 1 && amode == 3) amode = a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10) ? 1 : 0;
+  if (force && std::atoi(force) == 1 && (amode == 3 || amode == 4))
+    amode = a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10) ? 1 : 0;
   if (amode == 3) p.tiles = static_cast<int>(static_cast<long>(n_img) * p.tpi);
+  if (amode == 4) p.tiles = static_cast<int>(static_cast<long>(n_img) * p.tpi * p.n_tiles);
   if (amode == 0 && p.KB * 8 > kMaxTable) {
     *err = "conv: K too large for the gather path";
     return -2;
@@ -929,7 +1069,7 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     *err = "conv: im2col tensor map encoding failed";
     return -3;
   }
-  if (amode == 3 && make_tmap_halo(&ma, a, n_img, p.Wp, p.halo_bytes / (p.a_rowbytes * p.Wp)) != 0) {
+  if ((amode == 3 || amode == 4) && make_tmap_halo(&ma, a, n_img, p.Wp, p.halo_bytes / (p.a_rowbytes * p.Wp)) != 0) {
     *err = "conv: halo tensor map encoding failed";
     return -3;
   }
@@ -944,6 +1084,7 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
       case 0: e = launch_impl<64, 8, 0>(mw, ma, p, stream); break;
       case 1: e = launch_impl<64, 8, 1>(mw, ma, p, stream); break;
       case 2: e = launch_impl<64, 8, 2>(mw, ma, p, stream); break;
+      case 4: e = launch_impl<64, 8, 4>(mw, ma, p, stream); break;
       default: e = launch_impl<64, 2, 3>(mw, ma, p, stream); break;
     }
   } else {
@@ -951,6 +1092,7 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
       case 0: e = launch_impl<128, 6, 0>(mw, ma, p, stream); break;
       case 1: e = launch_impl<128, 6, 1>(mw, ma, p, stream); break;
       case 2: e = launch_impl<128, 6, 2>(mw, ma, p, stream); break;
+      case 4: e = launch_impl<128, 6, 4>(mw, ma, p, stream); break;
       default: e = launch_impl<128, 2, 3>(mw, ma, p, stream); break;
     }
   }

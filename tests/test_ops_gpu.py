@@ -64,6 +64,10 @@ CONV_CASES = [
     ("halo_stage1_residual", 4, 64, 56, 56, 64, 3, 1, 1, 1, True),
     ("halo_cin32_cout128_sigmoid", 1, 32, 33, 31, 128, 3, 1, 1, 2, False),
     ("halo_pad0_nonsquare", 2, 64, 34, 30, 64, 3, 1, 0, 1, False),
+    # 64-channel multiples whose weights stream: one halo box per channel chunk
+    ("halo4_stage2_residual", 4, 128, 28, 28, 128, 3, 1, 1, 1, True),
+    ("halo4_stage3_two_ntiles", 4, 256, 14, 14, 256, 3, 1, 1, 0, False),
+    ("halo4_cin192_cout96_sigmoid", 2, 192, 20, 20, 96, 3, 1, 1, 2, False),
 ]
 
 
@@ -97,13 +101,15 @@ def test_conv2d_parity(case):
     _no_device_error()
 
 
-@pytest.mark.parametrize("amode", ["0", "1"])
+@pytest.mark.parametrize("amode", ["0", "1", "4"])
 @pytest.mark.parametrize("case", [c for c in CONV_CASES if c[0] in (
-    "cfg1_64x56x56_3x3_relu", "halo_stage1_residual", "unet_32to64", "halo_s2d_stem_like_cin12_4x4")],
+    "cfg1_64x56x56_3x3_relu", "halo_stage1_residual", "unet_32to64", "halo_s2d_stem_like_cin12_4x4",
+    "halo4_stage2_residual", "halo4_stage3_two_ntiles", "halo4_cin192_cout96_sigmoid")],
     ids=lambda c: c[0])
 def test_conv2d_forced_paths(case, amode, monkeypatch):
-    """The cp.async gather (0) and im2col TMA (1) paths on layers that
-    default to the halo path give the same results."""
+    """Every A-staging path a layer can take gives the oracle's result: the
+    cp.async gather (0), im2col TMA (1) and, for 64-channel multiples, the
+    streamed-weight halo (4) next to the default choice."""
     monkeypatch.setenv("LOTUS_CONV_AMODE", amode)
     test_conv2d_parity(case)
 
@@ -114,6 +120,8 @@ def test_conv2d_forced_paths(case, amode, monkeypatch):
     ("stem_s2d_like_n64", 64, 12, 115, 115, 64, 4, 0, False),
     ("stage1_residual_n256", 256, 64, 56, 56, 64, 3, 1, True),
     ("cin32_n128", 128, 32, 40, 40, 64, 3, 1, False),
+    ("stage2_residual_n256", 256, 128, 28, 28, 128, 3, 1, True),
+    ("stage3_n256", 256, 256, 14, 14, 256, 3, 1, False),
 ], ids=lambda c: c[0])
 def test_conv2d_halo_many_tiles_per_cta(case, monkeypatch):
     """Full-size halo launches against the im2col / gather paths on the same
@@ -133,6 +141,10 @@ def test_conv2d_halo_many_tiles_per_cta(case, monkeypatch):
     monkeypatch.setenv("LOTUS_CONV_AMODE", "1" if c % 64 == 0 else "0")
     y_ref = K.conv2d(x, c, wp, b, cout, k, 1, p, 1, residual=res)
     assert_close(K.from_nhwc(y_halo, cout).cpu().numpy(), K.from_nhwc(y_ref, cout).cpu().numpy(), what=case[0])
+    if c % 64 == 0 and c > 64:
+        monkeypatch.setenv("LOTUS_CONV_AMODE", "4")
+        y4 = K.conv2d(x, c, wp, b, cout, k, 1, p, 1, residual=res)
+        assert_close(K.from_nhwc(y4, cout).cpu().numpy(), K.from_nhwc(y_ref, cout).cpu().numpy(), what=case[0] + "/4")
     _no_device_error()
 
 
