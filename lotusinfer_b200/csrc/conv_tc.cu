@@ -416,13 +416,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     const int erow = q * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
     const bool has_res = p.residual != nullptr && p.out_kind == 0;
-    int lt = 0;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
-      const int m0 = (t / p.n_tiles) * kBlockM;
-      const int n0 = (t % p.n_tiles) * BN;
-      const int ab = lt % C::kAccBufs;
-      int em = m0 + erow;
-      bool rvalid = em < p.M;
+    // output row of this thread in tile t (em) and whether it is a real pixel
+    auto row_of = [&](int t, int& em, bool& rvalid) {
+      em = (t / p.n_tiles) * kBlockM + erow;
+      rvalid = em < p.M;
       if (AMODE == 3 || AMODE == 4) {
         // position q of the padded-width grid -> output pixel
         const int mt = t / p.n_tiles;
@@ -433,15 +430,41 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         rvalid = oy < p.OH && ox < p.OW;
         em = (img * p.OH + oy) * p.OW + ox;
       }
-      const bool tile_full = n0 + BN <= p.Cout;
-      // residual rows do not depend on the accumulator: fetch them first
-      uint4 res[kResVecs];
-      if (has_res && rvalid) {
-        const uint4* rrow = reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out + n0 + hcol);
+    };
+    // residual rows do not depend on the accumulator.  At BN=64 (epilogue-
+    // bound layers) the rows of the next tile are loaded while this tile is
+    // processed: a load issued only just before this tile's accumulator wait
+    // exposes the full DRAM latency whenever the MMAs are ahead.  At BN=128
+    // the second register set would spill, and the rows of the tile itself
+    // are loaded ahead of its accumulator wait.
+    constexpr bool kPipeRes = BN == 64;
+    auto load_res = [&](int t, uint4 (&r)[kResVecs]) {
+      int em_t;
+      bool ok_t;
+      row_of(t, em_t, ok_t);
+      const int n0_t = (t % p.n_tiles) * BN;
+      if (has_res && ok_t && t < p.tiles) {
+        const uint4* rrow =
+            reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em_t) * p.Cs_out + n0_t + hcol);
 #pragma unroll
         for (int i = 0; i < kResVecs; ++i)
-          res[i] = (n0 + hcol + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
+          r[i] = (n0_t + hcol + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
       }
+    };
+    uint4 res[kResVecs], res_next[kPipeRes ? kResVecs : 1];
+    if (kPipeRes) load_res(blockIdx.x, res);
+    int lt = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
+      const int n0 = (t % p.n_tiles) * BN;
+      const int ab = lt % C::kAccBufs;
+      int em;
+      bool rvalid;
+      row_of(t, em, rvalid);
+      const bool tile_full = n0 + BN <= p.Cout;
+      if (kPipeRes)
+        load_res(t + static_cast<int>(gridDim.x), reinterpret_cast<uint4(&)[kResVecs]>(res_next));
+      else
+        load_res(t, res);
       int sc_n = 0, sc_iy = 0, sc_ix = 0;
       if (p.out_kind == 2 && rvalid) {
         sc_n = em / ohw;
@@ -477,6 +500,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           else
             epi_chunk_act<2>(p, v[cc], em, n0, cl, sb, tile_full, rp, sc_n, sc_iy, sc_ix);
         }
+      }
+      if (kPipeRes) {
+#pragma unroll
+        for (int i = 0; i < kResVecs; ++i) res[i] = res_next[kPipeRes ? i : 0];
       }
     }
   } else if (C::issuer_of(warp) >= 0) {
