@@ -145,11 +145,13 @@ struct Cfg {
   // AMODE 1/2: two independent pipelines (producer warp 9 + MMA warp 8 and
   // producer warp 11 + MMA warp 10), each with half of the stages, take
   // alternate tiles and share the epilogue warps and the accumulator ring
-  static constexpr int kRings = (AMODE == 1 || AMODE == 2 || AMODE == 4) ? 2 : 1;
+  // (BN=256 tiles fill all of TMEM with two accumulators: one pipeline; an
+  // N=256 MMA keeps the tensor pipe busier than one thread's issue cost)
+  static constexpr int kRings = ((AMODE == 1 || AMODE == 2 || AMODE == 4) && BN <= 128) ? 2 : 1;
   static constexpr int kRingStages = STAGES / kRings;
   static constexpr int kTmaWarp2 = 11;
   static constexpr int kMmaIssuers = AMODE == 3 ? 4 : (kRings == 2 ? 2 : 1);
-  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 416 : 384);
+  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 416 : (kRings == 2 ? 384 : 320));
   // issuer index of a warp (-1: not an issuer): warp 8 is issuer 0, warps
   // 10.. the others
   static __device__ __forceinline__ int issuer_of(int warp) {
@@ -438,6 +440,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // the second register set would spill, and the rows of the tile itself
     // are loaded ahead of its accumulator wait.
     constexpr bool kPipeRes = BN == 64;
+    constexpr bool kChunked = BN > 128;
     auto load_res = [&](int t, uint4 (&r)[kResVecs]) {
       int em_t;
       bool ok_t;
@@ -463,7 +466,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const bool tile_full = n0 + BN <= p.Cout;
       if (kPipeRes)
         load_res(t + static_cast<int>(gridDim.x), reinterpret_cast<uint4(&)[kResVecs]>(res_next));
-      else
+      else if (!kChunked)
         load_res(t, res);
       int sc_n = 0, sc_iy = 0, sc_ix = 0;
       if (p.out_kind == 2 && rvalid) {
@@ -475,6 +478,40 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAccBufs) & 1, kErrWaitAccum);
       if (!ok) *abort_flag = 1;
       tc_fence_after();
+      if (kChunked) {
+        // BN=256: 128 columns per warp, drained and stored 32 at a time (the
+        // whole half would not fit in registers); the accumulator goes back
+        // after the last chunk's load, its residual is read per chunk
+        const float* sb = s_bias + n0;
+#pragma unroll 1
+        for (int cc = 0; cc < kHalf / 32; ++cc) {
+          uint32_t vc[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tmem_base + t_lane + ab * BN + hcol + cc * 32, vc);  // warp-collective
+          tmem_ld_wait();
+          if (cc == kHalf / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[ab]);
+          }
+          const int cl = hcol + cc * 32;
+          uint4 rc[4];
+          if (has_res && rvalid) {
+            const uint4* rrow =
+                reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out + n0 + cl);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              rc[i] = (n0 + cl + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
+          }
+          if (ok && rvalid) {
+            if (p.out_kind == 0)
+              epi_chunk_act<0>(p, vc, em, n0, cl, sb, tile_full, has_res ? rc : nullptr, 0, 0, 0);
+            else
+              epi_chunk_act<1>(p, vc, em, n0, cl, sb, tile_full, nullptr, 0, 0, 0);
+          }
+        }
+        continue;
+      }
       // drain this warp's share of the accumulator into registers, then hand
       // the TMEM buffer back to the MMA warp before the math and the stores
       uint32_t v[kHalf / 32][32];
@@ -1046,7 +1083,16 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     const char* env = std::getenv("LOTUS_CONV_BN");
     bn = env ? std::atoi(env) : 0;
   }
-  if (bn != 64 && bn != 128) bn = a.n_cols <= 64 ? 64 : 128;
+  const bool plain_gemm = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
+  const int n_img = a.M / (a.OH * a.OW);
+  const size_t x_bytes = static_cast<size_t>(n_img) * a.H * a.W * a.Cs_in * 2;
+  // the im2col TMA path (below) takes 64-channel-aligned inputs of >= 128 KB
+  const bool im2col_ok = !plain_gemm && a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10);
+  const char* force = std::getenv("LOTUS_CONV_AMODE");
+  const int forced = force ? std::atoi(force) : -1;
+  if (bn != 64 && bn != 128 && bn != 256) bn = a.n_cols <= 64 ? 64 : (a.n_cols >= 256 && im2col_ok ? 256 : 128);
+  // BN=256 exists for the im2col path only
+  if (bn == 256 && (!im2col_ok || a.out_kind == 2 || (forced >= 0 && forced != 1))) bn = 128;
   p.n_tiles = (a.n_cols + bn - 1) / bn;
   const long m_tiles = (static_cast<long>(a.M) + kBlockM - 1) / kBlockM;
   if (m_tiles * p.n_tiles > 0x7FFFFFFFL) {
@@ -1060,22 +1106,19 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   // inputs, otherwise the cp.async gather.  Small inputs (< 128 KB) stay on
   // the gather path: the im2col map is only used on activation tensors at
   // least that large.
-  const bool plain_gemm = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
-  const int n_img = a.M / (a.OH * a.OW);
-  const size_t x_bytes = static_cast<size_t>(n_img) * a.H * a.W * a.Cs_in * 2;
   int amode = 0;
   if (plain_gemm)
     amode = 2;
-  else if (a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10))
+  else if (im2col_ok)
     amode = 1;
   // resident-weight halo mode where at least 70% of the computed positions are
   // real outputs (the padding columns and each image's last tile are waste)
-  if (!plain_gemm && halo_plan(a, bn, &p) >= 0.70) amode = 3;
-  const char* force = std::getenv("LOTUS_CONV_AMODE");
+  if (!plain_gemm && bn <= 128 && halo_plan(a, bn, &p) >= 0.70) amode = 3;
   // AMODE 4 only on request: with three weight stages per pipeline the
   // streamed weights, not the A bytes, bound these layers, and im2col is as
   // fast or faster on ResNet stages 2-3
-  if (force && std::atoi(force) == 4 && amode == 1 && halo4_plan(a, bn, bn == 64 ? 8 : 6, &p) >= 0.70) amode = 4;
+  if (force && std::atoi(force) == 4 && amode == 1 && bn <= 128 && halo4_plan(a, bn, bn == 64 ? 8 : 6, &p) >= 0.70)
+    amode = 4;
   if (force && std::atoi(force) == 0) amode = 0;
   if (force && std::atoi(force) == 1 && (amode == 3 || amode == 4))
     amode = a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10) ? 1 : 0;
@@ -1106,7 +1149,9 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   }
 
   cudaError_t e = cudaErrorInvalidValue;
-  if (bn == 64) {
+  if (bn == 256) {
+    e = launch_impl<256, 4, 1>(mw, ma, p, stream);  // amode == 1 (see the BN choice above)
+  } else if (bn == 64) {
     switch (amode) {
       case 0: e = launch_impl<64, 8, 0>(mw, ma, p, stream); break;
       case 1: e = launch_impl<64, 8, 1>(mw, ma, p, stream); break;

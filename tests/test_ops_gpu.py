@@ -68,6 +68,11 @@ CONV_CASES = [
     ("halo4_stage2_residual", 4, 128, 28, 28, 128, 3, 1, 1, 1, True),
     ("halo4_stage3_two_ntiles", 4, 256, 14, 14, 256, 3, 1, 1, 0, False),
     ("halo4_cin192_cout96_sigmoid", 2, 192, 20, 20, 96, 3, 1, 1, 2, False),
+    # Cout >= 256 on the im2col path: 256-column tiles
+    ("bn256_stage3_residual", 4, 256, 14, 14, 256, 3, 1, 1, 1, True),
+    ("bn256_stage4_cout512_residual", 8, 512, 7, 7, 512, 3, 1, 1, 1, True),
+    ("bn256_1x1s2_cout384_partial", 4, 128, 28, 28, 384, 1, 2, 0, 0, False),
+    ("bn256_3x3s2_sigmoid", 4, 128, 28, 28, 256, 3, 2, 1, 2, False),
 ]
 
 
