@@ -84,8 +84,9 @@ using namespace lotus_dev;
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;                     // fp16 elements = one 128-byte swizzle row
 constexpr int kABytes = kBlockM * kBlockK * 2;  // 16 KB per stage
-constexpr int kMaxTable = 4096;                 // gather-table entries (8-channel chunks)
-constexpr int kBiasMax = 4096;                  // bias entries staged in shared memory
+constexpr int kMaxTable = 2048;                 // gather-table entries (8-channel chunks): K <= 16384
+constexpr int kBiasMax = 1024;                  // bias entries staged in shared memory
+constexpr int kStageBytes = 32 * 64;            // per epilogue warp: 32 rows x 64 bytes of fp16 output
 
 struct ConvTcParams {
   const __half* x;
@@ -121,10 +122,10 @@ struct ConvTcParams {
 constexpr int kHaloSlotsMax = 8;
 // weights + halo ring (AMODE 3): what remains of the 227 KB of shared memory
 // after the barriers, a 1 KB bias area and the 1 KB alignment slack
-constexpr int kHaloRegion = 224 * 1024;
+constexpr int kHaloRegion = 208 * 1024;
 constexpr int kHaloBiasMax = 256;  // AMODE 3 has one N tile of at most 128 columns
 // AMODE 4: weight stages + 2 x kHalo4Slots halo buffers, bias of up to 512 columns
-constexpr int kHalo4Region = 220 * 1024;
+constexpr int kHalo4Region = 204 * 1024;
 constexpr int kHalo4BiasMax = 512;
 constexpr int kHalo4Slots = 2;  // halo buffers per pipeline
 
@@ -174,8 +175,10 @@ struct Cfg {
   static constexpr int kNumBars = 2 * STAGES + 2 * kAccBufs + 1 + 2 * kHaloSlotsMax;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
-  static constexpr int kTableOff =
+  // per-warp output staging (NHWC fp16 stores), then the gather table
+  static constexpr int kStageOff =
       kBiasOff + (AMODE == 3 ? kHaloBiasMax : (AMODE == 4 ? kHalo4BiasMax : kBiasMax)) * 4;
+  static constexpr int kTableOff = kStageOff + kEpiWarps * kStageBytes;
   static constexpr int bytes(int table_entries) { return kTableOff + table_entries * 4 + 1024; }
   static constexpr uint32_t kTmemCols = kAccBufs * BN;
 };
@@ -211,6 +214,80 @@ __device__ __forceinline__ float bias_of(const ConvTcParams& p, const float* sb,
   const int col = p.out_kind == 2 ? c : n0 + c;
   const int lim = p.out_kind == 2 ? p.t_cout : p.Cout;
   return (p.bias != nullptr && col < lim) ? __ldg(p.bias + col) : 0.f;
+}
+
+// NHWC fp16 epilogue of one 32-column chunk, warp-cooperative: every lane
+// computes its row's 64 bytes (bias, residual, activation, pad channels zero),
+// parks them in the warp's 32 x 64-byte staging buffer (16-byte chunks XOR-
+// swizzled by row so that neither side has bank conflicts), and the warp then
+// stores 8 rows x 64 contiguous bytes per instruction.  Storing 16 bytes per
+// lane straight from the accumulator row would touch 32 partial sectors per
+// instruction.  All 32 lanes must call it; `valid` = the lane's row is an
+// output pixel (em is its row index).
+template <int ACT>
+__device__ __forceinline__ void epi_store_nhwc(const ConvTcParams& p, const uint32_t (&v)[32], int em, bool valid,
+                                               int n0, int cl, const float* sb, bool full, const uint4* res,
+                                               uint8_t* stg, int lane) {
+  uint4* st = reinterpret_cast<uint4*>(stg);  // [32 rows][4 chunks]
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int c = cl + g * 8;  // column inside the tile
+    float f[8];
+    if (p.bias_smem) {
+      const float4 b0 = *reinterpret_cast<const float4*>(sb + c);
+      const float4 b1 = *reinterpret_cast<const float4*>(sb + c + 4);
+      f[0] = b0.x; f[1] = b0.y; f[2] = b0.z; f[3] = b0.w;
+      f[4] = b1.x; f[5] = b1.y; f[6] = b1.z; f[7] = b1.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = bias_of(p, sb, n0, c + j);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] += __uint_as_float(v[g * 8 + j]);
+    if (res) {
+      const __half2* rh = reinterpret_cast<const __half2*>(&res[g]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 rf = __half22float2(rh[j]);
+        f[2 * j] += rf.x;
+        f[2 * j + 1] += rf.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = act_t<ACT>(f[j]);
+    if (!full) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + c + j >= p.Cout) f[j] = 0.f;  // pad channels stay zero
+    }
+    st[lane * 4 + ((g ^ (lane >> 1)) & 3)] = make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]),
+                                                        pack_half2(f[4], f[5]), pack_half2(f[6], f[7]));
+  }
+  __syncwarp();
+  const int row_em = valid ? em : -1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 8 * i + (lane >> 2);  // staged row this lane stores
+    const int c = lane & 3;             // and its 16-byte chunk
+    const int em_r = __shfl_sync(0xffffffffu, row_em, r);
+    const uint4 val = st[r * 4 + ((c ^ (r >> 1)) & 3)];
+    const int col = n0 + cl + c * 8;
+    if (em_r >= 0 && (full || col < p.Cs_out))
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em_r) * p.Cs_out + col) = val;
+  }
+  __syncwarp();  // the buffer is rewritten by the next chunk
+}
+
+template <int ACT_UNUSED = 0>
+__device__ __forceinline__ void epi_store_nhwc_act(const ConvTcParams& p, const uint32_t (&v)[32], int em, bool valid,
+                                                   int n0, int cl, const float* sb, bool full, const uint4* res,
+                                                   uint8_t* stg, int lane) {
+  if (p.act == 1)
+    epi_store_nhwc<1>(p, v, em, valid, n0, cl, sb, full, res, stg, lane);
+  else if (p.act == 0)
+    epi_store_nhwc<0>(p, v, em, valid, n0, cl, sb, full, res, stg, lane);
+  else
+    epi_store_nhwc<2>(p, v, em, valid, n0, cl, sb, full, res, stg, lane);
 }
 
 // Epilogue of one 32-column chunk of one accumulator row.  `cl` is the
@@ -346,6 +423,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   float* s_bias = reinterpret_cast<float*>(smem + C::kBiasOff);
+  uint8_t* s_stage = smem + C::kStageOff + (threadIdx.x >> 5) * kStageBytes;  // epilogue warps only
   uint32_t* ktable = reinterpret_cast<uint32_t*>(smem + C::kTableOff);
 
   const int tid = threadIdx.x;
@@ -503,11 +581,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             for (int i = 0; i < 4; ++i)
               rc[i] = (n0 + cl + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
           }
-          if (ok && rvalid) {
-            if (p.out_kind == 0)
-              epi_chunk_act<0>(p, vc, em, n0, cl, sb, tile_full, has_res ? rc : nullptr, 0, 0, 0);
-            else
-              epi_chunk_act<1>(p, vc, em, n0, cl, sb, tile_full, nullptr, 0, 0, 0);
+          if (p.out_kind == 0) {
+            if (__all_sync(0xffffffffu, ok))
+              epi_store_nhwc_act(p, vc, em, rvalid, n0, cl, sb, tile_full, has_res ? rc : nullptr, s_stage, lane);
+          } else if (ok && rvalid) {
+            epi_chunk_act<1>(p, vc, em, n0, cl, sb, tile_full, nullptr, 0, 0, 0);
           }
         }
         continue;
@@ -524,7 +602,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);
-      if (ok && rvalid) {
+      // staged stores at BN >= 128 (measured: faster for ResNet stages 2-4,
+      // slower for the BN=64 halo layers, whose epilogue per tile is short)
+      if (BN >= 128 && p.out_kind == 0 && __all_sync(0xffffffffu, ok)) {
+        const float* sb = s_bias + n0;
+#pragma unroll
+        for (int cc = 0; cc < kHalf / 32; ++cc) {
+          const uint4* rp = has_res ? &res[cc * 4] : nullptr;
+          epi_store_nhwc_act(p, v[cc], em, rvalid, n0, hcol + cc * 32, sb, tile_full, rp, s_stage, lane);
+        }
+      } else if (ok && rvalid && (BN < 128 || p.out_kind != 0)) {
         const float* sb = p.out_kind == 2 ? s_bias : s_bias + n0;
 #pragma unroll
         for (int cc = 0; cc < kHalf / 32; ++cc) {
