@@ -83,6 +83,20 @@ int lotus_conv2d_prepack(const float* w_oihw, void* w_packed, const lotus_conv2d
 int lotus_conv2d_fwd(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                      const lotus_conv2d_desc* d, cudaStream_t stream);
 
+/* Split-K form of lotus_conv2d_fwd for launches with too few output tiles to
+ * fill the GPU (small batches, late layers): the K loop is split over CTAs
+ * that write fp32 partial tiles into `workspace`, and a second kernel sums
+ * them (in split order, deterministically) and applies bias, residual and
+ * activation.  lotus_conv2d_workspace_bytes(d) is the workspace size the
+ * split for this shape wants (0 = it does not split); with a smaller or null
+ * workspace the call runs unsplit, exactly like lotus_conv2d_fwd.  The
+ * workspace is caller-owned device memory, 16-byte aligned; it is scratch
+ * between the two kernels of one call, so calls sharing it must not overlap
+ * on the GPU.  The same reference kernels as lotus_conv2d_fwd. */
+size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d);
+int lotus_conv2d_fwd_ws(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                        const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* Transposed convolution (PyTorch ConvTranspose2d semantics, dilation 1).
  * Replaces lotus::TransConv2d (reference source/operator/transposed_conv2d.cu:17-140,
  * launched from source/layer/layer_transposed_conv2d.cu:37-72). */
@@ -117,6 +131,12 @@ int lotus_linear_prepack(const float* w, void* w_packed, int in_features, int ou
                          int fc_w, cudaStream_t stream);
 int lotus_linear_fwd(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
                      int out_features, int act, int out_kind, cudaStream_t stream);
+/* Split-K form of lotus_linear_fwd (GEMM path, m > 8), same contract as
+ * lotus_conv2d_fwd_ws. */
+size_t lotus_linear_workspace_bytes(int m, int in_features, int out_features);
+int lotus_linear_fwd_ws(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
+                        int out_features, int act, int out_kind, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
 /* Forced variants for per-operator tests and benches. */
 int lotus_gemm_bias_fwd(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
                         int out_features, int act, int out_kind, cudaStream_t stream);

@@ -112,18 +112,9 @@ int lotus_conv2d_prepack(const float* w_oihw, void* w_packed, const lotus_conv2d
                      "conv2d_prepack");
 }
 
-int lotus_conv2d_fwd(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
-                     const lotus_conv2d_desc* d, cudaStream_t stream) {
-  int oh, ow;
-  const int st = check_conv_desc(d, &oh, &ow);
-  if (st != LOTUS_OK) return st;
-  if (!x || !w_packed || !y) return fail(LOTUS_ERR_INVALID, "conv2d: null x, w or y");
-  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y) || (residual && !aligned16(residual)))
-    return fail(LOTUS_ERR_INVALID, "conv2d: x, w, y and residual must be 16-byte aligned");
-  if (residual && d->out_kind != LOTUS_OUT_NHWC_F16)
-    return fail(LOTUS_ERR_INVALID, "conv2d: residual needs the NHWC fp16 output");
-  if (d->out_kind == LOTUS_OUT_ROWS_F32 && (reinterpret_cast<uintptr_t>(y) & 3u))
-    return fail(LOTUS_ERR_INVALID, "conv2d: fp32 output must be 4-byte aligned");
+// Kernel arguments of a conv described by `d` (shape already checked).
+static ConvTcArgs conv_args(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                            const lotus_conv2d_desc* d, int oh, int ow) {
   ConvTcArgs a{};
   a.x = x;
   a.w_packed = w_packed;
@@ -147,10 +138,52 @@ int lotus_conv2d_fwd(const void* x, const void* w_packed, const float* bias, con
   a.M = d->n * oh * ow;
   a.act = d->act;
   a.out_kind = d->out_kind;
+  return a;
+}
+
+static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                         const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int oh, ow;
+  const int st = check_conv_desc(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  if (!x || !w_packed || !y) return fail(LOTUS_ERR_INVALID, "conv2d: null x, w or y");
+  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y) || (residual && !aligned16(residual)))
+    return fail(LOTUS_ERR_INVALID, "conv2d: x, w, y and residual must be 16-byte aligned");
+  if (residual && d->out_kind != LOTUS_OUT_NHWC_F16)
+    return fail(LOTUS_ERR_INVALID, "conv2d: residual needs the NHWC fp16 output");
+  if (d->out_kind == LOTUS_OUT_ROWS_F32 && (reinterpret_cast<uintptr_t>(y) & 3u))
+    return fail(LOTUS_ERR_INVALID, "conv2d: fp32 output must be 4-byte aligned");
+  if (workspace && !aligned16(workspace)) return fail(LOTUS_ERR_INVALID, "conv2d: workspace must be 16-byte aligned");
+  ConvTcArgs a = conv_args(x, w_packed, bias, residual, y, d, oh, ow);
+  a.ws = static_cast<float*>(workspace);
+  a.ws_bytes = workspace ? workspace_bytes : 0;
   const char* err = "";
   const int r = conv_tc_launch(a, stream, &err);
   if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
   return ok();
+}
+
+int lotus_conv2d_fwd(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                     const lotus_conv2d_desc* d, cudaStream_t stream) {
+  return conv_fwd_impl(x, w_packed, bias, residual, y, d, nullptr, 0, stream);
+}
+
+int lotus_conv2d_fwd_ws(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                        const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return conv_fwd_impl(x, w_packed, bias, residual, y, d, workspace, workspace_bytes, stream);
+}
+
+size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d) {
+  int oh, ow;
+  if (check_conv_desc(d, &oh, &ow) != LOTUS_OK) return 0;
+  // placeholder non-null, 16-aligned pointers: planning reads no memory
+  void* fake = reinterpret_cast<void*>(static_cast<uintptr_t>(256));
+  ConvTcArgs a = conv_args(fake, fake, nullptr, nullptr, fake, d, oh, ow);
+  size_t need = 0;
+  const char* err = "";
+  if (conv_tc_launch(a, nullptr, &err, &need) != 0) return 0;
+  ok();
+  return need;
 }
 
 // ------------------------------------------------------------------ tconv
@@ -287,10 +320,9 @@ static int check_linear(const void* x, const void* w, void* y, int m, int in_f, 
   return ok();
 }
 
-int lotus_gemm_bias_fwd(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
-                        int out_features, int act, int out_kind, cudaStream_t stream) {
-  const int st = check_linear(x, w_packed, y, m, in_features, out_features, act, out_kind);
-  if (st != LOTUS_OK) return st;
+// GEMM kernel arguments of a Linear layer (M = batch rows).
+static ConvTcArgs gemm_args(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
+                            int out_features, int act, int out_kind) {
   ConvTcArgs a{};
   a.x = x;
   a.w_packed = w_packed;
@@ -309,18 +341,53 @@ int lotus_gemm_bias_fwd(const void* x, const void* w_packed, const float* bias, 
   a.M = m;
   a.act = act;
   a.out_kind = out_kind;
+  return a;
+}
+
+static int gemm_fwd_impl(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
+                         int out_features, int act, int out_kind, void* workspace, size_t workspace_bytes,
+                         cudaStream_t stream) {
+  const int st = check_linear(x, w_packed, y, m, in_features, out_features, act, out_kind);
+  if (st != LOTUS_OK) return st;
+  if (workspace && !aligned16(workspace)) return fail(LOTUS_ERR_INVALID, "gemm: workspace must be 16-byte aligned");
+  ConvTcArgs a = gemm_args(x, w_packed, bias, y, m, in_features, out_features, act, out_kind);
+  a.ws = static_cast<float*>(workspace);
+  a.ws_bytes = workspace ? workspace_bytes : 0;
   const char* err = "";
   const int r = conv_tc_launch(a, stream, &err);
   if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("gemm: ") + err);
   return ok();
 }
 
+int lotus_gemm_bias_fwd(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
+                        int out_features, int act, int out_kind, cudaStream_t stream) {
+  return gemm_fwd_impl(x, w_packed, bias, y, m, in_features, out_features, act, out_kind, nullptr, 0, stream);
+}
+
 int lotus_linear_fwd(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
                      int out_features, int act, int out_kind, cudaStream_t stream) {
+  return lotus_linear_fwd_ws(x, w_packed, bias, y, m, in_features, out_features, act, out_kind, nullptr, 0, stream);
+}
+
+size_t lotus_linear_workspace_bytes(int m, int in_features, int out_features) {
+  if (m <= 8 || in_features <= 0 || out_features <= 0) return 0;  // the GEMV path needs none
+  void* fake = reinterpret_cast<void*>(static_cast<uintptr_t>(256));
+  ConvTcArgs a = gemm_args(fake, fake, nullptr, fake, m, in_features, out_features, 0, LOTUS_OUT_ROWS_F32);
+  size_t need = 0;
+  const char* err = "";
+  if (conv_tc_launch(a, nullptr, &err, &need) != 0) return 0;
+  ok();
+  return need;
+}
+
+int lotus_linear_fwd_ws(const void* x, const void* w_packed, const float* bias, void* y, int m, int in_features,
+                        int out_features, int act, int out_kind, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream) {
   const int st = check_linear(x, w_packed, y, m, in_features, out_features, act, out_kind);
   if (st != LOTUS_OK) return st;
   if (m > 8)
-    return lotus_gemm_bias_fwd(x, w_packed, bias, y, m, in_features, out_features, act, out_kind, stream);
+    return gemm_fwd_impl(x, w_packed, bias, y, m, in_features, out_features, act, out_kind, workspace, workspace_bytes,
+                         stream);
   const bool f16 = out_kind == LOTUS_OUT_NHWC_F16;
   const int ldy = f16 ? cs_of(out_features) : out_features;
   cudaError_t e = launch_gemv(w_packed, 1, round64(in_features), x, 1, cs_of(in_features), bias, y, f16 ? 1 : 0, ldy,

@@ -49,6 +49,11 @@
 // taps of that chunk, the weights stream per 64-wide K block in chunk-major
 // order (all taps of chunk 0, then chunk 1, ...).  Two producer/MMA pipelines
 // as in AMODE 1/2, each with its own weight stages and two halo buffers.
+// Split-K (AMODE 0/1/2, when a launch has too few output tiles to fill the
+// SMs and the caller passes a workspace): tile t = split * mn_tiles + mn,
+// split s covers K blocks [s*kbs, (s+1)*kbs); the epilogue writes raw fp32
+// partial tiles to the workspace and splitk_reduce_kernel sums them in split
+// order and applies bias, residual and activation.
 // The epilogue of tile i overlaps the main loop of the tiles after it.  Every wait is
 // bounded; an expired wait records an error code and the CTA drains and exits.
 //
@@ -117,7 +122,37 @@ struct ConvTcParams {
   int a_rowbytes;   // Cs_in * 2: 32, 64 or 128
   int a_layout;     // tcgen05 descriptor swizzle code of that row width
   int cchunks;      // AMODE 4: 64-channel chunks per pixel (Cs_in / 64)
+  // split-K
+  int ksplit;       // K splits (1 = none)
+  int kbs;          // K blocks per split
+  int mn_tiles;     // output tiles (tiles = mn_tiles * ksplit)
+  float* ws;        // [ksplit][ws_rows][ws_ld] fp32 partial sums
+  int ws_rows;      // m_tiles * 128
+  int ws_ld;        // n_tiles * BN
 };
+
+// Output tile and K-block range of tile t (split-K: t = split * mn_tiles + mn).
+struct TileK {
+  int mn, split, kb0, nkb;
+};
+__device__ __forceinline__ TileK tile_k(const ConvTcParams& p, int t) {
+  TileK r;
+  r.split = t / p.mn_tiles;
+  r.mn = t - r.split * p.mn_tiles;
+  r.kb0 = r.split * p.kbs;
+  r.nkb = p.KB - r.kb0 < p.kbs ? p.KB - r.kb0 : p.kbs;
+  return r;
+}
+
+// Raw fp32 accumulator chunk (32 columns) into the split-K workspace.
+__device__ __forceinline__ void store_partial(const ConvTcParams& p, const uint32_t (&v)[32], int split, int row,
+                                              int col) {
+  float4* dst = reinterpret_cast<float4*>(p.ws + (static_cast<size_t>(split) * p.ws_rows + row) * p.ws_ld + col);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]), __uint_as_float(v[4 * j + 2]),
+                         __uint_as_float(v[4 * j + 3]));
+}
 
 constexpr int kHaloSlotsMax = 8;
 // weights + halo ring (AMODE 3): what remains of the 227 KB of shared memory
@@ -495,9 +530,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     const int hcol = (warp >> 2) * kHalf;
     const int erow = q * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
-    const bool has_res = p.residual != nullptr && p.out_kind == 0;
+    // split-K exists only in the staged modes: elsewhere its code compiles away
+    constexpr bool kSplitable = AMODE <= 2;
+    const bool has_res = p.residual != nullptr && p.out_kind == 0 && (!kSplitable || p.ksplit == 1);
     // output row of this thread in tile t (em) and whether it is a real pixel
     auto row_of = [&](int t, int& em, bool& rvalid) {
+      if (AMODE != 3 && AMODE != 4) t = tile_k(p, t).mn;
       em = (t / p.n_tiles) * kBlockM + erow;
       rvalid = em < p.M;
       if (AMODE == 3 || AMODE == 4) {
@@ -523,7 +561,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       int em_t;
       bool ok_t;
       row_of(t, em_t, ok_t);
-      const int n0_t = (t % p.n_tiles) * BN;
+      const int n0_t = ((kSplitable ? tile_k(p, t).mn : t) % p.n_tiles) * BN;
       if (has_res && ok_t && t < p.tiles) {
         const uint4* rrow =
             reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em_t) * p.Cs_out + n0_t + hcol);
@@ -536,7 +574,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     if (kPipeRes) load_res(blockIdx.x, res);
     int lt = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
-      const int n0 = (t % p.n_tiles) * BN;
+      const TileK tk = kSplitable ? tile_k(p, t) : TileK{t, 0, 0, p.KB};
+      const int n0 = (tk.mn % p.n_tiles) * BN;
       const int ab = lt % C::kAccBufs;
       int em;
       bool rvalid;
@@ -573,6 +612,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             if (lane == 0) mbar_arrive(&tempty[ab]);
           }
           const int cl = hcol + cc * 32;
+          if (kSplitable && p.ksplit > 1) {
+            if (ok) store_partial(p, vc, tk.split, (tk.mn / p.n_tiles) * kBlockM + erow, n0 + cl);
+            continue;
+          }
           uint4 rc[4];
           if (has_res && rvalid) {
             const uint4* rrow =
@@ -602,6 +645,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);
+      if (kSplitable && p.ksplit > 1) {
+        if (ok) {
+#pragma unroll
+          for (int cc = 0; cc < kHalf / 32; ++cc)
+            store_partial(p, v[cc], tk.split, (tk.mn / p.n_tiles) * kBlockM + erow, n0 + hcol + cc * 32);
+        }
+        continue;
+      }
       // staged stores at BN >= 128 (measured: faster for ResNet stages 2-4,
       // slower for the BN=64 halo layers, whose epilogue per tile is short)
       if (BN >= 128 && p.out_kind == 0 && __all_sync(0xffffffffu, ok)) {
@@ -724,7 +775,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           umma_commit(&tfull[ab]);
           continue;
         }
-        for (int kb = 0; kb < p.KB; ++kb, ++it) {
+        const int nkb = tile_k(p, t).nkb;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int st = issuer * C::kRingStages + static_cast<int>(it % C::kRingStages);
           if (!mbar_wait_relaxed(&full[st], (it / C::kRingStages) & 1, kErrWaitFull)) {
             ok = false;
@@ -830,8 +882,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       int plt = 0;
       for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3 && AMODE != 4; t += gridDim.x, ++plt) {
         if (C::kRings == 2 && (plt & 1) != ring) continue;
-        const int m0 = (t / p.n_tiles) * kBlockM;
-        const int n0 = (t % p.n_tiles) * BN;
+        const TileK tk = tile_k(p, t);
+        const int m0 = (tk.mn / p.n_tiles) * kBlockM;
+        const int n0 = (tk.mn % p.n_tiles) * BN;
         int wst = 0, hst = 0, nimg = 0;
         if (AMODE == 1) {
           nimg = m0 / ohw;
@@ -841,8 +894,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           wst = ow * p.sw - p.pw;
           hst = oh * p.sh - p.ph;
         }
-        int r = 0, s = 0, c0 = 0;
-        for (int kb = 0; kb < p.KB; ++kb, ++it) {
+        // first K block of this split: its (tap, channel) position
+        const int cpt = p.Cs_in / kBlockK;  // AMODE 1: 64-channel blocks per tap
+        int c0 = 0, s = 0, r = 0;
+        if (AMODE == 1) {
+          const int tap0 = tk.kb0 / cpt;
+          c0 = (tk.kb0 - tap0 * cpt) * kBlockK;
+          r = tap0 / p.kw;
+          s = tap0 - r * p.kw;
+        }
+        for (int kb = tk.kb0; kb < tk.kb0 + tk.nkb; ++kb, ++it) {
           const int st = ring * C::kRingStages + static_cast<int>(it % C::kRingStages);
           if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kRingStages) & 1) ^ 1, kErrWaitEmpty)) {
             ok = false;
@@ -888,7 +949,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-      const int m0 = (t / p.n_tiles) * kBlockM;
+      const TileK tk = tile_k(p, t);
+      const int m0 = (tk.mn / p.n_tiles) * kBlockM;
       int ih0[8], iw0[8];
       const __half* xb[8];
 #pragma unroll
@@ -907,7 +969,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           xb[i] = p.x + static_cast<int64_t>(n_img) * p.H * p.W * p.Cs_in;
         }
       }
-      for (int kb = 0; kb < p.KB; ++kb, ++it) {
+      for (int kb = tk.kb0; kb < tk.kb0 + tk.nkb; ++kb, ++it) {
         const int st = it % STAGES;
         if (*abort_flag || !mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, kErrWaitEmpty)) {
           ok = false;
@@ -1102,6 +1164,66 @@ static double halo4_plan(const ConvTcArgs& a, int bn, int stages, ConvTcParams* 
   return static_cast<double>(a.OH) * a.OW / (static_cast<double>(tpi) * kBlockM);
 }
 
+// Split-K reduction: y[m, c] = act(bias[c] + sum_s ws[s][m][c] (+ residual)),
+// eight channels per thread, summed in split order (deterministic).  NHWC
+// fp16 output (pad channels written as zero) or fp32 rows.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int ws_rows, int ws_ld,
+                                     const float* __restrict__ bias, const __half* __restrict__ residual,
+                                     void* __restrict__ y, int M, int cout, int cs_out, int act, int out_kind) {
+  const int groups = out_kind == 0 ? cs_out / 8 : (cout + 7) / 8;
+  const int total = M * groups;  // < 2^31, checked by the launcher
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int m = i / groups;
+    const int c0 = (i - m * groups) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4* src = reinterpret_cast<const float4*>(ws + (static_cast<size_t>(sp) * ws_rows + m) * ws_ld + c0);
+      const float4 a = __ldg(src), b = __ldg(src + 1);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    float res[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (residual) {
+      const uint4 r = __ldg(reinterpret_cast<const uint4*>(residual + static_cast<size_t>(m) * cs_out + c0));
+      const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(rh[j]);
+        res[2 * j] = f.x;
+        res[2 * j + 1] = f.y;
+      }
+    }
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = c0 + j;
+      const float v = acc[j] + ((bias != nullptr && c < cout) ? __ldg(bias + c) : 0.f) + res[j];
+      o[j] = c < cout ? apply_act(v, act) : 0.f;
+    }
+    if (out_kind == 0) {
+      *reinterpret_cast<uint4*>(static_cast<__half*>(y) + static_cast<size_t>(m) * cs_out + c0) =
+          make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
+    } else {
+      float* yr = static_cast<float*>(y) + static_cast<size_t>(m) * cout;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j < cout) yr[c0 + j] = o[j];
+    }
+  }
+}
+
+// Split count for an output-tile grid of `mn` tiles over KB K blocks on `sms`
+// SMs: none unless the grid fills at most half of the SMs; at least 4 K blocks
+// per split; every split non-empty.
+static int split_count(long mn, int kb_total, int sms, int* kbs) {
+  *kbs = kb_total;
+  if (mn * 2 > sms || kb_total < 8) return 1;
+  const long s = std::min<long>(kb_total / 4, sms / mn);
+  if (s < 2) return 1;
+  *kbs = static_cast<int>((kb_total + s - 1) / s);
+  return (kb_total + *kbs - 1) / *kbs;
+}
+
 static int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -1133,7 +1255,7 @@ static cudaError_t launch_impl(const CUtensorMap& mw, const CUtensorMap& ma, con
   return cudaGetLastError();
 }
 
-int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
+int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, size_t* ws_need) {
   ConvTcParams p{};
   p.x = static_cast<const __half*>(a.x);
   p.bias = a.bias;
@@ -1211,6 +1333,31 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     amode = a.Cs_in % kBlockK == 0 && x_bytes >= (128u << 10) ? 1 : 0;
   if (amode == 3) p.tiles = static_cast<int>(static_cast<long>(n_img) * p.tpi);
   if (amode == 4) p.tiles = static_cast<int>(static_cast<long>(n_img) * p.tpi * p.n_tiles);
+  // split-K: launches whose output tiles fill at most half of the SMs split
+  // their K loop when the caller passed a large enough workspace
+  p.ksplit = 1;
+  p.kbs = p.KB;
+  p.mn_tiles = p.tiles;
+  if ((amode == 0 || amode == 1 || amode == 2) && a.out_kind != 2) {
+    int kbs = p.KB;
+    const int sp = split_count(p.tiles, p.KB, num_sms(), &kbs);
+    const size_t need = sp > 1 ? static_cast<size_t>(sp) * (m_tiles * kBlockM) * (p.n_tiles * bn) * 4 : 0;
+    if (ws_need) {
+      *ws_need = need;
+      return 0;
+    }
+    if (sp > 1 && a.ws != nullptr && need <= a.ws_bytes && static_cast<long>(a.M) * (p.n_tiles * bn / 8) < (1L << 31)) {
+      p.ksplit = sp;
+      p.kbs = kbs;
+      p.ws = a.ws;
+      p.ws_rows = static_cast<int>(m_tiles * kBlockM);
+      p.ws_ld = p.n_tiles * bn;
+      p.tiles = p.mn_tiles * sp;
+    }
+  } else if (ws_need) {
+    *ws_need = 0;
+    return 0;
+  }
   if (amode == 0 && p.KB * 8 > kMaxTable) {
     *err = "conv: K too large for the gather path";
     return -2;
@@ -1254,6 +1401,15 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
       case 4: e = launch_impl<128, 6, 4>(mw, ma, p, stream); break;
       default: e = launch_impl<128, 2, 3>(mw, ma, p, stream); break;
     }
+  }
+  if (e == cudaSuccess && p.ksplit > 1) {
+    const size_t total = static_cast<size_t>(a.M) * (a.out_kind == 0 ? a.Cs_out / 8 : (a.n_cols + 7) / 8);
+    const unsigned grid = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, static_cast<size_t>(num_sms()) * 8));
+    splitk_reduce_kernel<<<grid, 256, 0, stream>>>(p.ws, p.ksplit, p.ws_rows, p.ws_ld, a.bias,
+                                                   static_cast<const __half*>(a.residual), a.y, a.M, a.n_cols,
+                                                   a.Cs_out, a.act, a.out_kind);
+    note_launch();
+    e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);

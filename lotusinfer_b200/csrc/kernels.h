@@ -29,9 +29,14 @@ struct ConvTcArgs {
   int out_kind;           // 0 NHWC fp16, 1 fp32 rows, 2 tconv scatter
   int block_n;            // 0 = choose
   int t_oh, t_ow, t_sh, t_sw, t_ph, t_pw, t_kw, t_cout;
+  float* ws = nullptr;    // split-K workspace (fp32) or null
+  size_t ws_bytes = 0;
 };
 
-int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err);
+// Launches the conv / GEMM kernel (and the split-K reduction when it splits).
+// With ws_need != null it only plans: *ws_need = the workspace bytes the
+// split-K plan for `a` wants (0 = no split), nothing is launched.
+int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, size_t* ws_need = nullptr);
 int read_device_error();
 
 // pack.cu

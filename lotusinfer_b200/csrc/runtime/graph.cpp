@@ -287,6 +287,15 @@ void Graph::Build(const std::string& param_path, const std::string& bin_path) {
   TopoSortLayers();
   // bind in order so flatten aliases exist before their consumers bind
   for (auto& l : topo_sorted_layers_) l->Bind(operands_);
+  // one split-K workspace for the layer that wants the most
+  size_t ws = 0;
+  for (auto& l : topo_sorted_layers_) ws = std::max(ws, l->WorkspaceBytes());
+  if (ws > 0) {
+    void* p = nullptr;
+    CudaCheck(cudaMalloc(&p, ws), "cudaMalloc(workspace)");
+    workspace_ = std::shared_ptr<void>(p, [](void* q) { cudaFree(q); });
+    for (auto& l : topo_sorted_layers_) l->SetWorkspace(p, ws);
+  }
   CudaCheck(cudaStreamSynchronize(stream_), "graph build");
 }
 

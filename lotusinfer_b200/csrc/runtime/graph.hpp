@@ -82,6 +82,7 @@ class Graph {
   // space-to-depth stem rewrite (factor 1 = none)
   int stem_s2d_ = 1, stem_pad_h_ = 0, stem_pad_w_ = 0;
   std::vector<uint32_t> stem_shape_;
+  std::shared_ptr<void> workspace_;  // split-K scratch shared by the layers (one stream, one layer at a time)
 };
 
 }  // namespace lotus

@@ -183,9 +183,16 @@ void Conv2dLayer::Bind(const OperandMap& operands) {
 
 void Conv2dLayer::Forward(cudaStream_t stream) {
   const void* res = residual_name_.empty() ? nullptr : inputs_.back()->tensor_.Data();
-  LotusCheck(lotus_conv2d_fwd(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()), res,
-                              outputs_[0]->tensor_.Data(), &desc_, stream),
+  LotusCheck(lotus_conv2d_fwd_ws(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
+                                 res, outputs_[0]->tensor_.Data(), &desc_, workspace_, workspace_bytes_, stream),
              name_);
+}
+
+size_t Conv2dLayer::WorkspaceBytes() const { return lotus_conv2d_workspace_bytes(&desc_); }
+
+int Conv2dLayer::Launches() const {
+  const size_t need = WorkspaceBytes();
+  return (need > 0 && workspace_ != nullptr && need <= workspace_bytes_) ? 2 : 1;  // conv + split-K reduction
 }
 
 double Conv2dLayer::Flops() const {
@@ -273,10 +280,20 @@ void LinearLayer::Bind(const OperandMap& operands) {
 }
 
 void LinearLayer::Forward(cudaStream_t stream) {
-  LotusCheck(lotus_linear_fwd(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
-                              outputs_[0]->tensor_.Data(), m_, in_f_, out_f_, af_,
-                              out_f32_ ? LOTUS_OUT_ROWS_F32 : LOTUS_OUT_NHWC_F16, stream),
+  LotusCheck(lotus_linear_fwd_ws(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
+                                 outputs_[0]->tensor_.Data(), m_, in_f_, out_f_, af_,
+                                 out_f32_ ? LOTUS_OUT_ROWS_F32 : LOTUS_OUT_NHWC_F16, workspace_, workspace_bytes_,
+                                 stream),
              name_);
+}
+
+size_t LinearLayer::WorkspaceBytes() const { return lotus_linear_workspace_bytes(m_, in_f_, out_f_); }
+
+int LinearLayer::Launches() const {
+  // GEMV, or GEMM (+ the split-K reduction)
+  if (m_ <= 8) return 1;
+  const size_t need = WorkspaceBytes();
+  return (need > 0 && workspace_ != nullptr && need <= workspace_bytes_) ? 2 : 1;
 }
 
 double LinearLayer::Flops() const { return 2.0 * m_ * static_cast<double>(in_f_) * out_f_; }

@@ -53,6 +53,13 @@ class Layer {
   virtual double Bytes() const;
   // Number of library kernel launches one Forward issues.
   virtual int Launches() const { return 1; }
+  // Split-K workspace this layer's kernels want (0 = none) and the shared
+  // graph workspace it may use (layers run one after another on one stream).
+  virtual size_t WorkspaceBytes() const { return 0; }
+  void SetWorkspace(void* ws, size_t bytes) {
+    workspace_ = ws;
+    workspace_bytes_ = bytes;
+  }
   // Prepacked weight (device) and its size; null when the layer has none.
   virtual const void* Weight(size_t* bytes) const {
     if (bytes) *bytes = 0;
@@ -64,6 +71,8 @@ class Layer {
   std::vector<std::string> inputs_name_, outputs_name_;
   std::vector<std::shared_ptr<Operand>> inputs_, outputs_;
   ActivationFunction af_ = NONE;
+  void* workspace_ = nullptr;
+  size_t workspace_bytes_ = 0;
   friend class Graph;
 };
 
@@ -105,6 +114,8 @@ class Conv2dLayer : public Layer {
   void Bind(const OperandMap& operands) override;
   void Forward(cudaStream_t stream) override;
   double Flops() const override;
+  size_t WorkspaceBytes() const override;
+  int Launches() const override;
   lotus_conv2d_desc Desc() const { return desc_; }
   const void* Weight(size_t* bytes) const override {
     if (bytes) *bytes = w_bytes_;
@@ -148,6 +159,8 @@ class LinearLayer : public Layer {
   void Bind(const OperandMap& operands) override;
   void Forward(cudaStream_t stream) override;
   double Flops() const override;
+  size_t WorkspaceBytes() const override;
+  int Launches() const override;
   const void* Weight(size_t* bytes) const override {
     if (bytes) *bytes = w_bytes_;
     return w_packed_.get();

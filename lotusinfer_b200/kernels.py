@@ -79,10 +79,17 @@ def conv2d_prepack(w_oihw: torch.Tensor, c_in: int) -> torch.Tensor:
     return out.view(cout, -1)
 
 
+def conv2d_workspace_bytes(n, c_in, h, w, c_out, k, stride=1, pad=0, act=ACT_NONE, out_f32=False) -> int:
+    """Workspace bytes the split-K plan of this conv wants (0 = no split)."""
+    d = conv_desc(n, c_in, h, w, c_out, k, stride, pad, act, OUT_ROWS_F32 if out_f32 else OUT_NHWC_F16)
+    return int(abi.lib().lotus_conv2d_workspace_bytes(ctypes.byref(d)))
+
+
 def conv2d(x: torch.Tensor, c_in: int, w_packed: torch.Tensor, bias: Optional[torch.Tensor], c_out: int,
            k, stride=1, pad=0, act=ACT_NONE, residual: Optional[torch.Tensor] = None,
-           out_f32: bool = False) -> torch.Tensor:
-    """NHWC fp16 conv2d; returns NHWC fp16 [N, OH, OW, Cs_out] or fp32 rows [N*OH*OW, Cout]."""
+           out_f32: bool = False, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """NHWC fp16 conv2d; returns NHWC fp16 [N, OH, OW, Cs_out] or fp32 rows [N*OH*OW, Cout].
+    With `workspace` (a device buffer) the call may split K (lotus_conv2d_fwd_ws)."""
     n, h, w, cs = x.shape
     assert cs == channel_stride(c_in)
     d = conv_desc(n, c_in, h, w, c_out, k, stride, pad, act, OUT_ROWS_F32 if out_f32 else OUT_NHWC_F16)
@@ -92,8 +99,13 @@ def conv2d(x: torch.Tensor, c_in: int, w_packed: torch.Tensor, bias: Optional[to
         y = torch.empty((n * oh.value * ow.value, c_out), dtype=torch.float32, device=x.device)
     else:
         y = torch.empty((n, oh.value, ow.value, channel_stride(c_out)), dtype=torch.float16, device=x.device)
-    check(abi.lib().lotus_conv2d_fwd(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(residual), _ptr(y),
-                                     ctypes.byref(d), _stream()))
+    if workspace is None:
+        check(abi.lib().lotus_conv2d_fwd(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(residual), _ptr(y),
+                                         ctypes.byref(d), _stream()))
+    else:
+        check(abi.lib().lotus_conv2d_fwd_ws(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(residual), _ptr(y),
+                                            ctypes.byref(d), _ptr(workspace),
+                                            workspace.numel() * workspace.element_size(), _stream()))
     return y
 
 
@@ -137,13 +149,19 @@ def linear_prepack(w: torch.Tensor, fc_chw: Optional[Sequence[int]] = None) -> t
 
 
 def linear(x: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor], in_f: int, out_f: int,
-           act=ACT_NONE, out_f32=True, force_gemm=False) -> torch.Tensor:
-    """x fp16 rows [M, Cs(in_f)] -> fp32 [M, out_f] or fp16 [M, Cs(out_f)]."""
+           act=ACT_NONE, out_f32=True, force_gemm=False, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x fp16 rows [M, Cs(in_f)] -> fp32 [M, out_f] or fp16 [M, Cs(out_f)].
+    With `workspace` the GEMM path may split K (lotus_linear_fwd_ws)."""
     m = x.shape[0]
     if out_f32:
         y = torch.empty((m, out_f), dtype=torch.float32, device=x.device)
     else:
         y = torch.empty((m, channel_stride(out_f)), dtype=torch.float16, device=x.device)
+    if workspace is not None:
+        check(abi.lib().lotus_linear_fwd_ws(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(y), m, in_f, out_f, act,
+                                            OUT_ROWS_F32 if out_f32 else OUT_NHWC_F16, _ptr(workspace),
+                                            workspace.numel() * workspace.element_size(), _stream()))
+        return y
     fn = abi.lib().lotus_gemm_bias_fwd if force_gemm else abi.lib().lotus_linear_fwd
     check(fn(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(y), m, in_f, out_f, act,
              OUT_ROWS_F32 if out_f32 else OUT_NHWC_F16, _stream()))

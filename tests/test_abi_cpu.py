@@ -91,3 +91,15 @@ def test_entry_points_reject_null_and_misaligned_pointers_before_launch():
     assert L.lotus_tconv2d_out_hw(ctypes.byref(t), None, None) == -1
     assert L.lotus_linear_prepack(None, None, 4, 4, 0, 0, 0, None) == -1
     assert L.lotus_linear_prepack(ctypes.c_void_p(16), ctypes.c_void_p(16), 10, 4, 2, 2, 2, None) == -1  # 2*2*2 != 10
+
+
+def test_splitk_workspace_queries():
+    """The split-K planner needs no GPU: small grids with long K ask for a
+    workspace, full grids and the GEMV path do not."""
+    from lotusinfer_b200 import kernels as K
+    assert K.conv2d_workspace_bytes(1, 512, 7, 7, 512, 3, 1, 1) > 0      # 4 output tiles, K = 4608
+    assert K.conv2d_workspace_bytes(256, 512, 7, 7, 512, 3, 1, 1) == 0   # 196 tiles fill the GPU
+    assert K.conv2d_workspace_bytes(1, 3, 20, 20, 8, 3, 1, 1) == 0       # K = 64: one K block
+    L = abi.lib()
+    assert L.lotus_linear_workspace_bytes(32, 9216, 4096) > 0
+    assert L.lotus_linear_workspace_bytes(4, 9216, 4096) == 0            # batch <= 8 runs the GEMV

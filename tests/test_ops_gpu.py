@@ -153,6 +153,69 @@ def test_conv2d_halo_many_tiles_per_cta(case, monkeypatch):
     _no_device_error()
 
 
+SPLITK_CASES = [
+    # id, n, c, h, w, cout, k, stride, pad, act, residual: output grids too
+    # small to fill the GPU, so the K loop splits over CTAs
+    ("splitk_gather_stage3_bs1_residual", 1, 256, 14, 14, 256, 3, 1, 1, 1, True),
+    ("splitk_im2col_stage2_bs1", 1, 128, 28, 28, 128, 3, 1, 1, 1, False),
+    ("splitk_bn256_bs1_residual", 1, 256, 28, 28, 256, 3, 1, 1, 0, True),
+    ("splitk_stage4_bs1_k4608", 1, 512, 7, 7, 512, 3, 1, 1, 1, True),
+    ("splitk_cout17_sigmoid", 1, 64, 16, 16, 17, 3, 1, 1, 2, False),
+]
+
+
+@pytest.mark.parametrize("case", SPLITK_CASES, ids=[c[0] for c in SPLITK_CASES])
+def test_conv2d_splitk_parity(case):
+    """lotus_conv2d_fwd_ws: split-K partial sums + reduction (bias, residual,
+    activation) against the oracle; deterministic; a too-small workspace
+    runs unsplit."""
+    K = _k()
+    _, n, c, h, w, cout, k, s, p, act, with_res = case
+    rng = _rng(zlib.crc32(case[0].encode()))
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / (c * k * k)), (cout, c, k, k)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, cout).astype(np.float32)
+    oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    res = rng.normal(0, 1, (n, cout, oh, ow)).astype(np.float32) if with_res else None
+    want = oracle.conv2d(x, wt, b, (s, s), (p, p), act, residual=res)
+    need = K.conv2d_workspace_bytes(n, c, h, w, cout, k, s, p, act)
+    assert need > 0
+    ws = torch.empty(need // 4, dtype=torch.float32, device=DEV)
+    xg, wp = K.to_nhwc(_gpu(x)), K.conv2d_prepack(_gpu(wt), c)
+    rg = K.to_nhwc(_gpu(res)) if with_res else None
+    y = K.conv2d(xg, c, wp, _gpu(b), cout, k, s, p, act, residual=rg, workspace=ws)
+    assert_close(K.from_nhwc(y, cout).cpu().numpy(), want, what=case[0])
+    if y.shape[-1] != cout:
+        assert torch.count_nonzero(y[..., cout:]).item() == 0
+    assert torch.equal(y, K.conv2d(xg, c, wp, _gpu(b), cout, k, s, p, act, residual=rg, workspace=ws))
+    small = torch.empty(need // 4 - 4, dtype=torch.float32, device=DEV)
+    y_small = K.conv2d(xg, c, wp, _gpu(b), cout, k, s, p, act, residual=rg, workspace=small)
+    assert_close(K.from_nhwc(y_small, cout).cpu().numpy(), want, what=case[0] + "/unsplit")
+    if not with_res:
+        y32 = K.conv2d(xg, c, wp, _gpu(b), cout, k, s, p, act, out_f32=True, workspace=ws)
+        assert_close(y32.view(n, oh, ow, cout).permute(0, 3, 1, 2).cpu().numpy(), want, what=case[0] + "/f32")
+    _no_device_error()
+
+
+def test_linear_splitk_parity():
+    """AlexNet-like FC at batch 32 (32 output tiles, K = 9216) through the
+    split-K GEMM."""
+    K = _k()
+    rng = _rng(29)
+    m, kk, nn = 32, 9216, 512
+    wt = rng.normal(0, np.sqrt(1 / kk), (nn, kk)).astype(np.float32)
+    x = rng.uniform(-1, 1, (m, kk)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, nn).astype(np.float32)
+    from lotusinfer_b200 import abi
+    need = abi.lib().lotus_linear_workspace_bytes(m, kk, nn)
+    assert need > 0
+    ws = torch.empty(need // 4, dtype=torch.float32, device=DEV)
+    wp = K.linear_prepack(_gpu(wt))
+    got = K.linear(_gpu(x).half(), wp, _gpu(b), kk, nn, act=1, out_f32=True, workspace=ws).cpu().numpy()
+    assert_close(got, oracle.gemm(x, wt, b, act=1), what="linear split-K")
+    _no_device_error()
+
+
 def test_conv2d_repeatable_and_no_bias():
     K = _k()
     rng = _rng(11)
