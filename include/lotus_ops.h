@@ -97,6 +97,27 @@ size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d);
 int lotus_conv2d_fwd_ws(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                         const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* lotus_conv2d_fwd_ws without a caller workspace, for callers that cannot
+ * allocate device memory: cudaMalloc / cudaFree can synchronise the device and
+ * can fail, so code that runs inside a latency-critical serving loop, inside a
+ * host framework that owns the device memory pool, or anywhere a
+ * mid-inference out-of-memory must not happen cannot call it.  The split-K
+ * partial sums go to a scratch area compiled into this library,
+ * LOTUS_NOALLOC_SCRATCH_BYTES (8 MiB) per GPU, which every GPU that loads the
+ * library holds until the process exits; nothing is allocated per call.
+ * A shape whose split needs more than that is rejected with
+ * LOTUS_ERR_UNSUPPORTED (lotus_conv2d_workspace_bytes tells beforehand); a
+ * shape that does not split runs like lotus_conv2d_fwd.  The first call on a
+ * device (with that device current) looks up the scratch's device address;
+ * make it before any stream capture.  All calls share the one scratch, so
+ * calls whose kernels can overlap on the GPU (other streams, other host
+ * threads) race: the caller serialises them.  Each call writes every partial
+ * sum before reading it, so nothing needs clearing between calls.  No
+ * counterpart in the reference (it has no split-K). */
+#define LOTUS_NOALLOC_SCRATCH_BYTES (8u << 20)
+int lotus_conv2d_fwd_noalloc(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                             const lotus_conv2d_desc* d, cudaStream_t stream);
+
 /* Transposed convolution (PyTorch ConvTranspose2d semantics, dilation 1).
  * Replaces lotus::TransConv2d (reference source/operator/transposed_conv2d.cu:17-140,
  * launched from source/layer/layer_transposed_conv2d.cu:37-72). */

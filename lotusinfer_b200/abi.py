@@ -56,6 +56,7 @@ SIGNATURES = {
     "lotus_conv2d_fwd": (_I, [_V, _V, _V, _V, _V, _CD, _V]),
     "lotus_conv2d_workspace_bytes": (_S, [_CD]),
     "lotus_conv2d_fwd_ws": (_I, [_V, _V, _V, _V, _V, _CD, _V, _S, _V]),
+    "lotus_conv2d_fwd_noalloc": (_I, [_V, _V, _V, _V, _V, _CD, _V]),
     "lotus_tconv2d_out_hw": (_I, [_TD, _IP, _IP]),
     "lotus_tconv2d_packed_weight_bytes": (_S, [_TD]),
     "lotus_tconv2d_prepack": (_I, [_V, _V, _TD, _V]),

@@ -173,6 +173,26 @@ int lotus_conv2d_fwd_ws(const void* x, const void* w_packed, const float* bias, 
   return conv_fwd_impl(x, w_packed, bias, residual, y, d, workspace, workspace_bytes, stream);
 }
 
+int lotus_conv2d_fwd_noalloc(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                             const lotus_conv2d_desc* d, cudaStream_t stream) {
+  static_assert(kNoAllocScratchBytes == LOTUS_NOALLOC_SCRATCH_BYTES, "scratch size in the header");
+  int oh, ow;
+  const int st = check_conv_desc(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  const size_t need = lotus_conv2d_workspace_bytes(d);
+  if (need > kNoAllocScratchBytes)
+    return fail(LOTUS_ERR_UNSUPPORTED, "conv2d_noalloc: this shape's split-K needs " + std::to_string(need) +
+                                           " bytes of scratch, above the " + std::to_string(kNoAllocScratchBytes) +
+                                           " built into the library; use lotus_conv2d_fwd_ws with a caller workspace");
+  float* scratch = nullptr;
+  if (need > 0) {
+    const char* err = "";
+    if (conv_tc_noalloc_scratch(&scratch, &err) != 0)
+      return fail(LOTUS_ERR_CUDA, std::string("conv2d_noalloc: scratch set-up: ") + err);
+  }
+  return conv_fwd_impl(x, w_packed, bias, residual, y, d, scratch, scratch ? kNoAllocScratchBytes : 0, stream);
+}
+
 size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d) {
   int oh, ow;
   if (check_conv_desc(d, &oh, &ow) != LOTUS_OK) return 0;

@@ -1418,6 +1418,38 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, s
   return 0;
 }
 
+// Split-K scratch of lotus_conv2d_fwd_noalloc, for callers that cannot
+// allocate device memory themselves.  Compiled into the library: every GPU
+// that loads it holds these kNoAllocScratchBytes until the process exits.
+// Host code must not pass the symbol itself to a kernel (on the host it is a
+// stand-in, not a device address): conv_tc_noalloc_scratch() looks up the
+// address per device.
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+int conv_tc_noalloc_scratch(float** ptr, const char** err) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static float* addr[kMaxDevices] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *err = "no usable current CUDA device";
+    return -3;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    // once per device, with that device current (the caller's current device)
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *err = e != cudaSuccess ? cudaGetErrorString(e) : "cudaGetSymbolAddress returned null";
+      return -3;
+    }
+    addr[dev] = static_cast<float*>(p);
+  }
+  *ptr = addr[dev];
+  return 0;
+}
+
 int read_device_error() {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, lotus_dev::g_lotus_device_error, sizeof(int)) != cudaSuccess) return -1;

@@ -37,6 +37,12 @@ struct ConvTcArgs {
 // With ws_need != null it only plans: *ws_need = the workspace bytes the
 // split-K plan for `a` wants (0 = no split), nothing is launched.
 int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, size_t* ws_need = nullptr);
+
+// Built-in split-K scratch of lotus_conv2d_fwd_noalloc (LOTUS_NOALLOC_SCRATCH_BYTES).
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+// Device address of that scratch on the current device; the first call on a
+// device looks it up (cudaGetSymbolAddress).  0 = ok, < 0 = error in *err.
+int conv_tc_noalloc_scratch(float** ptr, const char** err);
 int read_device_error();
 
 // pack.cu
