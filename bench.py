@@ -180,6 +180,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
+        # rank 0's stdout carries exactly one JSON line: NCCL's version banner
+        # (NCCL_DEBUG=VERSION) would land there too, so keep it at warnings
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
 
     B = args.batch
