@@ -22,9 +22,16 @@ using namespace lotus_dev;
 
 // IT is the index type: 32-bit when every element offset fits (the common
 // case; 64-bit division in the grid-stride loop dominated the kernel), else 64-bit.
-template <typename IT>
+// KS = 3: the window is 3x3 at compile time, so the nine tap loads are
+// unrolled and in flight together (with runtime kh/kw each load waits for the
+// loop control of the one before); KS = 0: any window.
+template <typename IT, int KS>
 __global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __restrict__ y, int n, int c, int cs, int h,
                                     int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int act) {
+  if (KS > 0) {
+    kh = KS;
+    kw = KS;
+  }
   const int groups = cs / 8;
   const IT total = static_cast<IT>(n) * oh * ow * groups;
   for (IT i = blockIdx.x * static_cast<IT>(blockDim.x) + threadIdx.x; i < total;
@@ -40,10 +47,12 @@ __global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __rest
     for (int j = 0; j < 8; ++j) m[j] = -INFINITY;
     const int y0 = oy * sh - ph, x0 = ox * sw - pw;
     const __half* xb = x + static_cast<IT>(img) * h * w * cs + g * 8;
-    for (int r = 0; r < kh; ++r) {
+#pragma unroll
+    for (int r = 0; r < (KS > 0 ? KS : kh); ++r) {
       const int iy = y0 + r;
       if (iy < 0 || iy >= h) continue;
-      for (int s = 0; s < kw; ++s) {
+#pragma unroll
+      for (int s = 0; s < (KS > 0 ? KS : kw); ++s) {
         const int ix = x0 + s;
         if (ix < 0 || ix >= w) continue;
         float f[8];
@@ -100,11 +109,14 @@ cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, 
                            int sh, int sw, int ph, int pw, int act, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
   const bool small = static_cast<size_t>(n) * h * w * cs < (1u << 31) && total < (1u << 31);
-  if (small)
-    maxpool_nhwc_kernel<int><<<grid_for(total, 256, 32), 256, 0, s>>>(
+  if (small && kh == 3 && kw == 3)
+    maxpool_nhwc_kernel<int, 3><<<grid_for(total, 256, 32), 256, 0, s>>>(
+        static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
+  else if (small)
+    maxpool_nhwc_kernel<int, 0><<<grid_for(total, 256, 32), 256, 0, s>>>(
         static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
   else
-    maxpool_nhwc_kernel<size_t><<<grid_for(total, 256), 256, 0, s>>>(
+    maxpool_nhwc_kernel<size_t, 0><<<grid_for(total, 256), 256, 0, s>>>(
         static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
   note_launch();
   return cudaGetLastError();
