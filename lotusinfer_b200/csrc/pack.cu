@@ -120,9 +120,14 @@ __global__ void nhwc_to_nchw_kernel(const __half* __restrict__ x, float* __restr
 // y[n, i, j, (a*f + b)*c + ch] = xpad[n, ch, f*i + a, f*j + b] with
 // xpad[.., u, v] = x[.., u - pad_h, v - pad_w] inside the image, 0 outside;
 // channels c*f*f .. cs-1 are zero.  One thread per output pixel.
-template <typename IT>
+// FF/CC > 0 fix the factor and the channel count at compile time (the
+// 3-channel factor-2 ResNet stem): the loops unroll and all loads of a pixel
+// are in flight together; 0 = runtime values.
+template <typename IT, int FF, int CC>
 __global__ void space_to_depth_kernel(const float* __restrict__ x, __half* __restrict__ y, int n, int c, int h, int w,
                                       int f, int pad_h, int pad_w, int oh, int ow, int cs) {
+  if (FF > 0) f = FF;
+  if (CC > 0) c = CC;
   const IT pixels = static_cast<IT>(n) * oh * ow;
   const IT plane = static_cast<IT>(h) * w;
   for (IT p = blockIdx.x * static_cast<IT>(blockDim.x) + threadIdx.x; p < pixels;
@@ -137,14 +142,17 @@ __global__ void space_to_depth_kernel(const float* __restrict__ x, __half* __res
     // consecutive f-wide runs of one input row, so each warp load coalesces
     float v[8];
     int q = 0, vec = 0;
-    for (int a = 0; a < f; ++a) {
+#pragma unroll
+    for (int a = 0; a < (FF > 0 ? FF : f); ++a) {
       const int u = f * i + a - pad_h;
       const bool row_ok = u >= 0 && u < h;
-      for (int b = 0; b < f; ++b) {
+#pragma unroll
+      for (int b = 0; b < (FF > 0 ? FF : f); ++b) {
         const int col = f * j + b - pad_w;
         const bool ok = row_ok && col >= 0 && col < w;
         const float* src = xb + static_cast<IT>(u) * w + col;
-        for (int ch = 0; ch < c; ++ch) {
+#pragma unroll
+        for (int ch = 0; ch < (CC > 0 ? CC : c); ++ch) {
           v[q++] = ok ? __ldg(src + ch * plane) : 0.f;
           if (q == 8) {
             yd[vec++] = pack8(v);
@@ -165,12 +173,16 @@ __global__ void space_to_depth_kernel(const float* __restrict__ x, __half* __res
 cudaError_t launch_space_to_depth(const float* x, void* y, int n, int c, int h, int w, int f, int pad_h, int pad_w,
                                   int oh, int ow, int cs, cudaStream_t s) {
   const size_t pixels = static_cast<size_t>(n) * oh * ow;
-  if (static_cast<size_t>(n) * c * h * w < (1u << 31) && pixels * cs < (1u << 31))
-    space_to_depth_kernel<int><<<grid_for(pixels, 256, 32), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w, f,
-                                                                         pad_h, pad_w, oh, ow, cs);
+  const bool small = static_cast<size_t>(n) * c * h * w < (1u << 31) && pixels * cs < (1u << 31);
+  if (small && f == 2 && c == 3)
+    space_to_depth_kernel<int, 2, 3><<<grid_for(pixels, 256, 32), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w,
+                                                                               f, pad_h, pad_w, oh, ow, cs);
+  else if (small)
+    space_to_depth_kernel<int, 0, 0><<<grid_for(pixels, 256, 32), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w,
+                                                                               f, pad_h, pad_w, oh, ow, cs);
   else
-    space_to_depth_kernel<size_t><<<grid_for(pixels, 256), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w, f,
-                                                                        pad_h, pad_w, oh, ow, cs);
+    space_to_depth_kernel<size_t, 0, 0><<<grid_for(pixels, 256), 256, 0, s>>>(x, static_cast<__half*>(y), n, c, h, w,
+                                                                              f, pad_h, pad_w, oh, ow, cs);
   note_launch();
   return cudaGetLastError();
 }
