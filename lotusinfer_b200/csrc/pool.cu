@@ -105,6 +105,62 @@ __global__ void adaptive_avgpool_nhwc_kernel(const __half* __restrict__ x, void*
   }
 }
 
+// Large windows (a global pool such as ResNet's 7x7 -> 1x1): one block per
+// output pixel, its threads laid out as (pixel slice, channel group) so that a
+// warp reads consecutive 16-byte channel groups and each thread sums every
+// S-th pixel of the window.  The S partial sums are added in slice order in
+// shared memory.  Requires cs/8 <= blockDim.x.
+__global__ void __launch_bounds__(256) adaptive_avgpool_window_kernel(const __half* __restrict__ x,
+                                                                      void* __restrict__ y, int c, int cs, int h,
+                                                                      int w, int oh, int ow, int act, int out_f32) {
+  __shared__ float red[256 * 8];
+  const int groups = cs / 8;
+  const int slices = static_cast<int>(blockDim.x) / groups;
+  const int g = static_cast<int>(threadIdx.x) % groups;
+  const int sl = static_cast<int>(threadIdx.x) / groups;
+  const int pix = blockIdx.x;
+  const int ox = pix % ow;
+  const int t = pix / ow;
+  const int oy = t % oh;
+  const int img = t / oh;
+  const int hs = (oy * h) / oh, he = ((oy + 1) * h + oh - 1) / oh;
+  const int ws = (ox * w) / ow, we = ((ox + 1) * w + ow - 1) / ow;
+  const int wn = we - ws;
+  const int cnt = (he - hs) * wn;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (sl < slices) {
+    const __half* xb = x + static_cast<size_t>(img) * h * w * cs + g * 8;
+#pragma unroll 4
+    for (int k = sl; k < cnt; k += slices) {
+      const int iy = hs + k / wn;
+      const int ix = ws + k % wn;
+      float f[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (static_cast<size_t>(iy) * w + ix) * cs)), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += f[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[threadIdx.x * 8 + j] = acc[j];
+  }
+  __syncthreads();
+  if (sl != 0) return;
+  for (int s2 = 1; s2 < slices; ++s2) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] += red[(s2 * groups + g) * 8 + j];
+  }
+  const float inv = 1.0f / static_cast<float>(cnt);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = (g * 8 + j < c) ? act_fn(acc[j] * inv, act) : 0.f;
+  if (out_f32) {
+    float* yr = static_cast<float*>(y) + static_cast<size_t>(pix) * c;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (g * 8 + j < c) yr[g * 8 + j] = acc[j];
+  } else {
+    reinterpret_cast<uint4*>(static_cast<__half*>(y) + static_cast<size_t>(pix) * cs)[g] = pack8(acc);
+  }
+}
+
 cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow, int kh, int kw,
                            int sh, int sw, int ph, int pw, int act, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
@@ -125,6 +181,13 @@ cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, 
 cudaError_t launch_adaptive_avgpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow,
                                     int act, int out_f32, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
+  const size_t pixels = static_cast<size_t>(n) * oh * ow;
+  if (cs / 8 <= 256 && (h / oh) * (w / ow) >= 16 && pixels < (1u << 31) && static_cast<size_t>(h) * w * cs < (1u << 31)) {
+    adaptive_avgpool_window_kernel<<<static_cast<unsigned>(pixels), 256, 0, s>>>(static_cast<const __half*>(x), y, c,
+                                                                                 cs, h, w, oh, ow, act, out_f32);
+    note_launch();
+    return cudaGetLastError();
+  }
   adaptive_avgpool_nhwc_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half*>(x), y, n, c, cs, h, w,
                                                                     oh, ow, act, out_f32);
   note_launch();

@@ -330,7 +330,8 @@ def test_maxpool_exact(case):
 
 
 @pytest.mark.parametrize("case", [((2, 512, 7, 7), (1, 1)), ((1, 256, 6, 6), (6, 6)), ((1, 24, 13, 9), (6, 4)),
-                                  ((1, 3, 257, 257), (64, 64))])
+                                  ((1, 3, 257, 257), (64, 64)), ((3, 1000, 9, 11), (1, 1)),
+                                  ((2, 2048, 5, 4), (1, 1)), ((1, 4104, 4, 4), (1, 1)), ((2, 40, 33, 17), (2, 1))])
 def test_adaptive_avgpool(case):
     K = _k()
     shape, out = case
