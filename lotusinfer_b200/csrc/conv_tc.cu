@@ -170,10 +170,16 @@ struct Cfg {
   // stage (must stay below STAGES; two stages stay free for the tensor core)
   static constexpr int kLag = STAGES - 2;
   static constexpr int kEpiWarps = 8;                      // 2 per TMEM lane quarter
+  // BN=64 outside the gather mode: the epilogue warps form two groups of
+  // four that take alternate tiles (the gather mode's 448 threads leave 128
+  // registers a thread, too few for a whole 64-column row set)
+  static constexpr bool kEpiGroups = BN == 64 && AMODE != 0;
+  // warps that drain each accumulator
+  static constexpr int kEpiArrivals = kEpiGroups ? 4 : kEpiWarps;
   static constexpr int kMmaWarp = 8;
   static constexpr int kTmaWarp = 9;
   static constexpr int kGatherWarp0 = 10;                  // AMODE 0: warps 10-13
-  // AMODE 3: four MMA-issuing warps (8, 10, 11, 12) take tiles round robin;
+  // AMODE 3: three MMA-issuing warps (8, 10, 11) take tiles round robin;
   // one thread issues at most one tcgen05.mma per ~80 cycles whatever N is,
   // plus the integer work between two issues, so the short tap loops of
   // this mode need several issuers to keep the tensor pipe busy
@@ -186,8 +192,8 @@ struct Cfg {
   static constexpr int kRings = ((AMODE == 1 || AMODE == 2 || AMODE == 4) && BN <= 128) ? 2 : 1;
   static constexpr int kRingStages = STAGES / kRings;
   static constexpr int kTmaWarp2 = 11;
-  static constexpr int kMmaIssuers = AMODE == 3 ? 4 : (kRings == 2 ? 2 : 1);
-  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 416 : (kRings == 2 ? 384 : 320));
+  static constexpr int kMmaIssuers = AMODE == 3 ? 3 : (kRings == 2 ? 2 : 1);
+  static constexpr int kThreads = AMODE == 0 ? 448 : (AMODE == 3 ? 384 : (kRings == 2 ? 384 : 320));
   // issuer index of a warp (-1: not an issuer): warp 8 is issuer 0, warps
   // 10.. the others
   static __device__ __forceinline__ int issuer_of(int warp) {
@@ -472,7 +478,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
     for (int b = 0; b < C::kAccBufs; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], C::kEpiWarps);
+      mbar_init(&tempty[b], C::kEpiArrivals);
     }
     mbar_init(mma_done, C::kMmaIssuers);
     for (int h = 0; h < kHaloSlotsMax; ++h) {
@@ -570,6 +576,74 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           r[i] = (n0_t + hcol + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
       }
     };
+    if constexpr (C::kEpiGroups) {
+    // BN=64: the two groups of four warps (0-3 and 4-7, one warp per TMEM
+    // lane quarter in each) take alternate tiles, and a warp drains all 64
+    // columns of its 32 rows.  A tile then costs one chain of accumulator
+    // wait, loads, math and stores per warp instead of two half-width
+    // chains, and the two groups' chains overlap.
+    const int grp = warp >> 2;
+    const int gx = static_cast<int>(gridDim.x);
+    int lt = grp;
+    for (int t = static_cast<int>(blockIdx.x) + grp * gx; t < p.tiles; t += 2 * gx, lt += 2) {
+      const TileK tk = kSplitable ? tile_k(p, t) : TileK{t, 0, 0, p.KB};
+      const int n0 = (tk.mn % p.n_tiles) * BN;
+      const int ab = lt % C::kAccBufs;
+      int em;
+      bool rvalid;
+      row_of(t, em, rvalid);
+      const bool tile_full = n0 + BN <= p.Cout;
+      // residual rows of both 32-column chunks, read ahead of the accumulator wait
+      uint4 rc[2][4];
+      if (has_res && rvalid) {
+        const uint4* rrow = reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out + n0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          rc[i >> 2][i & 3] = (n0 + i * 8 < p.Cs_out) ? __ldg(rrow + i) : make_uint4(0, 0, 0, 0);
+      }
+      int sc_n = 0, sc_iy = 0, sc_ix = 0;
+      if (p.out_kind == 2 && rvalid) {
+        sc_n = em / ohw;
+        const int rem = em - sc_n * ohw;
+        sc_iy = rem / p.OW;
+        sc_ix = rem - sc_iy * p.OW;
+      }
+      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAccBufs) & 1, kErrWaitAccum);
+      if (!ok) *abort_flag = 1;
+      tc_fence_after();
+      uint32_t v[2][32];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        __syncwarp();
+        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * BN + cc * 32, v[cc]);  // warp-collective
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[ab]);
+      if (kSplitable && p.ksplit > 1) {
+        if (ok) {
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc)
+            store_partial(p, v[cc], tk.split, (tk.mn / p.n_tiles) * kBlockM + erow, n0 + cc * 32);
+        }
+        continue;
+      }
+      if (ok && rvalid) {
+        const float* sb = p.out_kind == 2 ? s_bias : s_bias + n0;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const uint4* rp = has_res ? rc[cc] : nullptr;
+          if (p.out_kind == 0)
+            epi_chunk_act<0>(p, v[cc], em, n0, cc * 32, sb, tile_full, rp, sc_n, sc_iy, sc_ix);
+          else if (p.out_kind == 1)
+            epi_chunk_act<1>(p, v[cc], em, n0, cc * 32, sb, tile_full, rp, sc_n, sc_iy, sc_ix);
+          else
+            epi_chunk_act<2>(p, v[cc], em, n0, cc * 32, sb, tile_full, rp, sc_n, sc_iy, sc_ix);
+        }
+      }
+    }
+    } else {
     uint4 res[kResVecs], res_next[kPipeRes ? kResVecs : 1];
     if (kPipeRes) load_res(blockIdx.x, res);
     int lt = 0;
@@ -680,6 +754,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll
         for (int i = 0; i < kResVecs; ++i) res[i] = res_next[kPipeRes ? i : 0];
       }
+    }
     }
   } else if (C::issuer_of(warp) >= 0) {
     // ================================================================ MMA issuer(s)
