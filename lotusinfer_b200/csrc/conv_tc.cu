@@ -121,6 +121,7 @@ struct ConvTcParams {
   int halo_bytes;   // bytes one halo box writes
   int a_rowbytes;   // Cs_in * 2: 32, 64 or 128
   int a_layout;     // tcgen05 descriptor swizzle code of that row width
+  uint32_t wp_magic;  // ceil(2^32 / Wp) (Wp >= 2): q / Wp == __umulhi(q, wp_magic) for q * Wp < 2^32
   int cchunks;      // AMODE 4: 64-channel chunks per pixel (Cs_in / 64)
   // split-K
   int ksplit;       // K splits (1 = none)
@@ -445,6 +446,12 @@ __device__ __forceinline__ void epi_chunk_act(const ConvTcParams& p, const uint3
     epi_chunk<OUT, 2>(p, v, em, n0, cl, sb, full, res, sc_n, sc_iy, sc_ix);
 }
 
+// q / Wp of a padded-grid position: with m = ceil(2^32 / d), floor(q * m /
+// 2^32) == floor(q / d) whenever q * d < 2^32 (here q < 2^17, d <= 256).
+__device__ __forceinline__ int div_wp(const ConvTcParams& p, int q) {
+  return static_cast<int>(__umulhi(static_cast<uint32_t>(q), p.wp_magic));
+}
+
 template <int BN, int STAGES, int AMODE>
 __global__ void __launch_bounds__(Cfg<BN, STAGES, AMODE>::kThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
@@ -584,14 +591,38 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // chains, and the two groups' chains overlap.
     const int grp = warp >> 2;
     const int gx = static_cast<int>(gridDim.x);
+    // halo mode (one N tile): image and tile-in-image of the group's tiles
+    // t0, t0 + 2*gridDim.x, ... kept as counters, no division per tile
+    int w_img = 0, w_ti = 0, g_img = 0, g_ti = 0;
+    if (AMODE == 3) {
+      const int t0 = static_cast<int>(blockIdx.x) + grp * gx;
+      w_img = t0 / p.tpi;
+      w_ti = t0 - w_img * p.tpi;
+      g_img = (2 * gx) / p.tpi;
+      g_ti = 2 * gx - g_img * p.tpi;
+    }
     int lt = grp;
     for (int t = static_cast<int>(blockIdx.x) + grp * gx; t < p.tiles; t += 2 * gx, lt += 2) {
       const TileK tk = kSplitable ? tile_k(p, t) : TileK{t, 0, 0, p.KB};
-      const int n0 = (tk.mn % p.n_tiles) * BN;
+      const int n0 = AMODE == 3 ? 0 : (tk.mn % p.n_tiles) * BN;
       const int ab = lt % C::kAccBufs;
       int em;
       bool rvalid;
-      row_of(t, em, rvalid);
+      if (AMODE == 3) {
+        const int q = w_ti * kBlockM + erow;
+        const int oy = div_wp(p, q);
+        const int ox = q - oy * p.Wp;
+        rvalid = oy < p.OH && ox < p.OW;
+        em = (w_img * p.OH + oy) * p.OW + ox;
+        w_ti += g_ti;
+        w_img += g_img;
+        if (w_ti >= p.tpi) {
+          w_ti -= p.tpi;
+          ++w_img;
+        }
+      } else {
+        row_of(t, em, rvalid);
+      }
       const bool tile_full = n0 + BN <= p.Cout;
       // residual rows of both 32-column chunks, read ahead of the accumulator wait
       uint4 rc[2][4];
@@ -1180,11 +1211,12 @@ static int make_tmap_halo(CUtensorMap* map, const ConvTcArgs& a, int n_img, int 
 // 32 or 64, one N tile, weights plus two halo buffers within kHaloRegion).
 static double halo_plan(const ConvTcArgs& a, int bn, ConvTcParams* p) {
   const int wp = a.W + 2 * a.pw;
-  if (a.sh != 1 || a.sw != 1 || a.out_kind == 2 || a.n_cols > bn) return 0.0;
+  if (a.sh != 1 || a.sw != 1 || a.out_kind == 2 || a.n_cols > bn || wp < 2) return 0.0;
   if (a.Cs_in != 16 && a.Cs_in != 32 && a.Cs_in != 64) return 0.0;
   if (wp > 256 || a.OW != wp - a.kw + 1 || a.k_pad % kBlockK != 0) return 0.0;
   const long q = static_cast<long>(a.OH) * wp;
   const int tpi = static_cast<int>((q + kBlockM - 1) / kBlockM);
+  if (static_cast<long long>(tpi) * kBlockM * wp >= (1ll << 32)) return 0.0;  // div_wp's exact range
   int max_off = 0;
   for (int j = 0; j < tpi; ++j) max_off = std::max(max_off, (j * kBlockM) % wp);
   const int rows = (max_off + (a.kh - 1) * wp + (a.kw - 1) + kBlockM - 1) / wp + 1;
@@ -1204,6 +1236,7 @@ static double halo_plan(const ConvTcArgs& a, int bn, ConvTcParams* p) {
   p->halo_bytes = halo_bytes;
   p->a_rowbytes = rb;
   p->a_layout = rb == 32 ? 6 : (rb == 64 ? 4 : 2);
+  p->wp_magic = static_cast<uint32_t>(((1ull << 32) + wp - 1) / wp);
   return static_cast<double>(a.OH) * a.OW / (static_cast<double>(tpi) * kBlockM);
 }
 
