@@ -801,8 +801,28 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       bool ok = true;
       // AMODE 3: the resident weights land once, on full[0]
       if (AMODE == 3 && p.tiles > static_cast<int>(blockIdx.x)) ok = mbar_wait_relaxed(&full[0], 0, kErrWaitFull);
+      // AMODE 3: tile-in-image, halo buffer and its phase of tile lt, and
+      // lt % n_iss, kept as counters (no division per tile)
+      int w_ti = 0, g_ti = 0, h_slot = 0, h_phase = 0, rr = 0;
+      if (AMODE == 3) {
+        w_ti = static_cast<int>(blockIdx.x) % p.tpi;
+        g_ti = static_cast<int>(gridDim.x) % p.tpi;
+      }
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++lt) {
-        if (C::kMmaIssuers > 1 && lt % n_iss != issuer) continue;
+        const int c_ti = w_ti, c_slot = h_slot, c_phase = h_phase;
+        if (AMODE == 3) {
+          w_ti += g_ti;
+          if (w_ti >= p.tpi) w_ti -= p.tpi;
+          if (++h_slot == p.halo_slots) {
+            h_slot = 0;
+            h_phase ^= 1;
+          }
+        }
+        if (C::kMmaIssuers > 1) {
+          const bool mine = rr == issuer;  // rr == lt % n_iss
+          if (++rr == n_iss) rr = 0;
+          if (!mine) continue;
+        }
         const int ab = lt % C::kAccBufs;
         // no shared-memory loads (the abort flag included) in this loop: one
         // issued behind queued MMAs waits for them to drain; the waits are
@@ -815,8 +835,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * BN;
         if (AMODE == 3) {
-          const int hs = lt % p.halo_slots;
-          if (!mbar_wait_relaxed(&hfull[hs], (lt / p.halo_slots) & 1, kErrWaitFull)) {
+          const int hs = c_slot;
+          if (!mbar_wait_relaxed(&hfull[hs], static_cast<uint32_t>(c_phase), kErrWaitFull)) {
             ok = false;
             break;
           }
@@ -824,10 +844,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           // descriptors are built once per tile; a tap or K step only moves
           // the start-address field (16-byte units in the low bits; every
           // address stays below 232448 bytes, so the 14-bit field cannot carry)
-          const int q0 = ((t / p.n_tiles) % p.tpi) * kBlockM;
+          const int q0 = c_ti * kBlockM;
           const uint32_t rb = static_cast<uint32_t>(p.a_rowbytes);
-          const uint64_t a_desc = make_sdesc_rows(
-              smem_u32(sA) + p.halo_off + hs * p.halo_stride + static_cast<uint32_t>(q0 % p.Wp) * rb, rb, p.a_layout);
+          const uint32_t ox0 = static_cast<uint32_t>(q0 - div_wp(p, q0) * p.Wp);  // q0 % Wp
+          const uint64_t a_desc =
+              make_sdesc_rows(smem_u32(sA) + p.halo_off + hs * p.halo_stride + ox0 * rb, rb, p.a_layout);
           const uint64_t b_desc = make_sdesc_sw128(smem_u32(sA));
           const int csub = p.Cs_in >> 4;  // K=16 slices per tap
           const uint32_t row16 = rb >> 4, wp16 = static_cast<uint32_t>(p.Wp) * row16;
@@ -917,17 +938,30 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         mbar_arrive_expect_tx(&full[0], static_cast<uint32_t>(p.KB) * C::kBBytes);
         for (int kb = 0; kb < p.KB; ++kb) tma_load_2d(sA + kb * C::kBBytes, &tmap_w, &full[0], kb * kBlockK, 0);
         int lt = 0;
+        // image, tile-in-image, halo buffer and phase of tile lt as counters
+        int img = static_cast<int>(blockIdx.x) / p.tpi;
+        int ti = static_cast<int>(blockIdx.x) - img * p.tpi;
+        const int g_img = static_cast<int>(gridDim.x) / p.tpi;
+        const int g_ti = static_cast<int>(gridDim.x) - g_img * p.tpi;
+        int hs = 0, hph = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
-          const int hs = lt % p.halo_slots;
-          if (*abort_flag || !mbar_wait(&hempty[hs], ((lt / p.halo_slots) & 1) ^ 1, kErrWaitEmpty)) {
+          if (*abort_flag || !mbar_wait(&hempty[hs], static_cast<uint32_t>(hph ^ 1), kErrWaitEmpty)) {
             ok = false;
             break;
           }
-          const int mt = t / p.n_tiles;
-          const int img = mt / p.tpi;
-          const int q0 = (mt - img * p.tpi) * kBlockM;
+          const int q0 = ti * kBlockM;
           mbar_arrive_expect_tx(&hfull[hs], static_cast<uint32_t>(p.halo_bytes));
-          tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], 0, -p.pw, q0 / p.Wp - p.ph, img);
+          tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], 0, -p.pw, div_wp(p, q0) - p.ph, img);
+          ti += g_ti;
+          img += g_img;
+          if (ti >= p.tpi) {
+            ti -= p.tpi;
+            ++img;
+          }
+          if (++hs == p.halo_slots) {
+            hs = 0;
+            hph ^= 1;
+          }
         }
         // before the CTA may exit (an abort included), every TMA load this
         // thread issued has landed: the weights, and the last load of each
