@@ -318,6 +318,7 @@ def test_gemv_reference_semantics_fp32(shape):
     ("alexnet_3x3_s2", 2, 64, 55, 55, 3, 2, 0),
     ("ref_test_9x9_s2_p4", 1, 3, 65, 65, 9, 2, 4),
     ("3x3_s2_p1_c12_odd_sizes", 3, 12, 37, 29, 3, 2, 1),
+    ("3x3_s2_p1_c8_tiny", 2, 8, 2, 3, 3, 2, 1),
 ], ids=lambda c: c[0])
 def test_maxpool_exact(case):
     K = _k()
