@@ -102,7 +102,11 @@ class ClockSampler:
 
 
 def cpu_baseline_sample(seconds_budget: float = 20.0):
-    """The oracle's ResNet-18 on all host threads over a bounded image sample."""
+    """The oracle's ResNet-18 on all host threads over a bounded image sample.
+
+    Returns the baseline record and the oracle's logits of the first n images
+    of the seed-0 batch (the images rank 0 benchmarks), which the parity
+    check reuses."""
     from lotusinfer_b200 import synth
     from oracle import oracle
     param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
@@ -116,10 +120,32 @@ def cpu_baseline_sample(seconds_budget: float = 20.0):
     n = int(max(1, min(16, (seconds_budget - t1) / max(t1, 1e-3))))
     x = synth.synthetic_input("resnet18", n, seed=0)
     t0 = time.perf_counter()
-    oracle.run_graph(param, binp, x, weights=w)
+    want = oracle.run_graph(param, binp, x, weights=w)
     dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"ResNet-18 forward over {n} of the 256 synthetic images (fp32 oracle, OpenMP)"}
+    return ({"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+             "sample": f"ResNet-18 forward over {n} of the 256 synthetic images (fp32 oracle, OpenMP)"}, want)
+
+
+def oracle_logits(n: int):
+    """The oracle's ResNet-18 logits of the first n images of the seed-0 batch."""
+    from lotusinfer_b200 import synth
+    from oracle import oracle
+    param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
+    return oracle.run_graph(param, binp, synth.synthetic_input("resnet18", n, seed=0))
+
+
+def parity_check(got, want):
+    """Benchmarked logits of the first images against the oracle's: max-abs,
+    max-abs over the oracle's largest magnitude, rel-L2 and top-1 agreement."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    err = float(np.abs(got - want).max())
+    srt = np.sort(want, axis=1)
+    return {"images": int(want.shape[0]), "reference": "CPU oracle (fp32), first images of rank 0's batch",
+            "max_abs": err, "norm_max_abs": err / float(np.abs(want).max()),
+            "rel_l2": float(np.linalg.norm(got - want) / np.linalg.norm(want)),
+            "top1_equal": int(np.sum(np.argmax(got, 1) == np.argmax(want, 1))),
+            "min_oracle_margin": float((srt[:, -1] - srt[:, -2]).min())}
 
 
 def run_reference(args):
@@ -180,10 +206,12 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        # rank 0's stdout carries exactly one JSON line: NCCL's version banner
-        # (NCCL_DEBUG=VERSION) would land there too, so keep it at warnings
+        # communicator set-up lines (rank counts) go to stderr; rank 0's
+        # stdout carries exactly one JSON line
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-            os.environ["NCCL_DEBUG"] = "WARN"
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
 
     B = args.batch
@@ -299,10 +327,17 @@ def main():
             "roofline": roofline, "clocks": clocks, "e2e": e2e,
             "gpu_launches": g.launches_per_forward() * args.steps,
             "layer_ms": {l["name"]: round(t, 4) for t, l in zip(layer_ms, layers)}}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_sample()
-    elif rank == 0:
-        line["cpu_baseline"] = None
+    if rank == 0:
+        # correctness at the benchmarked configuration: the first images of the
+        # last e2e step's logits (rank 0's seed-0 batch) against the oracle
+        want = None
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"], want = cpu_baseline_sample()
+        else:
+            line["cpu_baseline"] = None
+        if want is None:
+            want = oracle_logits(4)
+        line["parity"] = parity_check(logits_host.numpy()[:want.shape[0]], want)
     assert abi.device_error() == 0
     g.close()
     if world > 1:

@@ -53,7 +53,11 @@ int lotus_graph_get_output(lotus_graph* g, float* dst, size_t count, cudaStream_
 int lotus_graph_forward(lotus_graph* g, cudaStream_t stream);
 /* Reference Graph::Forward(): forward on the graph stream and wait. */
 int lotus_graph_forward_sync(lotus_graph* g);
-/* Wait for all work queued on the graph stream. */
+/* Wait for all work queued on the graph stream.  Both waiting calls also read
+ * (and clear) the device error word: if a kernel's bounded wait expired, its
+ * output tiles were skipped, and the call returns LOTUS_ERR_CUDA naming the
+ * code instead of reporting success.  Work queued with lotus_graph_forward
+ * reports such an error at the next waiting call. */
 int lotus_graph_synchronize(lotus_graph* g);
 
 /* Introspection for profiling and tests. */

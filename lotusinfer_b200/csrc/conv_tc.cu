@@ -77,6 +77,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "kernels.h"
@@ -130,6 +131,13 @@ struct ConvTcParams {
   float* ws;        // [ksplit][ws_rows][ws_ld] fp32 partial sums
   int ws_rows;      // m_tiles * 128
   int ws_ld;        // n_tiles * BN
+  // bounded waits: try_wait rounds before a wait gives up (kMaxWaitIters
+  // unless LOTUS_WAIT_LIMIT says otherwise)
+  uint32_t wait_limit;
+  // test hook (LOTUS_TEST_WITHHOLD_ARRIVAL=1): CTA 0's producer skips its
+  // first stage load, so the consumer's bounded wait must run out and the
+  // kernel must report it and return; no fault and no unbounded wait
+  int withhold_arrival;
 };
 
 // Output tile and K-block range of tile t (split-K: t = split * mn_tiles + mn).
@@ -639,7 +647,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         sc_iy = rem / p.OW;
         sc_ix = rem - sc_iy * p.OW;
       }
-      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAccBufs) & 1, kErrWaitAccum);
+      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAccBufs) & 1, kErrWaitAccum, p.wait_limit);
       if (!ok) *abort_flag = 1;
       tc_fence_after();
       uint32_t v[2][32];
@@ -697,7 +705,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         sc_iy = rem / p.OW;
         sc_ix = rem - sc_iy * p.OW;
       }
-      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAccBufs) & 1, kErrWaitAccum);
+      const bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAccBufs) & 1, kErrWaitAccum, p.wait_limit);
       if (!ok) *abort_flag = 1;
       tc_fence_after();
       if (kChunked) {
@@ -800,7 +808,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       int lt = 0;
       bool ok = true;
       // AMODE 3: the resident weights land once, on full[0]
-      if (AMODE == 3 && p.tiles > static_cast<int>(blockIdx.x)) ok = mbar_wait_relaxed(&full[0], 0, kErrWaitFull);
+      if (AMODE == 3 && p.tiles > static_cast<int>(blockIdx.x)) ok = mbar_wait_relaxed(&full[0], 0, kErrWaitFull, p.wait_limit);
       // AMODE 3: tile-in-image, halo buffer and its phase of tile lt, and
       // lt % n_iss, kept as counters (no division per tile)
       int w_ti = 0, g_ti = 0, h_slot = 0, h_phase = 0, rr = 0;
@@ -828,7 +836,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         // issued behind queued MMAs waits for them to drain; the waits are
         // relaxed for the same reason.  A stalled peer still ends the loop
         // through the bounded waits.
-        if (!mbar_wait_relaxed(&tempty[ab], ((lt / C::kAccBufs) & 1) ^ 1, kErrWaitAccum)) {
+        if (!mbar_wait_relaxed(&tempty[ab], ((lt / C::kAccBufs) & 1) ^ 1, kErrWaitAccum, p.wait_limit)) {
           ok = false;
           break;
         }
@@ -836,7 +844,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const uint32_t d_tmem = tmem_base + ab * BN;
         if (AMODE == 3) {
           const int hs = c_slot;
-          if (!mbar_wait_relaxed(&hfull[hs], static_cast<uint32_t>(c_phase), kErrWaitFull)) {
+          if (!mbar_wait_relaxed(&hfull[hs], static_cast<uint32_t>(c_phase), kErrWaitFull, p.wait_limit)) {
             ok = false;
             break;
           }
@@ -872,7 +880,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           const int taps = p.kh * p.kw;
           for (int cc = 0; cc < p.cchunks && ok; ++cc, ++hc) {
             const int hs = issuer * kHalo4Slots + static_cast<int>(hc % kHalo4Slots);
-            if (!mbar_wait_relaxed(&hfull[hs], (hc / kHalo4Slots) & 1, kErrWaitFull)) {
+            if (!mbar_wait_relaxed(&hfull[hs], (hc / kHalo4Slots) & 1, kErrWaitFull, p.wait_limit)) {
               ok = false;
               break;
             }
@@ -880,7 +888,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             int r = 0, sx = 0;
             for (int tap = 0; tap < taps; ++tap, ++it) {
               const int st = issuer * C::kRingStages + static_cast<int>(it % C::kRingStages);
-              if (!mbar_wait_relaxed(&full[st], (it / C::kRingStages) & 1, kErrWaitFull)) {
+              if (!mbar_wait_relaxed(&full[st], (it / C::kRingStages) & 1, kErrWaitFull, p.wait_limit)) {
                 ok = false;
                 break;
               }
@@ -905,7 +913,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const int nkb = tile_k(p, t).nkb;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int st = issuer * C::kRingStages + static_cast<int>(it % C::kRingStages);
-          if (!mbar_wait_relaxed(&full[st], (it / C::kRingStages) & 1, kErrWaitFull)) {
+          if (!mbar_wait_relaxed(&full[st], (it / C::kRingStages) & 1, kErrWaitFull, p.wait_limit)) {
             ok = false;
             break;
           }
@@ -924,7 +932,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       if (!ok) *abort_flag = 1;
       // every MMA this thread issued has completed once mma_done fires
       umma_commit(mma_done);
-      mbar_wait(mma_done, 0, kErrWaitFull);
+      mbar_wait(mma_done, 0, kErrWaitFull, p.wait_limit);
     }
   } else if (warp == C::kTmaWarp || (C::kRings == 2 && warp == C::kTmaWarp2)) {
     // ================================================================ TMA producer(s)
@@ -945,13 +953,17 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const int g_ti = static_cast<int>(gridDim.x) - g_img * p.tpi;
         int hs = 0, hph = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
-          if (*abort_flag || !mbar_wait(&hempty[hs], static_cast<uint32_t>(hph ^ 1), kErrWaitEmpty)) {
+          if (*abort_flag || !mbar_wait(&hempty[hs], static_cast<uint32_t>(hph ^ 1), kErrWaitEmpty, p.wait_limit)) {
             ok = false;
             break;
           }
           const int q0 = ti * kBlockM;
-          mbar_arrive_expect_tx(&hfull[hs], static_cast<uint32_t>(p.halo_bytes));
-          tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], 0, -p.pw, div_wp(p, q0) - p.ph, img);
+          // test hook: CTA 0's first halo buffer never fills
+          if (!(p.withhold_arrival && blockIdx.x == 0 && lt == 0)) {
+            mbar_arrive_expect_tx(&hfull[hs], static_cast<uint32_t>(p.halo_bytes));
+            tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], 0, -p.pw, div_wp(p, q0) - p.ph,
+                        img);
+          }
           ti += g_ti;
           img += g_img;
           if (ti >= p.tpi) {
@@ -966,9 +978,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         // before the CTA may exit (an abort included), every TMA load this
         // thread issued has landed: the weights, and the last load of each
         // halo buffer (earlier ones were waited for through hempty)
-        mbar_wait(&full[0], 0, kErrWaitFull);
+        mbar_wait(&full[0], 0, kErrWaitFull, p.wait_limit);
         for (int j = lt - 1; j >= 0 && j >= lt - p.halo_slots; --j)
-          mbar_wait(&hfull[j % p.halo_slots], (j / p.halo_slots) & 1, kErrWaitFull);
+          mbar_wait(&hfull[j % p.halo_slots], (j / p.halo_slots) & 1, kErrWaitFull, p.wait_limit);
       }
       if (AMODE == 4) {
         // halo chunk h of this pipeline: tile lt = ring + 2 * (h / cchunks), chunk h % cchunks
@@ -984,7 +996,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           const int img = mt / p.tpi;
           const int q0 = (mt - img * p.tpi) * kBlockM;
           const int hs = ring * kHalo4Slots + static_cast<int>(h % kHalo4Slots);
-          if (*abort_flag || !mbar_wait(&hempty[hs], ((h / kHalo4Slots) & 1) ^ 1, kErrWaitEmpty)) return false;
+          if (*abort_flag || !mbar_wait(&hempty[hs], ((h / kHalo4Slots) & 1) ^ 1, kErrWaitEmpty, p.wait_limit)) return false;
           mbar_arrive_expect_tx(&hfull[hs], static_cast<uint32_t>(p.halo_bytes));
           tma_load_4d(sA + p.halo_off + hs * p.halo_stride, &tmap_a, &hfull[hs], cc * kBlockK, -p.pw, q0 / p.Wp - p.ph,
                       img);
@@ -1000,7 +1012,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           for (int cc = 0; cc < p.cchunks && ok; ++cc, ++h) {
             for (int tap = 0; tap < taps; ++tap, ++it) {
               const int st = ring * C::kRingStages + static_cast<int>(it % C::kRingStages);
-              if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kRingStages) & 1) ^ 1, kErrWaitEmpty)) {
+              if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kRingStages) & 1) ^ 1, kErrWaitEmpty, p.wait_limit)) {
                 ok = false;
                 break;
               }
@@ -1017,7 +1029,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
         // the last halo loads of this pipeline have landed before the CTA may exit
         for (int j = static_cast<int>(h_issued) - 1; j >= 0 && j >= static_cast<int>(h_issued) - kHalo4Slots; --j)
-          mbar_wait(&hfull[ring * kHalo4Slots + j % kHalo4Slots], (j / kHalo4Slots) & 1, kErrWaitFull);
+          mbar_wait(&hfull[ring * kHalo4Slots + j % kHalo4Slots], (j / kHalo4Slots) & 1, kErrWaitFull, p.wait_limit);
       }
       int plt = 0;
       for (int t = blockIdx.x; t < p.tiles && ok && AMODE != 3 && AMODE != 4; t += gridDim.x, ++plt) {
@@ -1045,10 +1057,11 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
         for (int kb = tk.kb0; kb < tk.kb0 + tk.nkb; ++kb, ++it) {
           const int st = ring * C::kRingStages + static_cast<int>(it % C::kRingStages);
-          if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kRingStages) & 1) ^ 1, kErrWaitEmpty)) {
+          if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kRingStages) & 1) ^ 1, kErrWaitEmpty, p.wait_limit)) {
             ok = false;
             break;
           }
+          if (p.withhold_arrival && blockIdx.x == 0 && it == 0) continue;  // test hook: stage never fills
           mbar_arrive_expect_tx(&full[st], kTx);
           tma_load_2d(sB + st * C::kBBytes, &tmap_w, &full[st], kb * kBlockK, n0);
           if (AMODE == 1) {
@@ -1073,7 +1086,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         // (the last kRingStages stages; earlier ones were waited for through
         // their empty barriers)
         for (int j = static_cast<int>(it) - 1; j >= 0 && j >= static_cast<int>(it) - C::kRingStages; --j)
-          mbar_wait(&full[ring * C::kRingStages + j % C::kRingStages], (j / C::kRingStages) & 1, kErrWaitFull);
+          mbar_wait(&full[ring * C::kRingStages + j % C::kRingStages], (j / C::kRingStages) & 1, kErrWaitFull, p.wait_limit);
       }
     }
   } else if (AMODE == 0) {
@@ -1111,7 +1124,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       }
       for (int kb = tk.kb0; kb < tk.kb0 + tk.nkb; ++kb, ++it) {
         const int st = it % STAGES;
-        if (*abort_flag || !mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, kErrWaitEmpty)) {
+        if (*abort_flag || !mbar_wait(&empty[st], ((it / STAGES) & 1) ^ 1, kErrWaitEmpty, p.wait_limit)) {
           ok = false;
           break;
         }
@@ -1163,6 +1176,30 @@ static void* driver_fn(const char* name) {
   if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
     return ptr;
   return nullptr;
+}
+
+constexpr int kMaxDevices = 64;
+
+// Process-unique id of the calling thread's current CUDA context (cuCtxGetId),
+// 0 if there is none or the driver does not say.  Per-device caches compare
+// it to notice a context that was destroyed and recreated (cudaDeviceReset).
+uint64_t current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    get_current = reinterpret_cast<GetCurrent>(driver_fn("cuCtxGetCurrent"));
+    get_id = reinterpret_cast<GetId>(driver_fn("cuCtxGetId"));
+  });
+  if (!get_current || !get_id) return 0;
+  // no runtime call that could initialise a context here: this runs inside
+  // stream captures, where such calls are not allowed
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&c) != CUDA_SUCCESS || c == nullptr || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return static_cast<uint64_t>(id);
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
@@ -1306,6 +1343,15 @@ static double halo4_plan(const ConvTcArgs& a, int bn, int stages, ConvTcParams* 
   return static_cast<double>(a.OH) * a.OW / (static_cast<double>(tpi) * kBlockM);
 }
 
+// Bounded-wait limit of a launch: LOTUS_WAIT_LIMIT try_wait rounds (1 .. 2^30)
+// when set, kMaxWaitIters otherwise.
+uint32_t wait_limit_from_env() {
+  const char* e = std::getenv("LOTUS_WAIT_LIMIT");
+  if (!e) return kMaxWaitIters;
+  const long v = std::atol(e);
+  return (v >= 1 && v <= (1L << 30)) ? static_cast<uint32_t>(v) : kMaxWaitIters;
+}
+
 // Split-K reduction: y[m, c] = act(bias[c] + sum_s ws[s][m][c] (+ residual)),
 // eight channels per thread, summed in split order (deterministic).  NHWC
 // fp16 output (pad channels written as zero) or fp32 rows.
@@ -1366,13 +1412,15 @@ static int split_count(long mn, int kb_total, int sms, int* kbs) {
   return (kb_total + *kbs - 1) / *kbs;
 }
 
+// SM count of the current device, cached per device ordinal.
 static int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -1384,13 +1432,19 @@ static cudaError_t launch_impl(const CUtensorMap& mw, const CUtensorMap& ma, con
   static_assert(C::bytes(AMODE == 0 ? kMaxTable : 0) <= 232448, "dynamic shared memory above 227 KB");
   const int smem = C::bytes(AMODE == 0 ? p.KB * 8 : 0);
   auto kern = conv_tc_kernel<BN, STAGES, AMODE>;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::bytes(AMODE == 0 ? kMaxTable : 0));
-  });
-  if (attr_err != cudaSuccess) return attr_err;
+  // the shared-memory opt-in is a property of the function in one context:
+  // set it once per device and again whenever that device's context changed
+  // (a cudaDeviceReset creates a new one)
+  static std::atomic<uint64_t> attr_ctx[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  const uint64_t ctx = current_context_id();
+  if (ctx == 0 || attr_ctx[dev].load(std::memory_order_acquire) != ctx) {
+    const cudaError_t ae = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                C::bytes(AMODE == 0 ? kMaxTable : 0));
+    if (ae != cudaSuccess) return ae;
+    attr_ctx[dev].store(ctx, std::memory_order_release);
+  }
   const int grid = p.tiles < num_sms() ? p.tiles : num_sms();
   kern<<<grid, C::kThreads, smem, stream>>>(mw, ma, p);
   note_launch();
@@ -1428,6 +1482,9 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, s
   p.t_pw = a.t_pw;
   p.t_kw = a.t_kw;
   p.t_cout = a.t_cout;
+  p.wait_limit = wait_limit_from_env();
+  const char* wh = std::getenv("LOTUS_TEST_WITHHOLD_ARRIVAL");
+  p.withhold_arrival = (wh && std::atoi(wh) == 1) ? 1 : 0;
 
   int bn = a.block_n;
   if (bn == 0) {
@@ -1569,17 +1626,20 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, s
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
 int conv_tc_noalloc_scratch(float** ptr, const char** err) {
-  constexpr int kMaxDevices = 64;
   static std::mutex mu;
   static float* addr[kMaxDevices] = {};
+  static uint64_t addr_ctx[kMaxDevices] = {};
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     *err = "no usable current CUDA device";
     return -3;
   }
+  const uint64_t ctx = current_context_id();
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    // once per device, with that device current (the caller's current device)
+  // once per device, with that device current (the caller's current device),
+  // and again when the device's context was recreated (after a
+  // cudaDeviceReset the module and with it the scratch live elsewhere)
+  if (addr[dev] == nullptr || ctx == 0 || addr_ctx[dev] != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -1587,6 +1647,7 @@ int conv_tc_noalloc_scratch(float** ptr, const char** err) {
       return -3;
     }
     addr[dev] = static_cast<float*>(p);
+    addr_ctx[dev] = ctx;
   }
   *ptr = addr[dev];
   return 0;

@@ -27,7 +27,9 @@ enum : int {
 };
 
 // One try_wait may suspend for a hardware-defined interval before it
-// returns false; 1<<22 attempts bound a lost arrival to a few seconds.
+// returns false; 1<<22 attempts bound a lost arrival to a few seconds.  The
+// kernels take their limit as a launch parameter (this value by default), so
+// that a test can shorten it and make a withheld arrival expire quickly.
 constexpr uint32_t kMaxWaitIters = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -71,8 +73,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err_code) {
-  for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err_code,
+                                          uint32_t limit = kMaxWaitIters) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
   atomicExch(&g_lotus_device_error, err_code);
@@ -98,8 +101,9 @@ __device__ __forceinline__ bool mbar_try_wait_relaxed(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_wait_relaxed(uint64_t* bar, uint32_t parity, int err_code) {
-  for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
+__device__ __forceinline__ bool mbar_wait_relaxed(uint64_t* bar, uint32_t parity, int err_code,
+                                                  uint32_t limit = kMaxWaitIters) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait_relaxed(bar, parity)) return true;
   }
   atomicExch(&g_lotus_device_error, err_code);

@@ -4,6 +4,11 @@
 #include <queue>
 #include <set>
 #include <stdexcept>
+#include <string>
+
+namespace lotus_impl {
+int read_device_error();  // conv_tc.cu: returns and clears the device error word (-1: unreadable)
+}
 
 namespace lotus {
 
@@ -371,7 +376,18 @@ void Graph::ForwardAsync(cudaStream_t stream) {
 
 void Graph::Forward() {
   ForwardAsync(stream_);
-  CudaCheck(cudaStreamSynchronize(stream_), "Forward");
+  Synchronize();
+}
+
+void Graph::Synchronize() {
+  CudaCheck(cudaSetDevice(device_), "cudaSetDevice");
+  CudaCheck(cudaStreamSynchronize(stream_), "graph synchronize");
+  // a kernel whose bounded wait ran out skipped its output tiles: report it
+  // instead of handing back wrong results as a success
+  const int dev_err = lotus_impl::read_device_error();
+  if (dev_err != 0)
+    throw std::runtime_error("a kernel's bounded wait expired (device error code " + std::to_string(dev_err) +
+                             "); the outputs of this forward are invalid");
 }
 
 std::vector<float> Graph::ProfileLayers(int reps) {

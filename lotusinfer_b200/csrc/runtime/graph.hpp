@@ -46,6 +46,9 @@ class Graph {
   void Forward();
   // Enqueues the forward pass on `stream` (nullptr = the graph's own stream).
   void ForwardAsync(cudaStream_t stream = nullptr);
+  // Waits for the graph stream; throws if a kernel reported an expired
+  // bounded wait (its outputs are then invalid).
+  void Synchronize();
 
   Tensor& InputTensor() { return operands_.at(input_operand_)->tensor_; }
   Tensor& OutputTensor() { return operands_.at(output_operand_)->tensor_; }

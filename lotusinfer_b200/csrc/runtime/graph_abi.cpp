@@ -109,8 +109,11 @@ int lotus_graph_forward_sync(lotus_graph* g) {
 
 int lotus_graph_synchronize(lotus_graph* g) {
   if (!g) return lotus_impl::set_error(LOTUS_ERR_INVALID, "null graph");
-  const cudaError_t e = cudaStreamSynchronize(g->g->Stream());
-  if (e != cudaSuccess) return lotus_impl::set_error(LOTUS_ERR_CUDA, cudaGetErrorString(e));
+  try {
+    g->g->Synchronize();
+  } catch (const std::exception& e) {
+    return lotus_impl::set_error(LOTUS_ERR_CUDA, std::string("graph_synchronize: ") + e.what());
+  }
   return lotus_impl::set_error(LOTUS_OK, "");
 }
 

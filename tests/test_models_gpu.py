@@ -1,11 +1,22 @@
 """Whole-network parity: the native graph runtime against the CPU oracle's
 graph runner on the same synthetic PNNX model files.
 
-Per-network tolerance: logits/masks within max-abs 5e-2 and rel-L2 5e-3 of the
-fp32 oracle (activations are stored as fp16 between layers, so per-layer
-rounding compounds over 18-23 layers); ResNet-18 / AlexNet top-1 identical on
-every image whose oracle top-1/top-2 margin exceeds 10x the measured max-abs
-error; U-Net masks (sigmoid > 0.5) identical outside the same band.
+Tolerance, stated against the scale of the output (random Kaiming weights
+with no normalisation give ResNet-18 logits up to ~250 in magnitude, and
+activations are stored as fp16 between 18-23 layers, whose rounding
+compounds):
+  * logits: max|got - want| <= NET_NORM_MAX_ABS * max|want| and
+    rel-L2 <= NET_REL_L2;
+  * top-1 class identical on EVERY checked image (no exclusion band; a
+    mismatch reports the oracle's top-1/top-2 margin);
+  * U-Net masks (sigmoid > 0.5): identical on every pixel whose oracle
+    probability is farther from 0.5 than the measured max-abs error; the
+    pixels inside that band are counted and at most one in ten thousand may
+    flip.
+Batch sizes: ResNet-18 at 1/32/256 (256 is the benchmarked workload), U-Net
+at 1/16, AlexNet at 1/32/256 plus 2 and 12.  Images are independent (BatchNorm is
+folded), so at the large batches a fixed slice of the output rows, spread over
+the whole batch, is compared with the oracle run on the same images.
 """
 import numpy as np
 import pytest
@@ -15,8 +26,9 @@ from tests._metrics import max_abs, rel_l2
 
 pytestmark = pytest.mark.gpu
 
-NET_MAX_ABS = 5e-2
+NET_NORM_MAX_ABS = 5e-3
 NET_REL_L2 = 5e-3
+SLICE = 16  # oracle images per large-batch check
 
 
 @pytest.fixture(scope="module")
@@ -31,28 +43,47 @@ def _graph(name, model_dir, batch, **kw):
     return Graph(param, binp, batch, **kw), param, binp
 
 
-def _top1_check(got, want):
+def _slice(batch, n=SLICE):
+    """Image indices checked against the oracle: all of a small batch, else
+    n indices spread from the first to the last image."""
+    if batch <= n:
+        return np.arange(batch)
+    return np.unique(np.linspace(0, batch - 1, n).round().astype(int))
+
+
+def _check_logits(got, want, what):
+    scale = float(np.abs(want).max())
     err = max_abs(got, want)
+    rl = rel_l2(got, want)
+    assert err <= NET_NORM_MAX_ABS * scale, f"{what}: max_abs {err:.3e} > {NET_NORM_MAX_ABS} x {scale:.1f}"
+    assert rl <= NET_REL_L2, f"{what}: rel_l2 {rl:.3e}"
     srt = np.sort(want, axis=1)
     margin = srt[:, -1] - srt[:, -2]
-    decisive = margin > 10 * err
-    same = np.argmax(got, 1) == np.argmax(want, 1)
-    assert np.all(same[decisive]), (margin, err)
-    return int(decisive.sum()), int(same.sum())
+    g1, w1 = np.argmax(got, 1), np.argmax(want, 1)
+    bad = np.nonzero(g1 != w1)[0]
+    assert bad.size == 0, (f"{what}: top-1 differs on rows {bad.tolist()} (oracle margins "
+                           f"{margin[bad].tolist()}, max_abs error {err:.3e})")
+    return err, rl
 
 
-@pytest.mark.parametrize("batch", [1, 4])
-def test_resnet18_matches_oracle(model_dir, batch):
+def _run_slice(name, model_dir, batch, seed=0, n=SLICE):
     from lotusinfer_b200 import synth
-    g, param, binp = _graph("resnet18", model_dir, batch)
-    x = synth.synthetic_input("resnet18", batch, seed=0)
+    g, param, binp = _graph(name, model_dir, batch)
+    x = synth.synthetic_input(name, batch, seed=seed)
     got = g.run(x)
-    want = oracle.run_graph(param, binp, x)
-    assert got.shape == want.shape == (batch, 1000)
-    assert max_abs(got, want) <= NET_MAX_ABS * max(1.0, float(np.abs(want).max()) / 10)
-    assert rel_l2(got, want) <= NET_REL_L2, rel_l2(got, want)
-    _top1_check(got, want)
     g.close()
+    idx = _slice(batch, n)
+    want = oracle.run_graph(param, binp, np.ascontiguousarray(x[idx]))
+    return got[idx], want
+
+
+@pytest.mark.parametrize("batch", [1, 4, 32, 256])
+def test_resnet18_matches_oracle(model_dir, batch):
+    """bs256 is the benchmarked configuration; 1 and 32 are the other
+    configured batches, 4 a small odd one."""
+    got, want = _run_slice("resnet18", model_dir, batch)
+    assert got.shape == want.shape
+    _check_logits(got, want, f"resnet18 bs{batch}")
 
 
 def test_resnet18_cuda_graph_replay_and_fusion_equivalence(model_dir):
@@ -75,32 +106,25 @@ def test_resnet18_cuda_graph_replay_and_fusion_equivalence(model_dir):
     g2.close()
 
 
-def test_unet_matches_oracle(model_dir):
-    from lotusinfer_b200 import synth
-    g, param, binp = _graph("unet", model_dir, 1)
-    x = synth.synthetic_input("unet", 1, seed=0)
-    got = g.run(x)
-    want = oracle.run_graph(param, binp, x)
-    assert got.shape == want.shape == (1, 1, 256, 256)
+@pytest.mark.parametrize("batch", [1, 16])
+def test_unet_matches_oracle(model_dir, batch):
+    got, want = _run_slice("unet", model_dir, batch, n=4)  # 4 oracle images: ~100 GFLOP on the CPU
+    assert got.shape == want.shape and got.shape[1:] == (1, 256, 256)
     err = max_abs(got, want)
-    assert err <= NET_MAX_ABS and rel_l2(got, want) <= NET_REL_L2, (err, rel_l2(got, want))
-    band = np.abs(want - 0.5) <= 10 * err
-    assert np.array_equal((got > 0.5)[~band], (want > 0.5)[~band])
-    g.close()
+    assert err <= NET_NORM_MAX_ABS and rel_l2(got, want) <= NET_REL_L2, (err, rel_l2(got, want))
+    band = np.abs(want - 0.5) <= err
+    flips = (got > 0.5) != (want > 0.5)
+    assert not np.any(flips[~band]), f"mask differs outside the {err:.2e} band: {int(flips[~band].sum())} pixels"
+    assert flips.sum() <= max(1, flips.size // 10000), f"{int(flips.sum())} of {flips.size} pixels flipped"
 
 
-@pytest.mark.parametrize("batch", [2, 12])
+@pytest.mark.parametrize("batch", [1, 2, 12, 32, 256])
 def test_alexnet_matches_oracle(model_dir, batch):
-    """batch 2 runs the FC layers on the GEMV path, batch 12 on the tcgen05 GEMM."""
-    from lotusinfer_b200 import synth
-    g, param, binp = _graph("alexnet", model_dir, batch)
-    x = synth.synthetic_input("alexnet", batch, seed=0)
-    got = g.run(x)
-    want = oracle.run_graph(param, binp, x)
-    assert got.shape == want.shape == (batch, 1000)
-    assert rel_l2(got, want) <= NET_REL_L2, rel_l2(got, want)
-    _top1_check(got, want)
-    g.close()
+    """batch <= 8 runs the FC layers on the GEMV path, larger batches on the
+    tcgen05 GEMM (split-K at the smaller ones)."""
+    got, want = _run_slice("alexnet", model_dir, batch)
+    assert got.shape == want.shape
+    _check_logits(got, want, f"alexnet bs{batch}")
 
 
 S2D_STEM = {"resnet18": 2, "alexnet": 4}  # stem stride = space-to-depth factor
