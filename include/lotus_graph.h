@@ -26,6 +26,7 @@ typedef struct lotus_graph lotus_graph;
 #define LOTUS_GRAPH_NO_CUDA_GRAPH 1     /* flags: launch layers eagerly on every forward */
 #define LOTUS_GRAPH_NO_RESIDUAL_FUSION 2 /* flags: keep pnnx.Expression add as its own kernel */
 #define LOTUS_GRAPH_NO_S2D_STEM 4        /* flags: run a strided 3-channel stem conv directly */
+#define LOTUS_GRAPH_NO_POOL_FUSION 8     /* flags: keep a max pool after a conv as its own kernel */
 
 /* Graph(param, bin, batch) of the reference (source/graph.cpp:44-111) on
  * `device` (-1 = current). */

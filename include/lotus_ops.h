@@ -180,6 +180,26 @@ typedef struct lotus_pool2d_desc {
 int lotus_maxpool2d_out_hw(const lotus_pool2d_desc* d, int* oh, int* ow);
 int lotus_maxpool2d_fwd(const void* x, void* y, const lotus_pool2d_desc* d, cudaStream_t stream);
 
+/* Convolution with the max pool that follows it fused into its epilogue:
+ * y = maxpool3x3/2/pad1(act(conv(x, w) + bias)), NHWC fp16 in and out
+ * ([n, ph, pw, Cs(c_out)] with the pool's output size).  Replaces the
+ * reference's Conv2d launch followed by its Maxpool2d launch on the conv's
+ * output (source/operator/conv2d.cu:17-187, source/operator/maxpool2d.cu:16-66,
+ * one after the other in source/graph.cpp:84-109); the full-size conv output
+ * is never written.  Pooling pads with -inf (PyTorch semantics).  `pool` NULL
+ * runs the same row kernel without the pool (y is then the conv output).
+ * Supported: stride-1 convs without padding whose kernel row is one 64-wide
+ * K block (Cs(c_in) * kw == 64, e.g. the space-to-depth ResNet stem: 12
+ * channels padded to 16, 4x4 kernel), output rows of at most 128 pixels, at
+ * most 64 output channels, kh <= 6, the pool 3x3 / stride 2 / pad 1 with no
+ * activation of its own (or ReLU after a ReLU conv).
+ * lotus_conv2d_maxpool_supported returns LOTUS_OK for a request the fused
+ * kernel takes, else LOTUS_ERR_UNSUPPORTED / LOTUS_ERR_INVALID with the reason
+ * in lotus_last_error_string(); it launches nothing. */
+int lotus_conv2d_maxpool_supported(const lotus_conv2d_desc* d, const lotus_pool2d_desc* pool);
+int lotus_conv2d_maxpool_fwd(const void* x, const void* w_packed, const float* bias, void* y,
+                             const lotus_conv2d_desc* d, const lotus_pool2d_desc* pool, cudaStream_t stream);
+
 /* Adaptive average pooling, NHWC fp16 in; PyTorch windows
  * [floor(i*H/OH), ceil((i+1)*H/OH)).  Output NHWC fp16 (out_f32 = 0) or
  * fp32 rows [n, oh*ow*c] in NHWC order (out_f32 = 1).  Replaces

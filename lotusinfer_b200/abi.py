@@ -70,6 +70,8 @@ SIGNATURES = {
     "lotus_gemv_bias_fwd": (_I, [_V, _I, _V, _I, _V, _V, _I, _I, _I, _I, _I, _V]),
     "lotus_maxpool2d_out_hw": (_I, [_PD, _IP, _IP]),
     "lotus_maxpool2d_fwd": (_I, [_V, _V, _PD, _V]),
+    "lotus_conv2d_maxpool_supported": (_I, [_CD, _PD]),
+    "lotus_conv2d_maxpool_fwd": (_I, [_V, _V, _V, _V, _CD, _PD, _V]),
     "lotus_adaptive_avgpool2d_fwd": (_I, [_V, _V, _I, _I, _I, _I, _I, _I, _I, _I, _V]),
     "lotus_add_act_fwd": (_I, [_V, _V, _V, _S, _I, _I, _V]),
     "lotus_concat_channels_fwd": (_I, [_V, _I, _V, _I, _V, _I, _I, _I, _V]),

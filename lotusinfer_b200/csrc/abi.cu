@@ -462,6 +462,67 @@ int lotus_maxpool2d_fwd(const void* x, void* y, const lotus_pool2d_desc* d, cuda
                      "maxpool2d");
 }
 
+// Row-conv arguments of a conv (+ pool) request, or an error status.
+static int row_conv_args(const lotus_conv2d_desc* d, const lotus_pool2d_desc* pool, ConvRowArgs* a) {
+  int oh, ow;
+  const int st = check_conv_desc(d, &oh, &ow);
+  if (st != LOTUS_OK) return st;
+  if (d->out_kind != LOTUS_OUT_NHWC_F16)
+    return fail(LOTUS_ERR_UNSUPPORTED, "conv2d_maxpool: NHWC fp16 output only");
+  if (d->stride_h != 1 || d->stride_w != 1 || d->pad_h != 0 || d->pad_w != 0)
+    return fail(LOTUS_ERR_UNSUPPORTED, "conv2d_maxpool: stride 1, no padding only");
+  if (pool) {
+    int ph, pw;
+    const int ps = lotus_maxpool2d_out_hw(pool, &ph, &pw);
+    if (ps != LOTUS_OK) return ps;
+    if (pool->n != d->n || pool->c != d->c_out || pool->h != oh || pool->w != ow)
+      return fail(LOTUS_ERR_INVALID, "conv2d_maxpool: pool input must be the conv output");
+    if (pool->kh != 3 || pool->kw != 3 || pool->stride_h != 2 || pool->stride_w != 2 || pool->pad_h != 1 ||
+        pool->pad_w != 1)
+      return fail(LOTUS_ERR_UNSUPPORTED, "conv2d_maxpool: 3x3 / stride 2 / pad 1 pooling only");
+    // max commutes with the monotone activations, but a second activation after
+    // the pool is only the identity for ReLU after ReLU
+    if (!(pool->act == LOTUS_ACT_NONE || (pool->act == LOTUS_ACT_RELU && d->act == LOTUS_ACT_RELU)))
+      return fail(LOTUS_ERR_UNSUPPORTED, "conv2d_maxpool: activation after the pool");
+  }
+  a->N = d->n;
+  a->H = d->h;
+  a->W = d->w;
+  a->Cs_in = cs_of(d->c_in);
+  a->kh = d->kh;
+  a->kw = d->kw;
+  a->Cout = d->c_out;
+  a->Cs_out = cs_of(d->c_out);
+  a->act = d->act;
+  a->pool = pool ? 1 : 0;
+  const char* err = "";
+  if (conv_row_check(*a, &err) != 0) return fail(LOTUS_ERR_UNSUPPORTED, std::string("conv2d_maxpool: ") + err);
+  return ok();
+}
+
+int lotus_conv2d_maxpool_supported(const lotus_conv2d_desc* d, const lotus_pool2d_desc* pool) {
+  ConvRowArgs a{};
+  return row_conv_args(d, pool, &a);
+}
+
+int lotus_conv2d_maxpool_fwd(const void* x, const void* w_packed, const float* bias, void* y,
+                             const lotus_conv2d_desc* d, const lotus_pool2d_desc* pool, cudaStream_t stream) {
+  ConvRowArgs a{};
+  const int st = row_conv_args(d, pool, &a);
+  if (st != LOTUS_OK) return st;
+  if (!x || !w_packed || !y) return fail(LOTUS_ERR_INVALID, "conv2d_maxpool: null x, w or y");
+  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y))
+    return fail(LOTUS_ERR_INVALID, "conv2d_maxpool: x, w and y must be 16-byte aligned");
+  a.x = x;
+  a.w_packed = w_packed;
+  a.bias = bias;
+  a.y = y;
+  const char* err = "";
+  const int r = conv_row_launch(a, stream, &err);
+  if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d_maxpool: ") + err);
+  return ok();
+}
+
 int lotus_adaptive_avgpool2d_fwd(const void* x, void* y, int n, int c, int h, int w, int oh, int ow, int act,
                                  int out_f32, cudaStream_t stream) {
   if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(LOTUS_ERR_INVALID, "adaptive_avgpool2d: bad pointer");

@@ -1,0 +1,562 @@
+// Row-tile convolution on sm_100a tensor cores with an optional fused
+// 3x3 / stride-2 / pad-1 max pool of its activated output.
+//
+// Scope: stride-1 convs without padding whose kernel row is exactly one
+// 64-wide K block (Cs_in * kw == 64), output rows of at most 128 pixels and
+// at most 64 output channels.  This is the ResNet-18 stem after the
+// space-to-depth rewrite (4x4 kernel over 16-channel pixels, 112-pixel rows),
+// whose output the reference feeds straight into a 3x3/2 max pool
+// (source/operator/conv2d.cu:17-187 then source/operator/maxpool2d.cu:16-66,
+// wired by source/graph.cpp:84-109).
+//
+// GEMM view: one tile = one output row (oy) of one image, M = 128 positions
+// (ox = 0..127; ox >= OW are computed and dropped), N = Cout (<= 64),
+// K = kh * 64.  In NHWC the kw taps of one kernel row read kw consecutive
+// pixels, i.e. kw * Cs_in = 64 contiguous fp16 values starting at pixel
+// (oy + r, ox).  A 4-D TMA map whose innermost dimension is those 64 values
+// and whose next dimension steps ONE pixel (an overlapping stride) lands a
+// whole input row as 128 rows of 128 bytes, 128B-swizzled: exactly the
+// K-major A operand of kernel row r for every position of the tile, with a
+// 1024-byte-aligned start.  Input rows live in a ring of kRowSlots slots;
+// output row oy reads slots of input rows oy .. oy+kh-1, so every input row
+// is loaded once per CTA segment and serves kh output rows.
+//
+// Roles (352 threads):
+//   warps 0-7   epilogue: warp w drains TMEM lane quarter w%4, columns
+//               32*(w/4) .. +31: bias, activation, fp16, then either the
+//               conv row itself or the max pool: the horizontal 3-wide max
+//               by warp shuffles (lane 0's left neighbour comes from the
+//               previous quarter through shared memory), the vertical max
+//               carried in registers from row to row (a thread always holds
+//               the same ox and channels);
+//   warp 8      TMEM allocation, MMA issuer 0 (even tiles);
+//   warp 9      TMA producer: the weights once, then input rows in order;
+//   warp 10     MMA issuer 1 (odd tiles).
+// Each CTA owns a contiguous range of output units (pooled rows, or conv
+// rows without the pool) over the whole batch, walked as per-image
+// segments; with the pool a segment also computes the conv row just above
+// its first pooled row (the shared row of two pooled windows).
+//
+// Barrier protocol (all waits bounded): rfull[slot] (TMA bytes), rempty[slot]
+// (count 2: each issuer commits once per load after its last MMA reading it;
+// an issuer waits on every load of the sequence in order, so a slot can only
+// be refilled after both issuers have observed its previous load), tfull /
+// tempty per TMEM accumulator (8 x 64 columns), wfull for the weights.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdlib>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace lotus_impl {
+
+using namespace lotus_dev;
+
+namespace {
+
+constexpr int kRowSlots = 8;                   // input-row ring
+constexpr int kRowPos = 128;                   // positions (A rows) per tile
+constexpr int kSlotBytes = kRowPos * 128;      // one input row: 128 rows x 128 B
+constexpr int kRowAcc = 8;                     // TMEM accumulators of 64 columns
+constexpr int kRowMaxKh = kRowSlots - 2;       // a tile's loads plus the next tile's fit the ring
+constexpr int kWBlockBytes = 64 * 128;         // one 64-wide K block of 64 weight rows
+constexpr int kEpiWarps = 8;
+constexpr int kIssuer0 = 8, kProducer = 9, kIssuer1 = 10;
+constexpr int kThreads = 11 * 32;
+
+struct RowParams {
+  const float* bias;
+  __half* y;
+  int N, OH, OW, Cout, Cs_out, kh, act;
+  int pool;          // 0: conv rows out, 1: fused 3x3/2 pad-1 max pool
+  int PH, PW;        // pooled size (pool == 1)
+  int units;         // N * (pool ? PH : OH)
+  int w_bytes;       // kh * kWBlockBytes
+  int map5;          // input-row map has the kw taps as their own dimension
+  uint32_t wait_limit;
+};
+
+// Shared-memory layout (from the 1024-aligned base): weights, input-row ring,
+// barriers, misc words, bias, the epilogue's edge-exchange buffer.
+constexpr int kMaxWBytes = kRowMaxKh * kWBlockBytes;
+constexpr int kRingOff = kMaxWBytes;  // weights first (only w_bytes of it used)
+constexpr int kBarOff = kRingOff + kRowSlots * kSlotBytes;
+constexpr int kNumBars = 1 + 2 * kRowSlots + 2 * kRowAcc + 1;
+constexpr int kMiscOff = kBarOff + kNumBars * 8;
+constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
+constexpr int kEdgeOff = kBiasOff + 64 * 4;
+constexpr int kEdgeBytes = 2 * 4 * 2 * 64;  // [tile parity][quarter][column half][32 fp16]
+constexpr int kSmemBytes = kEdgeOff + kEdgeBytes + 1024;
+static_assert(kSmemBytes <= 232448, "row kernel shared memory above 227 KB");
+
+// One segment of a CTA's units: image n, conv rows lo..hi.
+struct Seg {
+  int n, lo, hi;
+};
+
+// Next segment of the unit range [u, u1); advances u.
+__device__ __forceinline__ bool next_seg(const RowParams& p, int& u, int u1, Seg& s) {
+  if (u >= u1) return false;
+  const int per = p.pool ? p.PH : p.OH;
+  const int n = u / per;
+  const int a = u - n * per;
+  const int e = min(per, a + (u1 - u));
+  s.n = n;
+  if (p.pool) {
+    // pooled row py covers conv rows 2py-1 .. 2py+1 (inside the image)
+    s.lo = max(2 * a - 1, 0);
+    s.hi = min(2 * e - 1, p.OH - 1);
+  } else {
+    s.lo = a;
+    s.hi = e - 1;
+  }
+  u += e - a;
+  return true;
+}
+
+__device__ __forceinline__ uint32_t hmax3_u32(uint32_t a, uint32_t b, uint32_t c) {
+  __half2 x = *reinterpret_cast<__half2*>(&a), y = *reinterpret_cast<__half2*>(&b),
+          z = *reinterpret_cast<__half2*>(&c);
+  __half2 m = __hmax2(__hmax2(x, y), z);
+  return *reinterpret_cast<uint32_t*>(&m);
+}
+__device__ __forceinline__ uint32_t hmax2_u32(uint32_t a, uint32_t b) {
+  __half2 x = *reinterpret_cast<__half2*>(&a), y = *reinterpret_cast<__half2*>(&b);
+  __half2 m = __hmax2(x, y);
+  return *reinterpret_cast<uint32_t*>(&m);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+constexpr uint32_t kNegInf2 = 0xFC00FC00u;  // two fp16 -inf
+
+template <int ACT>
+__device__ __forceinline__ float act_f(float v) {
+  if (ACT == 1) return fmaxf(v, 0.0f);
+  if (ACT == 2) return 1.0f / (1.0f + expf(-v));
+  return v;
+}
+
+// 32 consecutive fp16 (64 bytes) from registers to global memory.
+__device__ __forceinline__ void store_row32(__half* dst, const uint32_t (&h)[16], int c0, int cs_out) {
+#pragma unroll
+  for (int s = 0; s < 4; ++s)
+    if (c0 + 8 * s < cs_out)
+      *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(h[4 * s], h[4 * s + 1], h[4 * s + 2], h[4 * s + 3]);
+}
+
+template <int ACT>
+__device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint64_t* tfull, uint64_t* tempty,
+                                         volatile int* abort_flag, uint32_t tmem_base, int u0, int u1) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, hc = warp >> 2;
+  const int ox = q * 32 + lane;
+  const bool xvalid = ox < p.OW;
+  const int c0 = hc * 32;
+  const float* s_bias = reinterpret_cast<const float*>(smem + kBiasOff);
+  uint32_t* edge = reinterpret_cast<uint32_t*>(smem + kEdgeOff);
+  const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+  uint32_t carry[16], vmax[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) carry[k] = vmax[k] = kNegInf2;
+  int lt = 0;
+  int u = u0;
+  Seg sg;
+  while (next_seg(p, u, u1, sg)) {
+    bool carry_ok = false;
+    for (int oy = sg.lo; oy <= sg.hi; ++oy, ++lt) {
+      const int ab = lt % kRowAcc;
+      bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / kRowAcc) & 1, kErrWaitAccum, p.wait_limit);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      uint32_t v[32];
+      if (ok) {
+        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * 64 + c0, v);
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&tempty[ab]);
+        if (!ok) *abort_flag = 1;
+      }
+      uint32_t h[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int c = c0 + 2 * k;
+        float f0 = ok ? act_f<ACT>(__uint_as_float(v[2 * k]) + s_bias[c]) : 0.f;
+        float f1 = ok ? act_f<ACT>(__uint_as_float(v[2 * k + 1]) + s_bias[c + 1]) : 0.f;
+        if (c >= p.Cout) f0 = 0.f;  // pad channels stay zero
+        if (c + 1 >= p.Cout) f1 = 0.f;
+        h[k] = xvalid ? pack2(f0, f1) : kNegInf2;
+      }
+      if (!p.pool) {
+        if (ok && xvalid)
+          store_row32(p.y + ((static_cast<int64_t>(sg.n) * p.OH + oy) * p.OW + ox) * p.Cs_out + c0, h, c0, p.Cs_out);
+        continue;
+      }
+      // horizontal 3-wide max at even ox; lane 0's left neighbour (ox - 1)
+      // is lane 31 of the previous quarter, exchanged through shared memory
+      uint32_t* eg = edge + ((lt & 1) * 8 + q * 2 + hc) * 16;
+      if (lane == 31) {
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          reinterpret_cast<uint4*>(eg)[s] = make_uint4(h[4 * s], h[4 * s + 1], h[4 * s + 2], h[4 * s + 3]);
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+      const uint32_t* eprev = edge + ((lt & 1) * 8 + (q > 0 ? q - 1 : 0) * 2 + hc) * 16;
+      uint32_t m[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        uint32_t left = __shfl_up_sync(0xffffffffu, h[k], 1);
+        const uint32_t right = __shfl_down_sync(0xffffffffu, h[k], 1);
+        if (lane == 0) left = q > 0 ? eprev[k] : kNegInf2;
+        m[k] = hmax3_u32(left, h[k], right);
+      }
+      const bool out_lane = ok && xvalid && (ox & 1) == 0;
+      __half* yrow = nullptr;
+      if (oy & 1) {
+        // odd row 2py+1 closes pooled row py, unless it only carries into
+        // this segment's first pooled row
+        if (oy != sg.lo) {
+          uint32_t o[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) o[k] = hmax2_u32(vmax[k], m[k]);
+          yrow = p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0;
+          if (out_lane) store_row32(yrow, o, c0, p.Cs_out);
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) carry[k] = m[k];
+        carry_ok = true;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) vmax[k] = carry_ok ? hmax2_u32(carry[k], m[k]) : m[k];
+        if (oy == p.OH - 1) {  // an odd-height map's last pooled row has no row below
+          yrow = p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0;
+          if (out_lane) store_row32(yrow, vmax, c0, p.Cs_out);
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                const RowParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem;
+  uint8_t* ring = smem + kRingOff;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint64_t* rfull = wfull + 1;
+  uint64_t* rempty = rfull + kRowSlots;
+  uint64_t* tfull = rempty + kRowSlots;
+  uint64_t* tempty = tfull + kRowAcc;
+  uint64_t* mma_done = tempty + kRowAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kMiscOff + 4);
+  float* s_bias = reinterpret_cast<float*>(smem + kBiasOff);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // this CTA's units [u0, u1) (pooled rows or conv rows over the batch)
+  const int u0 = static_cast<int>(static_cast<int64_t>(p.units) * blockIdx.x / gridDim.x);
+  const int u1 = static_cast<int>(static_cast<int64_t>(p.units) * (blockIdx.x + 1) / gridDim.x);
+
+  if (tid == 0) {
+    mbar_init(wfull, 1);
+    for (int s = 0; s < kRowSlots; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], 2);
+    }
+    for (int b = 0; b < kRowAcc; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    mbar_init(mma_done, 2);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (tid < 64) s_bias[tid] = (p.bias != nullptr && tid < p.Cout) ? __ldg(p.bias + tid) : 0.f;
+  if (warp == kProducer && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == kIssuer0) {
+    tmem_alloc(tmem_slot, kRowAcc * 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < kEpiWarps) {
+    if (p.act == 1)
+      epilogue<1>(p, smem, tfull, tempty, abort_flag, tmem_base, u0, u1);
+    else if (p.act == 0)
+      epilogue<0>(p, smem, tfull, tempty, abort_flag, tmem_base, u0, u1);
+    else
+      epilogue<2>(p, smem, tfull, tempty, abort_flag, tmem_base, u0, u1);
+  } else if (warp == kProducer) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(wfull, static_cast<uint32_t>(p.w_bytes));
+      for (int r = 0; r < p.kh; ++r) tma_load_2d(sW + r * kWBlockBytes, &tmap_w, wfull, r * 64, 0);
+      uint32_t L = 0;
+      int u = u0;
+      Seg sg;
+      while (ok && next_seg(p, u, u1, sg)) {
+        for (int yin = sg.lo; yin <= sg.hi + p.kh - 1; ++yin, ++L) {
+          const uint32_t slot = L % kRowSlots;
+          if (*abort_flag ||
+              !mbar_wait(&rempty[slot], ((L / kRowSlots) & 1) ^ 1, kErrWaitEmpty, p.wait_limit)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&rfull[slot], kSlotBytes);
+          if (p.map5)
+            tma_load_5d(ring + slot * kSlotBytes, &tmap_x, &rfull[slot], 0, 0, 0, yin, sg.n);
+          else
+            tma_load_4d(ring + slot * kSlotBytes, &tmap_x, &rfull[slot], 0, 0, yin, sg.n);
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      // every TMA load this thread issued has landed before the CTA may exit
+      mbar_wait(wfull, 0, kErrWaitFull, p.wait_limit);
+      for (int64_t j = static_cast<int64_t>(L) - 1; j >= 0 && j >= static_cast<int64_t>(L) - kRowSlots; --j)
+        mbar_wait(&rfull[j % kRowSlots], static_cast<uint32_t>(j / kRowSlots) & 1, kErrWaitFull, p.wait_limit);
+    }
+  } else if (warp == kIssuer0 || warp == kIssuer1) {
+    if (lane == 0) {
+      const int issuer = warp == kIssuer0 ? 0 : 1;
+      constexpr uint32_t idesc = make_idesc_f16_m128(64);
+      // no shared-memory loads in this loop (they would wait behind queued
+      // MMAs); waits are relaxed, every one bounded
+      bool ok = mbar_wait_relaxed(wfull, 0, kErrWaitFull, p.wait_limit);
+      uint32_t next_wait = 0, next_rel = 0, Lseg = 0;
+      int lt = 0;
+      int u = u0;
+      Seg sg;
+      const uint64_t b_base = make_sdesc_sw128(smem_u32(sW));
+      while (ok && next_seg(p, u, u1, sg)) {
+        const int ntiles = sg.hi - sg.lo + 1;
+        const uint32_t nloads = static_cast<uint32_t>(ntiles + p.kh - 1);
+        for (int j = 0; j < ntiles && ok; ++j, ++lt) {
+          if ((lt & 1) != issuer) continue;
+          const int ab = lt % kRowAcc;
+          if (!mbar_wait_relaxed(&tempty[ab], ((lt / kRowAcc) & 1) ^ 1, kErrWaitAccum, p.wait_limit)) {
+            ok = false;
+            break;
+          }
+          // every load up to the tile's last one, in order (including loads
+          // only the other issuer's tiles read)
+          const uint32_t last = Lseg + static_cast<uint32_t>(j + p.kh - 1);
+          for (; next_wait <= last; ++next_wait) {
+            if (!mbar_wait_relaxed(&rfull[next_wait % kRowSlots], (next_wait / kRowSlots) & 1, kErrWaitFull,
+                                   p.wait_limit)) {
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + ab * 64;
+          for (int r = 0; r < p.kh; ++r) {
+            const uint32_t L = Lseg + static_cast<uint32_t>(j + r);
+            const uint64_t a_desc = make_sdesc_sw128(smem_u32(ring + (L % kRowSlots) * kSlotBytes));
+            const uint64_t b_desc = b_base + static_cast<uint32_t>(r * (kWBlockBytes >> 4));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)  // K step = 32 bytes = 2 start-address units
+              umma_f16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (r | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&tfull[ab]);
+          // this issuer's next tile (j + 2) reads loads from Lseg + j + 2 on
+          const uint32_t rel_to = std::min(Lseg + static_cast<uint32_t>(j + 1), next_wait - 1);
+          for (; next_rel <= rel_to; ++next_rel) umma_commit(&rempty[next_rel % kRowSlots]);
+        }
+        if (!ok) break;
+        // segment end: observe and release the rest of its loads
+        const uint32_t end = Lseg + nloads - 1;
+        for (; next_wait <= end; ++next_wait) {
+          if (!mbar_wait_relaxed(&rfull[next_wait % kRowSlots], (next_wait / kRowSlots) & 1, kErrWaitFull,
+                                 p.wait_limit)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        for (; next_rel <= end; ++next_rel) umma_commit(&rempty[next_rel % kRowSlots]);
+        Lseg += nloads;
+      }
+      if (!ok) *abort_flag = 1;
+      // every MMA of both issuers has completed once mma_done fires
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, kErrWaitFull, p.wait_limit);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kIssuer0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kRowAcc * 64);
+  }
+}
+
+// Input rows of the NHWC activation as 64-value runs: element (e, x, y, n)
+// is x[n, y, x + e / Cs_in, e % Cs_in], so dimension 0 (64 contiguous fp16 =
+// kw pixels) overlaps the next pixel's run (stride Cs_in * 2 bytes).  Box
+// {64, 128, 1, 1}, 128B swizzle; x < OW keeps every run inside its image row
+// and x >= OW reads zeros.  Variant 5 describes the same bytes with the kw
+// taps as their own dimension (box inner 32 bytes), in case the encoder
+// refuses the overlapping innermost run.
+int make_row_map(CUtensorMap* map, const ConvRowArgs& a, int ow, int variant) {
+  auto enc = encode_tiled();
+  if (!enc) return -1;
+  const cuuint64_t px = static_cast<cuuint64_t>(a.Cs_in) * 2;
+  CUresult r;
+  if (variant == 4) {
+    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(ow), static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.N)};
+    cuuint64_t strides[3] = {px, px * a.W, px * a.W * a.H};
+    cuuint32_t box[4] = {64, kRowPos, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[5] = {static_cast<cuuint64_t>(a.Cs_in), static_cast<cuuint64_t>(a.kw),
+                          static_cast<cuuint64_t>(ow), static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.N)};
+    cuuint64_t strides[4] = {px, px, px * a.W, px * a.W * a.H};
+    cuuint32_t box[5] = {static_cast<cuuint32_t>(a.Cs_in), static_cast<cuuint32_t>(a.kw), kRowPos, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(a.x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+int make_weight_map(CUtensorMap* map, const ConvRowArgs& a) {
+  auto enc = encode_tiled();
+  if (!enc) return -1;
+  const int k_pad = a.kh * 64;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k_pad), static_cast<cuuint64_t>(a.Cout)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k_pad) * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.w_packed), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+}  // namespace
+
+int conv_row_check(const ConvRowArgs& a, const char** err) {
+  if (a.Cs_in * a.kw != 64 || a.Cs_in % 8 != 0) {
+    *err = "row conv: needs Cs_in * kw == 64";
+    return -2;
+  }
+  if (a.kh < 1 || a.kh > kRowMaxKh || a.H < a.kh || a.W < a.kw) {
+    *err = "row conv: kernel height outside 1..6 or larger than the input";
+    return -2;
+  }
+  const int ow = a.W - a.kw + 1;
+  if (ow > kRowPos) {
+    *err = "row conv: output rows longer than 128 pixels";
+    return -2;
+  }
+  if (a.Cout < 1 || a.Cout > 64 || a.Cs_out != (a.Cout + 7) / 8 * 8) {
+    *err = "row conv: 1..64 output channels";
+    return -2;
+  }
+  if (a.pool != 0 && a.pool != 1) {
+    *err = "row conv: unknown pool";
+    return -2;
+  }
+  if (static_cast<int64_t>(a.N) * (a.H - a.kh + 1) > 0x7FFFFFFF) {
+    *err = "row conv: too many rows";
+    return -2;
+  }
+  return 0;
+}
+
+int conv_row_launch(const ConvRowArgs& a, cudaStream_t stream, const char** err) {
+  if (conv_row_check(a, err) != 0) return -2;
+  RowParams p{};
+  p.bias = a.bias;
+  p.y = static_cast<__half*>(a.y);
+  p.N = a.N;
+  p.OH = a.H - a.kh + 1;
+  p.OW = a.W - a.kw + 1;
+  p.Cout = a.Cout;
+  p.Cs_out = a.Cs_out;
+  p.kh = a.kh;
+  p.act = a.act;
+  p.pool = a.pool;
+  p.PH = (p.OH - 1) / 2 + 1;
+  p.PW = (p.OW - 1) / 2 + 1;
+  p.units = a.N * (a.pool ? p.PH : p.OH);
+  p.w_bytes = a.kh * kWBlockBytes;
+  p.wait_limit = wait_limit_from_env();
+
+  CUtensorMap mw, mx;
+  if (make_weight_map(&mw, a) != 0) {
+    *err = "row conv: weight tensor map encoding failed";
+    return -3;
+  }
+  const char* v = std::getenv("LOTUS_ROW_TMAP");
+  const bool force5 = v && std::atoi(v) == 5;
+  p.map5 = (force5 || make_row_map(&mx, a, p.OW, 4) != 0) ? 1 : 0;
+  if (p.map5 && make_row_map(&mx, a, p.OW, 5) != 0) {
+    *err = "row conv: input-row tensor map encoding failed";
+    return -2;
+  }
+
+  static std::atomic<uint64_t> attr_ctx[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = "row conv: no usable device";
+    return -3;
+  }
+  const uint64_t ctx = current_context_id();
+  if (ctx == 0 || attr_ctx[dev].load(std::memory_order_acquire) != ctx) {
+    const cudaError_t ae = cudaFuncSetAttribute(conv_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kSmemBytes);
+    if (ae != cudaSuccess) {
+      *err = cudaGetErrorString(ae);
+      return -3;
+    }
+    attr_ctx[dev].store(ctx, std::memory_order_release);
+  }
+  const int grid = std::min(num_sms(), p.units);
+  conv_row_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mw, mx, p);
+  note_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *err = cudaGetErrorString(e);
+    return -3;
+  }
+  return 0;
+}
+
+int conv_row_read_device_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, lotus_dev::g_lotus_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v != 0) {
+    int zero = 0;
+    cudaMemcpyToSymbol(lotus_dev::g_lotus_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace lotus_impl

@@ -1170,7 +1170,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 
 // ---------------------------------------------------------------- host side
 
-static void* driver_fn(const char* name) {
+void* driver_fn(const char* name) {
   cudaDriverEntryPointQueryResult q;
   void* ptr = nullptr;
   if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
@@ -1202,7 +1202,7 @@ uint64_t current_context_id() {
   return static_cast<uint64_t>(id);
 }
 
-static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -1413,7 +1413,7 @@ static int split_count(long mn, int kb_total, int sms, int* kbs) {
 }
 
 // SM count of the current device, cached per device ordinal.
-static int num_sms() {
+int num_sms() {
   static std::atomic<int> cache[kMaxDevices];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
@@ -1653,7 +1653,8 @@ int conv_tc_noalloc_scratch(float** ptr, const char** err) {
   return 0;
 }
 
-int read_device_error() {
+// Returns and clears this translation unit's device error word.
+static int read_own_device_error() {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, lotus_dev::g_lotus_device_error, sizeof(int)) != cudaSuccess) return -1;
   if (v != 0) {
@@ -1661,6 +1662,14 @@ int read_device_error() {
     cudaMemcpyToSymbol(lotus_dev::g_lotus_device_error, &zero, sizeof(int));
   }
   return v;
+}
+
+int read_device_error() {
+  // every kernel file keeps its own error word; report the first non-zero
+  // one and clear them all
+  const int a = read_own_device_error();
+  const int b = conv_row_read_device_error();
+  return a != 0 ? a : b;
 }
 
 }  // namespace lotus_impl

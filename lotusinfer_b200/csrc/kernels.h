@@ -4,6 +4,8 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 namespace lotus_impl {
@@ -43,7 +45,35 @@ constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 // Device address of that scratch on the current device; the first call on a
 // device looks it up (cudaGetSymbolAddress).  0 = ok, < 0 = error in *err.
 int conv_tc_noalloc_scratch(float** ptr, const char** err);
+// Returns and clears the device error word of every kernel file (first
+// non-zero code, 0 = none, -1 = unreadable).
 int read_device_error();
+
+// Shared host helpers (conv_tc.cu): a driver entry point by name, the tiled
+// tensor-map encoder, the current device's SM count, the bounded-wait limit
+// of a launch (LOTUS_WAIT_LIMIT or the default) and the process-unique id of
+// the current CUDA context (0 = none).
+void* driver_fn(const char* name);
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
+int num_sms();
+uint32_t wait_limit_from_env();
+uint64_t current_context_id();
+
+// conv_row.cu: the row-tile conv (stride 1, no padding, Cs_in*kw == 64,
+// OW <= 128, Cout <= 64) with an optional fused 3x3 / stride-2 / pad-1 max
+// pool of its activated output.
+struct ConvRowArgs {
+  const void* x;          // NHWC fp16 [N, H, W, Cs_in]
+  const void* w_packed;   // [Cout, kh*64] fp16 (the conv prepack)
+  const float* bias;      // [Cout] or null
+  void* y;                // NHWC fp16 [N, OH, OW, Cs_out] or pooled [N, PH, PW, Cs_out]
+  int N, H, W, Cs_in, kh, kw, Cout, Cs_out, act;
+  int pool;               // 0 none, 1 max pool 3x3 / stride 2 / pad 1
+};
+// 0 when the row kernel takes this shape, else -2 with the reason in *err.
+int conv_row_check(const ConvRowArgs& a, const char** err);
+int conv_row_launch(const ConvRowArgs& a, cudaStream_t stream, const char** err);
+int conv_row_read_device_error();
 
 // pack.cu
 cudaError_t launch_conv_prepack(const float* w, void* wp, int cout, int cin, int kh, int kw, int cs_in, int k_pad,

@@ -15,9 +15,10 @@
 namespace lotus_dev {
 
 // Error word written by a kernel whose bounded wait expired (0 = none).
-// Read and cleared on the host through lotus_device_error().  Defined here
-// because exactly one translation unit (conv_tc.cu) includes this header.
-__device__ int g_lotus_device_error = 0;
+// Read and cleared on the host through lotus_device_error().  Each
+// translation unit that includes this header has its own copy (the library
+// is built without relocatable device code); the host reads all of them.
+static __device__ int g_lotus_device_error = 0;
 
 enum : int {
   kErrNone = 0,
@@ -154,6 +155,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 5-D tiled load (no multicast), coordinates innermost first, same rules.
+__device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar))
       : "memory");
 }
 

@@ -228,6 +228,42 @@ void Graph::Build(const std::string& param_path, const std::string& bin_path) {
     }
   }
 
+  // pool fusion: conv (sole consumer: a 3x3/2 pad-1 max pool) -> pool becomes
+  // one conv whose epilogue writes the pooled output (the ResNet stem; the
+  // full-size conv output is never stored)
+  if (opt_.fuse_pool) {
+    std::vector<std::string> fused;
+    for (auto& name : layer_order_) {
+      auto pool = std::dynamic_pointer_cast<Maxpool2dLayer>(layers_.at(name));
+      if (!pool) continue;
+      const std::string& src = pool->inputs_name_.at(0);
+      auto conv = std::dynamic_pointer_cast<Conv2dLayer>(producer_of(src));
+      if (!conv || !conv->Residual().empty() || conv->HasPool() || consumers_of(src).size() != 1) continue;
+      const std::string& cin = conv->inputs_name_.at(0);
+      const auto& xs = (cin == input_operand_ && stem_s2d_ > 1) ? stem_shape_ : shapes.at(cin);
+      const auto& ys = shapes.at(src);
+      if (xs.size() != 4 || ys.size() != 4) continue;
+      lotus_conv2d_desc d = conv->Desc();
+      d.n = static_cast<int>(xs[0]);
+      d.h = static_cast<int>(xs[2]);
+      d.w = static_cast<int>(xs[3]);
+      d.act = conv->af_;
+      lotus_pool2d_desc pd = pool->Desc();
+      pd.n = d.n;
+      pd.c = static_cast<int>(ys[1]);
+      pd.h = static_cast<int>(ys[2]);
+      pd.w = static_cast<int>(ys[3]);
+      if (lotus_conv2d_maxpool_supported(&d, &pd) != LOTUS_OK) continue;
+      conv->SetPool(pd);
+      conv->outputs_name_ = pool->outputs_name_;
+      fused.push_back(name);
+    }
+    for (auto& n : fused) {
+      layers_.erase(n);
+      layer_order_.erase(std::find(layer_order_.begin(), layer_order_.end(), n));
+    }
+  }
+
   // operands that carry data after fusion
   std::set<std::string> live;
   for (auto& kv : layers_) {

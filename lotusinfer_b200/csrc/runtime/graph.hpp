@@ -31,6 +31,7 @@ class Graph {
     bool cuda_graph = true;      // replay Forward from a CUDA graph after the first run
     bool fuse_residual = true;   // fold conv -> add (-> ReLU) into the conv epilogue
     bool s2d_stem = true;        // run a strided few-channel stem conv over the space-to-depth input
+    bool fuse_pool = true;       // fold a 3x3/2 max pool into the conv that feeds it, where the fused kernel applies
   };
 
   Graph(const std::string& param_path, const std::string& bin_path, uint32_t batch_size);

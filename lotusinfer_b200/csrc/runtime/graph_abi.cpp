@@ -40,6 +40,7 @@ lotus_graph* lotus_graph_create(const char* param_path, const char* bin_path, in
     o.cuda_graph = (flags & LOTUS_GRAPH_NO_CUDA_GRAPH) == 0;
     o.fuse_residual = (flags & LOTUS_GRAPH_NO_RESIDUAL_FUSION) == 0;
     o.s2d_stem = (flags & LOTUS_GRAPH_NO_S2D_STEM) == 0;
+    o.fuse_pool = (flags & LOTUS_GRAPH_NO_POOL_FUSION) == 0;
     std::unique_ptr<lotus::Graph> graph(new lotus::Graph(param_path, bin_path, static_cast<uint32_t>(batch), o));
     auto* h = new lotus_graph;
     h->g = std::move(graph);

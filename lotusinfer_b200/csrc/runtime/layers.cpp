@@ -174,6 +174,14 @@ void Conv2dLayer::Bind(const OperandMap& operands) {
   if (static_cast<int>(x.Dim(1)) != desc_.c_in) throw std::runtime_error(name_ + ": input channel mismatch");
   int oh = 0, ow = 0;
   LotusCheck(lotus_conv2d_out_hw(&desc_, &oh, &ow), name_);
+  if (has_pool_) {
+    pool_.n = desc_.n;
+    pool_.c = desc_.c_out;
+    pool_.h = oh;
+    pool_.w = ow;
+    LotusCheck(lotus_maxpool2d_out_hw(&pool_, &oh, &ow), name_);
+    LotusCheck(lotus_conv2d_maxpool_supported(&desc_, &pool_), name_);
+  }
   if (y.Dim(0) != x.Dim(0) || static_cast<int>(y.Dim(1)) != desc_.c_out || static_cast<int>(y.Dim(2)) != oh ||
       static_cast<int>(y.Dim(3)) != ow)
     throw std::runtime_error(name_ + ": output shape mismatch");
@@ -182,15 +190,23 @@ void Conv2dLayer::Bind(const OperandMap& operands) {
 }
 
 void Conv2dLayer::Forward(cudaStream_t stream) {
+  if (has_pool_) {
+    LotusCheck(lotus_conv2d_maxpool_fwd(inputs_[0]->tensor_.Data(), w_packed_.get(),
+                                        static_cast<const float*>(bias_.get()), outputs_[0]->tensor_.Data(), &desc_,
+                                        &pool_, stream),
+               name_);
+    return;
+  }
   const void* res = residual_name_.empty() ? nullptr : inputs_.back()->tensor_.Data();
   LotusCheck(lotus_conv2d_fwd_ws(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
                                  res, outputs_[0]->tensor_.Data(), &desc_, workspace_, workspace_bytes_, stream),
              name_);
 }
 
-size_t Conv2dLayer::WorkspaceBytes() const { return lotus_conv2d_workspace_bytes(&desc_); }
+size_t Conv2dLayer::WorkspaceBytes() const { return has_pool_ ? 0 : lotus_conv2d_workspace_bytes(&desc_); }
 
 int Conv2dLayer::Launches() const {
+  if (has_pool_) return 1;
   const size_t need = WorkspaceBytes();
   return (need > 0 && workspace_ != nullptr && need <= workspace_bytes_) ? 2 : 1;  // conv + split-K reduction
 }

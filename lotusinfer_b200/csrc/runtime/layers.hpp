@@ -111,6 +111,14 @@ class Conv2dLayer : public Layer {
     inputs_name_.push_back(operand);
   }
   const std::string& Residual() const { return residual_name_; }
+  // Fold the max pool that consumes this conv's output into the conv's
+  // epilogue (lotus_conv2d_maxpool_fwd); the output operand becomes the
+  // pool's.
+  void SetPool(const lotus_pool2d_desc& pool) {
+    pool_ = pool;
+    has_pool_ = true;
+  }
+  bool HasPool() const { return has_pool_; }
   void Bind(const OperandMap& operands) override;
   void Forward(cudaStream_t stream) override;
   double Flops() const override;
@@ -129,6 +137,8 @@ class Conv2dLayer : public Layer {
   std::shared_ptr<void> bias_;
   std::string residual_name_;
   lotus_conv2d_desc desc_{};
+  lotus_pool2d_desc pool_{};
+  bool has_pool_ = false;
 };
 
 class TransposedConv2dLayer : public Layer {
@@ -179,6 +189,12 @@ class Maxpool2dLayer : public Layer {
   Maxpool2dLayer(const pnnx::Operator& op, int kh, int kw, int sh, int sw, int ph, int pw);
   void Bind(const OperandMap& operands) override;
   void Forward(cudaStream_t stream) override;
+  // Window, stride, padding and folded activation (sizes are set at Bind).
+  lotus_pool2d_desc Desc() const {
+    lotus_pool2d_desc d = desc_;
+    d.act = af_;
+    return d;
+  }
 
  private:
   lotus_pool2d_desc desc_{};

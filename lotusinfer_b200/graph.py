@@ -50,6 +50,7 @@ GRAPH_SIGNATURES = {
 NO_CUDA_GRAPH = 1
 NO_RESIDUAL_FUSION = 2
 NO_S2D_STEM = 4
+NO_POOL_FUSION = 8
 
 _bound = False
 
@@ -78,9 +79,9 @@ def _cuda_copy(dst: int, src: int, nbytes: int) -> None:
 
 class Graph:
     def __init__(self, param_path: str, bin_path: str, batch: int, device: int = -1, cuda_graph: bool = True,
-                 fuse_residual: bool = True, s2d_stem: bool = True):
+                 fuse_residual: bool = True, s2d_stem: bool = True, fuse_pool: bool = True):
         flags = ((0 if cuda_graph else NO_CUDA_GRAPH) | (0 if fuse_residual else NO_RESIDUAL_FUSION) |
-                 (0 if s2d_stem else NO_S2D_STEM))
+                 (0 if s2d_stem else NO_S2D_STEM) | (0 if fuse_pool else NO_POOL_FUSION))
         L = _lib()
         h = L.lotus_graph_create(param_path.encode(), bin_path.encode(), int(batch), int(device), flags)
         if not h:

@@ -200,6 +200,23 @@ def maxpool2d(x: torch.Tensor, c: int, k, stride, pad=0, act=ACT_NONE) -> torch.
     return y
 
 
+def conv2d_maxpool(x: torch.Tensor, c_in: int, w_packed: torch.Tensor, bias: Optional[torch.Tensor], c_out: int,
+                   k, act=ACT_NONE, pool: bool = True) -> torch.Tensor:
+    """Row-tile conv (stride 1, no padding) with the fused 3x3/2 pad-1 max
+    pool, or without the pool when pool=False; NHWC fp16 in and out."""
+    n, h, w, _ = x.shape
+    kh, kw = _pair(k)
+    d = conv_desc(n, c_in, h, w, c_out, (kh, kw), 1, 0, act)
+    oh, ow = h - kh + 1, w - kw + 1
+    pd = Pool2dDesc(n, c_out, oh, ow, 3, 3, 2, 2, 1, 1, ACT_NONE) if pool else None
+    if pool:
+        oh, ow = (oh - 1) // 2 + 1, (ow - 1) // 2 + 1
+    y = torch.empty((n, oh, ow, channel_stride(c_out)), dtype=torch.float16, device=x.device)
+    check(abi.lib().lotus_conv2d_maxpool_fwd(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(y), ctypes.byref(d),
+                                             ctypes.byref(pd) if pool else None, _stream()))
+    return y
+
+
 def adaptive_avgpool2d(x: torch.Tensor, c: int, out_hw, act=ACT_NONE, out_f32=False) -> torch.Tensor:
     n, h, w, cs = x.shape
     oh, ow = _pair(out_hw)

@@ -103,3 +103,24 @@ def test_splitk_workspace_queries():
     L = abi.lib()
     assert L.lotus_linear_workspace_bytes(32, 9216, 4096) > 0
     assert L.lotus_linear_workspace_bytes(4, 9216, 4096) == 0            # batch <= 8 runs the GEMV
+
+
+def test_conv2d_maxpool_support_query():
+    """The fused conv + pool entry point says which shapes it takes, without a GPU."""
+    from lotusinfer_b200 import abi
+    from lotusinfer_b200.abi import Conv2dDesc, Pool2dDesc
+    L = abi.lib()
+    ok = Conv2dDesc(256, 12, 115, 115, 64, 4, 4, 1, 1, 0, 0, 1, 0)
+    pool = Pool2dDesc(256, 64, 112, 112, 3, 3, 2, 2, 1, 1, 0)
+    assert L.lotus_conv2d_maxpool_supported(ctypes.byref(ok), ctypes.byref(pool)) == 0
+    assert L.lotus_conv2d_maxpool_supported(ctypes.byref(ok), None) == 0
+    padded = Conv2dDesc(1, 64, 56, 56, 64, 3, 3, 1, 1, 1, 1, 1, 0)
+    assert L.lotus_conv2d_maxpool_supported(ctypes.byref(padded), None) == -2
+    wide = Conv2dDesc(1, 12, 200, 200, 64, 4, 4, 1, 1, 0, 0, 1, 0)  # 197-pixel output rows
+    assert L.lotus_conv2d_maxpool_supported(ctypes.byref(wide), None) == -2
+    cout128 = Conv2dDesc(1, 12, 115, 115, 128, 4, 4, 1, 1, 0, 0, 1, 0)
+    assert L.lotus_conv2d_maxpool_supported(ctypes.byref(cout128), None) == -2
+    pool2 = Pool2dDesc(256, 64, 112, 112, 2, 2, 2, 2, 0, 0, 0)
+    assert L.lotus_conv2d_maxpool_supported(ctypes.byref(ok), ctypes.byref(pool2)) == -2
+    wrong_in = Pool2dDesc(256, 64, 111, 112, 3, 3, 2, 2, 1, 1, 0)
+    assert L.lotus_conv2d_maxpool_supported(ctypes.byref(ok), ctypes.byref(wrong_in)) == -1

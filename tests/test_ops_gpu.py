@@ -383,3 +383,71 @@ def test_tconv2d_parity(case):
         y = K.tconv2d(K.to_nhwc(_gpu(x)), cin, wp, _gpu(b), cout, k, s, p, op, act)
         assert_close(K.from_nhwc(y, cout).cpu().numpy(), want, what=f"{case[0]} act={act}")
     _no_device_error()
+
+
+ROW_CASES = [
+    # id, n, c_in, h, w, cout, (kh, kw), act, pool
+    # the space-to-depth ResNet stem (12 channels padded to 16, 4x4) and its 3x3/2 pool
+    ("stem_s2d_bs2_pool", 2, 12, 115, 115, 64, (4, 4), 1, True),
+    ("stem_s2d_bs8_pool", 8, 12, 115, 115, 64, (4, 4), 1, True),  # CTA ranges cross images
+    ("stem_s2d_bs1_conv_only", 1, 12, 115, 115, 64, (4, 4), 1, False),
+    # odd conv height and width (last pooled row has no row below), 40 channels (pad channels)
+    ("odd_rows_cout40_pool", 3, 16, 20, 19, 40, (4, 4), 0, True),
+    ("cin32_kw2_sigmoid_pool", 2, 32, 9, 30, 64, (2, 2), 2, True),
+    ("cin8_kw8_kh5_conv_only", 2, 8, 16, 40, 24, (5, 8), 1, False),
+    ("one_row_per_image_pool", 5, 16, 4, 50, 64, (4, 4), 1, True),  # OH = 1
+]
+
+
+@pytest.mark.parametrize("case", ROW_CASES, ids=[c[0] for c in ROW_CASES])
+def test_conv2d_maxpool_row_kernel(case):
+    K = _k()
+    _, n, c, h, w, cout, (kh, kw), act, pool = case
+    rng = _rng(zlib.crc32(case[0].encode()))
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / (c * kh * kw)), (cout, c, kh, kw)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, cout).astype(np.float32)
+    conv = oracle.conv2d(x, wt, b, (1, 1), (0, 0), act)
+    want = oracle.maxpool2d(conv, (3, 3), (2, 2), (1, 1)) if pool else conv
+    xg = K.to_nhwc(_gpu(x))
+    wp = K.conv2d_prepack(_gpu(wt), c)
+    y = K.conv2d_maxpool(xg, c, wp, _gpu(b), cout, (kh, kw), act, pool=pool)
+    got = K.from_nhwc(y, cout).cpu().numpy()
+    assert_close(got, want, what=case[0])
+    if y.shape[-1] != cout:
+        assert torch.count_nonzero(y[..., cout:]).item() == 0
+    _no_device_error()
+
+
+def test_conv2d_maxpool_row_map_variants_agree(monkeypatch):
+    """The input-row map as one overlapping 64-value run (4-D) and with the
+    taps as their own dimension (5-D) give bit-identical results."""
+    K = _k()
+    rng = _rng(7)
+    x = rng.uniform(-1, 1, (2, 12, 115, 115)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / 192), (64, 12, 4, 4)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, 64).astype(np.float32)
+    xg = K.to_nhwc(_gpu(x))
+    wp = K.conv2d_prepack(_gpu(wt), 12)
+    y4 = K.conv2d_maxpool(xg, 12, wp, _gpu(b), 64, 4, 1)
+    monkeypatch.setenv("LOTUS_ROW_TMAP", "5")
+    y5 = K.conv2d_maxpool(xg, 12, wp, _gpu(b), 64, 4, 1)
+    assert torch.equal(y4, y5)
+    _no_device_error()
+
+
+def test_conv2d_maxpool_matches_separate_conv_and_pool():
+    """Fused result equals the library's own conv followed by its max pool,
+    bit for bit (same fp16 rounding of the conv output, max is exact)."""
+    K = _k()
+    rng = _rng(11)
+    x = rng.uniform(-1, 1, (4, 12, 115, 115)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / 192), (64, 12, 4, 4)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, 64).astype(np.float32)
+    xg = K.to_nhwc(_gpu(x))
+    wp = K.conv2d_prepack(_gpu(wt), 12)
+    fused = K.conv2d_maxpool(xg, 12, wp, _gpu(b), 64, 4, 1)
+    conv = K.conv2d(xg, 12, wp, _gpu(b), 64, 4, 1, 0, 1)
+    sep = K.maxpool2d(conv, 64, 3, 2, 1)
+    assert torch.equal(fused, sep)
+    _no_device_error()
