@@ -148,6 +148,137 @@ def parity_check(got, want):
             "min_oracle_margin": float((srt[:, -1] - srt[:, -2]).min())}
 
 
+# ----------------------------------------------------------------- per-op / per-model measurements
+# ResNet-18 layer shapes at batch B (NHWC fp16): (c_in, h, w, c_out, k, stride, pad, residual)
+LAYERS = {
+    "stem": (3, 224, 224, 64, 7, 2, 3, False),
+    "stem_s2d": (12, 115, 115, 64, 4, 1, 0, False),   # the stem after the space-to-depth rewrite
+    "s1": (64, 56, 56, 64, 3, 1, 1, True),
+    "s2d": (64, 56, 56, 128, 3, 2, 1, False),
+    "s2": (128, 28, 28, 128, 3, 1, 1, True),
+    "s3": (256, 14, 14, 256, 3, 1, 1, True),
+    "s4": (512, 7, 7, 512, 3, 1, 1, True),
+    "ds2": (64, 56, 56, 128, 1, 2, 0, False),
+}
+OPS = sorted(["layer", "stem_pool", "conv_cfg1", "gemm_cfg2", "gemv_cfg2", "gemv_fc6", "maxpool"])
+
+
+def _events_ms(fn, reps, stream=None):
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def run_op(args):
+    """One operator of the path, timed with CUDA events over --reps launches
+    after --warmup launches; one JSON line.  FLOPs are 2*M*N*K of the model
+    op (no padding); bytes are the algorithmic bytes read + written once."""
+    import torch
+    from lotusinfer_b200 import abi
+    from lotusinfer_b200 import kernels as K
+    torch.manual_seed(0)
+    dev = torch.device("cuda:0")
+    peak, peak_sus, hbm, peak_src = _peaks()
+    B = args.batch
+    out = {"op": args.op, "batch": B, "reps": args.reps}
+    if args.op in ("layer", "stem_pool"):
+        name = "stem_s2d" if args.op == "stem_pool" else args.layer
+        c, h, w, cout, k, s, p, res = LAYERS[name]
+        x = K.to_nhwc(torch.randn(B, c, h, w, device=dev))
+        wt = torch.randn(cout, c, k, k, device=dev) * (2.0 / (c * k * k)) ** 0.5
+        wp = K.conv2d_prepack(wt, c)
+        bias = torch.rand(cout, device=dev) * 0.2 - 0.1
+        oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+        if args.op == "stem_pool":
+            fn = lambda: K.conv2d_maxpool(x, c, wp, bias, cout, k, 1)  # noqa: E731
+            # model FLOPs of the 7x7/2 stem (3 channels), which this conv computes after the rewrite
+            flops = 2.0 * B * oh * ow * cout * 3 * 7 * 7
+            ph, pw = (oh - 1) // 2 + 1, (ow - 1) // 2 + 1
+            nbytes = B * h * w * abi.channel_stride(c) * 2 + B * ph * pw * cout * 2
+            out["layer"] = "stem (space-to-depth 4x4 over 16 channels) + 3x3/2 max pool, fused"
+        else:
+            r = K.to_nhwc(torch.randn(B, cout, oh, ow, device=dev)) if res else None
+            fn = lambda: K.conv2d(x, c, wp, bias, cout, k, s, p, 1, residual=r)  # noqa: E731
+            flops = 2.0 * B * oh * ow * cout * c * k * k
+            nbytes = (B * h * w * abi.channel_stride(c) + B * oh * ow * cout * (2 if res else 1)) * 2
+            out["layer"] = name
+    elif args.op == "conv_cfg1":
+        x = K.to_nhwc(torch.rand(B, 64, 56, 56, device=dev) * 2 - 1)
+        wp = K.conv2d_prepack(torch.randn(64, 64, 3, 3, device=dev) * (2.0 / 576) ** 0.5, 64)
+        bias = torch.rand(64, device=dev) * 0.2 - 0.1
+        fn = lambda: K.conv2d(x, 64, wp, bias, 64, 3, 1, 1, 1)  # noqa: E731
+        flops = 2.0 * B * 56 * 56 * 64 * 576
+        nbytes = (2 * B * 56 * 56 * 64 + 64 * 576) * 2
+    elif args.op == "gemm_cfg2":
+        xa = (torch.rand(B, 512, device=dev) * 2 - 1).half()
+        wp = K.linear_prepack(torch.randn(1000, 512, device=dev) / 512 ** 0.5)
+        bias = torch.rand(1000, device=dev) * 0.2 - 0.1
+        fn = lambda: K.linear(xa, wp, bias, 512, 1000, out_f32=True, force_gemm=True)  # noqa: E731
+        flops = 2.0 * B * 1000 * 512
+        nbytes = (B * 512 + 1000 * 512) * 2 + B * 1000 * 4
+    else:  # GEMV family and max pool: HBM-bound
+        if args.op in ("gemv_cfg2", "gemv_fc6"):
+            hh, ww = (1000, 512) if args.op == "gemv_cfg2" else (4096, 9216)
+            wm = torch.randn(hh, ww, device=dev) / ww ** 0.5
+            xv = torch.rand(1, ww, device=dev) * 2 - 1
+            bias = torch.rand(hh, device=dev) * 0.2 - 0.1
+            fn = lambda: K.gemv(wm, xv, bias)  # noqa: E731
+            flops = 2.0 * hh * ww
+            nbytes = (hh * ww + ww + 2 * hh) * 4
+            out["shape"] = f"{hh}x{ww} fp32 weights, batch 1"
+        else:
+            x = K.to_nhwc(torch.rand(B, 64, 112, 112, device=dev))
+            fn = lambda: K.maxpool2d(x, 64, 3, 2, 1)  # noqa: E731
+            flops = 0.0
+            nbytes = B * 64 * (112 * 112 + 56 * 56) * 2
+            out["shape"] = f"{B}x64x112x112 -> 56x56, 3x3/2 pad 1, NHWC fp16"
+    for _ in range(max(args.warmup, 1)):
+        fn()
+    ms = _events_ms(fn, args.reps)
+    out.update({"ms": ms, "gflop": flops / 1e9, "mbytes": nbytes / 1e6,
+                "tflops": flops / ms / 1e9 if flops else None, "gbs": nbytes / ms / 1e6,
+                "frac_tensor_peak": (flops / ms / 1e9) / peak if flops else None,
+                "frac_hbm_peak": (nbytes / ms / 1e6) / hbm, "peak_source": peak_src,
+                "l2": "operands fit in the 126 MB L2 (latency figure)" if nbytes < 100e6 else "operands exceed L2"})
+    assert abi.device_error() == 0
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_model(args):
+    """Whole-network forward of --model at --batch: CUDA-graph replay timed
+    with CUDA events (images/s, TFLOP/s of the model's FLOPs), or with
+    --eager N eager passes (every layer its own launch, for launch lists)."""
+    import torch
+    from lotusinfer_b200 import abi, synth
+    from lotusinfer_b200.graph import Graph
+    param, binp = synth.make_model(args.model, MODEL_DIR, seed=0)
+    g = Graph(param, binp, args.batch, cuda_graph=args.eager == 0)
+    g.set_input(synth.synthetic_input(args.model, args.batch, seed=0))
+    s = torch.cuda.ExternalStream(g.stream)
+    passes = args.eager if args.eager else args.reps
+    for _ in range(0 if args.eager else max(args.warmup, 3)):
+        g.forward()
+    g.synchronize()
+    ms = _events_ms(g.forward, passes, s)
+    flops = sum(l["flops"] for l in g.layers())
+    peak, _, _, peak_src = _peaks()
+    print(json.dumps({"model": args.model, "batch": args.batch, "mode": "eager" if args.eager else "cuda-graph",
+                      "passes": passes, "ms_per_forward": ms, "images_per_s": args.batch / ms * 1e3,
+                      "gflop_per_forward": flops / 1e9, "tflops": flops / ms / 1e9,
+                      "frac_tensor_peak": flops / ms / 1e9 / peak, "peak_source": peak_src,
+                      "launches_per_forward": g.launches_per_forward()}), flush=True)
+    g.close()
+    assert abi.device_error() == 0
+    return 0
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -188,10 +319,19 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-reps", type=int, default=5)
+    ap.add_argument("--op", choices=OPS, help="time one operator instead of the ResNet-18 step")
+    ap.add_argument("--layer", default="s1", choices=sorted(LAYERS), help="ResNet-18 layer shape for --op layer")
+    ap.add_argument("--reps", type=int, default=20, help="timed launches of --op / --model")
+    ap.add_argument("--model", choices=["resnet18", "unet", "alexnet"], help="time one network's forward")
+    ap.add_argument("--eager", type=int, default=0, help="--model: N eager passes instead of CUDA-graph replay")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.impl == "reference":
         return run_reference(args)
+    if args.op:
+        return run_op(args)
+    if args.model:
+        return run_model(args)
 
     import torch
     import torch.distributed as dist

@@ -24,11 +24,11 @@
 // Roles (352 threads):
 //   warps 0-7   epilogue: warp w drains TMEM lane quarter w%4, columns
 //               32*(w/4) .. +31: bias, activation, fp16, then either the
-//               conv row itself or the max pool: the horizontal 3-wide max
-//               by warp shuffles (lane 0's left neighbour comes from the
-//               previous quarter through shared memory), the vertical max
-//               carried in registers from row to row (a thread always holds
-//               the same ox and channels);
+//               conv row itself or the max pool: the vertical max carried in
+//               registers from row to row (a thread always holds the same ox
+//               and channels), then once per pooled row the horizontal
+//               3-wide max by warp shuffles (lane 0's left neighbour comes
+//               from the previous quarter through shared memory);
 //   warp 8      TMEM allocation, MMA issuer 0 (even tiles);
 //   warp 9      TMA producer: the weights once, then input rows in order;
 //   warp 10     MMA issuer 1 (odd tiles).
@@ -79,7 +79,6 @@ struct RowParams {
   int PH, PW;        // pooled size (pool == 1)
   int units;         // N * (pool ? PH : OH)
   int w_bytes;       // kh * kWBlockBytes
-  int map5;          // input-row map has the kw taps as their own dimension
   uint32_t wait_limit;
 };
 
@@ -167,7 +166,7 @@ __device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint
   uint32_t carry[16], vmax[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) carry[k] = vmax[k] = kNegInf2;
-  int lt = 0;
+  int lt = 0, prow = 0;
   int u = u0;
   Seg sg;
   while (next_seg(p, u, u1, sg)) {
@@ -203,47 +202,48 @@ __device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint
           store_row32(p.y + ((static_cast<int64_t>(sg.n) * p.OH + oy) * p.OW + ox) * p.Cs_out + c0, h, c0, p.Cs_out);
         continue;
       }
-      // horizontal 3-wide max at even ox; lane 0's left neighbour (ox - 1)
-      // is lane 31 of the previous quarter, exchanged through shared memory
-      uint32_t* eg = edge + ((lt & 1) * 8 + q * 2 + hc) * 16;
-      if (lane == 31) {
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          reinterpret_cast<uint4*>(eg)[s] = make_uint4(h[4 * s], h[4 * s + 1], h[4 * s + 2], h[4 * s + 3]);
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-      const uint32_t* eprev = edge + ((lt & 1) * 8 + (q > 0 ? q - 1 : 0) * 2 + hc) * 16;
-      uint32_t m[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        uint32_t left = __shfl_up_sync(0xffffffffu, h[k], 1);
-        const uint32_t right = __shfl_down_sync(0xffffffffu, h[k], 1);
-        if (lane == 0) left = q > 0 ? eprev[k] : kNegInf2;
-        m[k] = hmax3_u32(left, h[k], right);
-      }
-      const bool out_lane = ok && xvalid && (ox & 1) == 0;
-      __half* yrow = nullptr;
+      // vertical max first, in registers (a thread always holds the same ox
+      // and channels): carried row 2py-1, then 2py, then 2py+1
+      bool close = false;  // this row completes a pooled row of the segment
       if (oy & 1) {
-        // odd row 2py+1 closes pooled row py, unless it only carries into
-        // this segment's first pooled row
-        if (oy != sg.lo) {
-          uint32_t o[16];
+        if (oy != sg.lo) {  // (else it only carries into the segment's first pooled row)
 #pragma unroll
-          for (int k = 0; k < 16; ++k) o[k] = hmax2_u32(vmax[k], m[k]);
-          yrow = p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0;
-          if (out_lane) store_row32(yrow, o, c0, p.Cs_out);
+          for (int k = 0; k < 16; ++k) vmax[k] = hmax2_u32(vmax[k], h[k]);
+          close = true;
         }
 #pragma unroll
-        for (int k = 0; k < 16; ++k) carry[k] = m[k];
+        for (int k = 0; k < 16; ++k) carry[k] = h[k];
         carry_ok = true;
       } else {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) vmax[k] = carry_ok ? hmax2_u32(carry[k], m[k]) : m[k];
-        if (oy == p.OH - 1) {  // an odd-height map's last pooled row has no row below
-          yrow = p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0;
-          if (out_lane) store_row32(yrow, vmax, c0, p.Cs_out);
-        }
+        for (int k = 0; k < 16; ++k) vmax[k] = carry_ok ? hmax2_u32(carry[k], h[k]) : h[k];
+        close = oy == p.OH - 1;  // an odd-height map's last pooled row has no row below
       }
+      if (!close) continue;  // uniform over the epilogue warps: depends on oy and the segment only
+      // horizontal 3-wide max at even ox, once per pooled row; lane 0's left
+      // neighbour (ox - 1) is lane 31 of the previous quarter, exchanged
+      // through shared memory (double-buffered by pooled-row parity, so one
+      // barrier per pooled row suffices)
+      uint32_t* eg = edge + ((prow & 1) * 8 + q * 2 + hc) * 16;
+      if (lane == 31) {
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          reinterpret_cast<uint4*>(eg)[s] = make_uint4(vmax[4 * s], vmax[4 * s + 1], vmax[4 * s + 2], vmax[4 * s + 3]);
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+      const uint32_t* eprev = edge + ((prow & 1) * 8 + (q > 0 ? q - 1 : 0) * 2 + hc) * 16;
+      ++prow;
+      uint32_t o[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        uint32_t left = __shfl_up_sync(0xffffffffu, vmax[k], 1);
+        const uint32_t right = __shfl_down_sync(0xffffffffu, vmax[k], 1);
+        if (lane == 0) left = q > 0 ? eprev[k] : kNegInf2;
+        o[k] = hmax3_u32(left, vmax[k], right);
+      }
+      if (ok && xvalid && (ox & 1) == 0)
+        store_row32(p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0, o, c0,
+                    p.Cs_out);
     }
   }
 }
@@ -322,10 +322,7 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
             break;
           }
           mbar_arrive_expect_tx(&rfull[slot], kSlotBytes);
-          if (p.map5)
-            tma_load_5d(ring + slot * kSlotBytes, &tmap_x, &rfull[slot], 0, 0, 0, yin, sg.n);
-          else
-            tma_load_4d(ring + slot * kSlotBytes, &tmap_x, &rfull[slot], 0, 0, yin, sg.n);
+          tma_load_4d(ring + slot * kSlotBytes, &tmap_x, &rfull[slot], 0, 0, yin, sg.n);
         }
       }
       if (!ok) *abort_flag = 1;
@@ -415,33 +412,19 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
 // Input rows of the NHWC activation as 64-value runs: element (e, x, y, n)
 // is x[n, y, x + e / Cs_in, e % Cs_in], so dimension 0 (64 contiguous fp16 =
 // kw pixels) overlaps the next pixel's run (stride Cs_in * 2 bytes).  Box
-// {64, 128, 1, 1}, 128B swizzle; x < OW keeps every run inside its image row
-// and x >= OW reads zeros.  Variant 5 describes the same bytes with the kw
-// taps as their own dimension (box inner 32 bytes), in case the encoder
-// refuses the overlapping innermost run.
-int make_row_map(CUtensorMap* map, const ConvRowArgs& a, int ow, int variant) {
+// {64, 128, 1, 1} = 16 KB, 128B swizzle (inner box = swizzle span); x < OW
+// keeps every run inside its image row and x >= OW reads zeros.
+int make_row_map(CUtensorMap* map, const ConvRowArgs& a, int ow) {
   auto enc = encode_tiled();
   if (!enc) return -1;
   const cuuint64_t px = static_cast<cuuint64_t>(a.Cs_in) * 2;
-  CUresult r;
-  if (variant == 4) {
-    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(ow), static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.N)};
-    cuuint64_t strides[3] = {px, px * a.W, px * a.W * a.H};
-    cuuint32_t box[4] = {64, kRowPos, 1, 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  } else {
-    cuuint64_t dims[5] = {static_cast<cuuint64_t>(a.Cs_in), static_cast<cuuint64_t>(a.kw),
-                          static_cast<cuuint64_t>(ow), static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.N)};
-    cuuint64_t strides[4] = {px, px, px * a.W, px * a.W * a.H};
-    cuuint32_t box[5] = {static_cast<cuuint32_t>(a.Cs_in), static_cast<cuuint32_t>(a.kw), kRowPos, 1, 1};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(a.x), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  }
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(ow), static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.N)};
+  cuuint64_t strides[3] = {px, px * a.W, px * a.W * a.H};
+  cuuint32_t box[4] = {64, kRowPos, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
@@ -514,10 +497,7 @@ int conv_row_launch(const ConvRowArgs& a, cudaStream_t stream, const char** err)
     *err = "row conv: weight tensor map encoding failed";
     return -3;
   }
-  const char* v = std::getenv("LOTUS_ROW_TMAP");
-  const bool force5 = v && std::atoi(v) == 5;
-  p.map5 = (force5 || make_row_map(&mx, a, p.OW, 4) != 0) ? 1 : 0;
-  if (p.map5 && make_row_map(&mx, a, p.OW, 5) != 0) {
+  if (make_row_map(&mx, a, p.OW) != 0) {
     *err = "row conv: input-row tensor map encoding failed";
     return -2;
   }

@@ -158,16 +158,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       : "memory");
 }
 
-// 5-D tiled load (no multicast), coordinates innermost first, same rules.
-__device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1, int c2,
-                                            int c3, int c4) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // 4-D im2col load (no multicast) of `pixels x channels` rows of an NHWC
 // tensor: coordinates (c, w, h, n) of the first output pixel's window corner
 // inside the map's bounding box, plus the filter tap offsets (s, r).

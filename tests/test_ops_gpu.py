@@ -419,23 +419,6 @@ def test_conv2d_maxpool_row_kernel(case):
     _no_device_error()
 
 
-def test_conv2d_maxpool_row_map_variants_agree(monkeypatch):
-    """The input-row map as one overlapping 64-value run (4-D) and with the
-    taps as their own dimension (5-D) give bit-identical results."""
-    K = _k()
-    rng = _rng(7)
-    x = rng.uniform(-1, 1, (2, 12, 115, 115)).astype(np.float32)
-    wt = rng.normal(0, np.sqrt(2.0 / 192), (64, 12, 4, 4)).astype(np.float32)
-    b = rng.uniform(-0.1, 0.1, 64).astype(np.float32)
-    xg = K.to_nhwc(_gpu(x))
-    wp = K.conv2d_prepack(_gpu(wt), 12)
-    y4 = K.conv2d_maxpool(xg, 12, wp, _gpu(b), 64, 4, 1)
-    monkeypatch.setenv("LOTUS_ROW_TMAP", "5")
-    y5 = K.conv2d_maxpool(xg, 12, wp, _gpu(b), 64, 4, 1)
-    assert torch.equal(y4, y5)
-    _no_device_error()
-
-
 def test_conv2d_maxpool_matches_separate_conv_and_pool():
     """Fused result equals the library's own conv followed by its max pool,
     bit for bit (same fp16 rounding of the conv output, max is exact)."""
