@@ -21,17 +21,18 @@
 // output row oy reads slots of input rows oy .. oy+kh-1, so every input row
 // is loaded once per CTA segment and serves kh output rows.
 //
-// Roles (352 threads):
-//   warps 0-7   epilogue: warp w drains TMEM lane quarter w%4, columns
-//               32*(w/4) .. +31: bias, activation, fp16, then either the
-//               conv row itself or the max pool: the vertical max carried in
-//               registers from row to row (a thread always holds the same ox
-//               and channels), then once per pooled row the horizontal
-//               3-wide max by warp shuffles (lane 0's left neighbour comes
-//               from the previous quarter through shared memory);
-//   warp 8      TMEM allocation, MMA issuer 0 (even tiles);
-//   warp 9      TMA producer: the weights once, then input rows in order;
-//   warp 10     MMA issuer 1 (odd tiles).
+// Roles (608 threads):
+//   warps 0-15  epilogue: warp w drains TMEM lane quarter w%4, columns
+//               16*(w/4) .. +15.  Without the pool: bias, activation, fp16
+//               store of the conv row.  With the pool: fp16(acc + bias), its
+//               vertical max carried in registers from row to row (a thread
+//               always holds the same ox and channels), then once per pooled
+//               row the horizontal 3-wide max by warp shuffles (lane 0's
+//               left neighbour comes from the previous quarter through
+//               shared memory), then the activation of the pooled pixel;
+//   warp 16     TMEM allocation, MMA issuer 0 (even tiles);
+//   warp 17     TMA producer: the weights once, then input rows in order;
+//   warp 18     MMA issuer 1 (odd tiles).
 // Each CTA owns a contiguous range of output units (pooled rows, or conv
 // rows without the pool) over the whole batch, walked as per-image
 // segments; with the pool a segment also computes the conv row just above
@@ -67,9 +68,10 @@ constexpr int kSlotBytes = kRowPos * 128;      // one input row: 128 rows x 128 
 constexpr int kRowAcc = 8;                     // TMEM accumulators of 64 columns
 constexpr int kRowMaxKh = kRowSlots - 2;       // a tile's loads plus the next tile's fit the ring
 constexpr int kWBlockBytes = 64 * 128;         // one 64-wide K block of 64 weight rows
-constexpr int kEpiWarps = 8;
-constexpr int kIssuer0 = 8, kProducer = 9, kIssuer1 = 10;
-constexpr int kThreads = 11 * 32;
+constexpr int kEpiWarps = 16;                  // 4 per TMEM lane quarter, 16 columns each
+constexpr int kEpiCols = 64 / (kEpiWarps / 4);
+constexpr int kIssuer0 = kEpiWarps, kProducer = kEpiWarps + 1, kIssuer1 = kEpiWarps + 2;
+constexpr int kThreads = (kEpiWarps + 3) * 32;
 
 struct RowParams {
   const float* bias;
@@ -91,7 +93,7 @@ constexpr int kNumBars = 1 + 2 * kRowSlots + 2 * kRowAcc + 1;
 constexpr int kMiscOff = kBarOff + kNumBars * 8;
 constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
 constexpr int kEdgeOff = kBiasOff + 64 * 4;
-constexpr int kEdgeBytes = 2 * 4 * 2 * 64;  // [tile parity][quarter][column half][32 fp16]
+constexpr int kEdgeBytes = 2 * kEpiWarps * kEpiCols * 2;  // [pooled-row parity][warp][16 fp16]
 constexpr int kSmemBytes = kEdgeOff + kEdgeBytes + 1024;
 static_assert(kSmemBytes <= 232448, "row kernel shared memory above 227 KB");
 
@@ -120,22 +122,10 @@ __device__ __forceinline__ bool next_seg(const RowParams& p, int& u, int u1, Seg
   return true;
 }
 
-__device__ __forceinline__ uint32_t hmax3_u32(uint32_t a, uint32_t b, uint32_t c) {
-  __half2 x = *reinterpret_cast<__half2*>(&a), y = *reinterpret_cast<__half2*>(&b),
-          z = *reinterpret_cast<__half2*>(&c);
-  __half2 m = __hmax2(__hmax2(x, y), z);
-  return *reinterpret_cast<uint32_t*>(&m);
-}
-__device__ __forceinline__ uint32_t hmax2_u32(uint32_t a, uint32_t b) {
-  __half2 x = *reinterpret_cast<__half2*>(&a), y = *reinterpret_cast<__half2*>(&b);
-  __half2 m = __hmax2(x, y);
-  return *reinterpret_cast<uint32_t*>(&m);
-}
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
-constexpr uint32_t kNegInf2 = 0xFC00FC00u;  // two fp16 -inf
 
 template <int ACT>
 __device__ __forceinline__ float act_f(float v) {
@@ -144,28 +134,42 @@ __device__ __forceinline__ float act_f(float v) {
   return v;
 }
 
-// 32 consecutive fp16 (64 bytes) from registers to global memory.
-__device__ __forceinline__ void store_row32(__half* dst, const uint32_t (&h)[16], int c0, int cs_out) {
-#pragma unroll
-  for (int s = 0; s < 4; ++s)
-    if (c0 + 8 * s < cs_out)
-      *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(h[4 * s], h[4 * s + 1], h[4 * s + 2], h[4 * s + 3]);
+__device__ __forceinline__ uint32_t hmax2_u32(uint32_t a, uint32_t b) {
+  __half2 x = *reinterpret_cast<__half2*>(&a), y = *reinterpret_cast<__half2*>(&b);
+  __half2 m = __hmax2(x, y);
+  return *reinterpret_cast<uint32_t*>(&m);
 }
+constexpr uint32_t kNegInf2 = 0xFC00FC00u;  // two fp16 -inf
 
+// Epilogue warps.  Each thread keeps its 16 bias values in registers.
+// Without the pool: act(acc + bias) -> fp16 store of the conv row.  With the
+// pool: fp16(acc + bias) per conv row, the 3x3 window max on those fp16
+// values (vertical in registers, horizontal by shuffles once per pooled row),
+// then the activation of the pooled value.  Rounding to fp16 and the
+// ReLU / identity activations are non-decreasing and ReLU commutes with the
+// rounding, so this equals pooling the conv output the unfused kernels store,
+// bit for bit (a sigmoid activation is applied to the rounded maximum).
 template <int ACT>
 __device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint64_t* tfull, uint64_t* tempty,
                                          volatile int* abort_flag, uint32_t tmem_base, int u0, int u1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = warp & 3, hc = warp >> 2;
+  const int q = warp & 3, cg = warp >> 2;
   const int ox = q * 32 + lane;
   const bool xvalid = ox < p.OW;
-  const int c0 = hc * 32;
-  const float* s_bias = reinterpret_cast<const float*>(smem + kBiasOff);
+  const int c0 = cg * kEpiCols;
+  const bool pad = c0 + kEpiCols > p.Cout;  // this warp's columns reach past Cout (warp-uniform)
+  const bool odd_w = (p.OW & 1) != 0;       // the last pooled column has no right neighbour
+  float bias[kEpiCols];
+  {
+    const float* s_bias = reinterpret_cast<const float*>(smem + kBiasOff);
+#pragma unroll
+    for (int k = 0; k < kEpiCols; ++k) bias[k] = s_bias[c0 + k];
+  }
   uint32_t* edge = reinterpret_cast<uint32_t*>(smem + kEdgeOff);
   const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
-  uint32_t carry[16], vmax[16];
+  uint32_t carry[kEpiCols / 2], vmax[kEpiCols / 2];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) carry[k] = vmax[k] = kNegInf2;
+  for (int k = 0; k < kEpiCols / 2; ++k) carry[k] = vmax[k] = kNegInf2;
   int lt = 0, prow = 0;
   int u = u0;
   Seg sg;
@@ -173,12 +177,13 @@ __device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint
     bool carry_ok = false;
     for (int oy = sg.lo; oy <= sg.hi; ++oy, ++lt) {
       const int ab = lt % kRowAcc;
-      bool ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / kRowAcc) & 1, kErrWaitAccum, p.wait_limit);
-      ok = __all_sync(0xffffffffu, ok);
+      bool ok = true;
+      if (lane == 0) ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / kRowAcc) & 1, kErrWaitAccum, p.wait_limit);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
       tc_fence_after();
-      uint32_t v[32];
+      uint32_t r[kEpiCols];
       if (ok) {
-        tmem_ld_32x32b_x32(tmem_base + t_lane + ab * 64 + c0, v);
+        tmem_ld_32x32b_x16(tmem_base + t_lane + ab * 64 + c0, r);
         tmem_ld_wait();
       }
       tc_fence_before();
@@ -187,20 +192,33 @@ __device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint
         mbar_arrive(&tempty[ab]);
         if (!ok) *abort_flag = 1;
       }
-      uint32_t h[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int c = c0 + 2 * k;
-        float f0 = ok ? act_f<ACT>(__uint_as_float(v[2 * k]) + s_bias[c]) : 0.f;
-        float f1 = ok ? act_f<ACT>(__uint_as_float(v[2 * k + 1]) + s_bias[c + 1]) : 0.f;
-        if (c >= p.Cout) f0 = 0.f;  // pad channels stay zero
-        if (c + 1 >= p.Cout) f1 = 0.f;
-        h[k] = xvalid ? pack2(f0, f1) : kNegInf2;
-      }
       if (!p.pool) {
-        if (ok && xvalid)
-          store_row32(p.y + ((static_cast<int64_t>(sg.n) * p.OH + oy) * p.OW + ox) * p.Cs_out + c0, h, c0, p.Cs_out);
+        if (ok && xvalid) {
+          uint32_t h[kEpiCols / 2];
+#pragma unroll
+          for (int k = 0; k < kEpiCols / 2; ++k) {
+            float f0 = act_f<ACT>(__uint_as_float(r[2 * k]) + bias[2 * k]);
+            float f1 = act_f<ACT>(__uint_as_float(r[2 * k + 1]) + bias[2 * k + 1]);
+            if (pad && c0 + 2 * k >= p.Cout) f0 = 0.f;  // pad channels stay zero
+            if (pad && c0 + 2 * k + 1 >= p.Cout) f1 = 0.f;
+            h[k] = pack2(f0, f1);
+          }
+          __half* dst = p.y + ((static_cast<int64_t>(sg.n) * p.OH + oy) * p.OW + ox) * p.Cs_out + c0;
+#pragma unroll
+          for (int s = 0; s < kEpiCols / 8; ++s)
+            if (c0 + 8 * s < p.Cs_out)
+              *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(h[4 * s], h[4 * s + 1], h[4 * s + 2], h[4 * s + 3]);
+        }
         continue;
+      }
+      // fp16(acc + bias) of this conv row (garbage when !ok: never stored)
+      uint32_t h[kEpiCols / 2];
+#pragma unroll
+      for (int k = 0; k < kEpiCols / 2; ++k)
+        h[k] = pack2(__uint_as_float(r[2 * k]) + bias[2 * k], __uint_as_float(r[2 * k + 1]) + bias[2 * k + 1]);
+      if (odd_w && !xvalid) {
+#pragma unroll
+        for (int k = 0; k < kEpiCols / 2; ++k) h[k] = kNegInf2;
       }
       // vertical max first, in registers (a thread always holds the same ox
       // and channels): carried row 2py-1, then 2py, then 2py+1
@@ -208,42 +226,72 @@ __device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint
       if (oy & 1) {
         if (oy != sg.lo) {  // (else it only carries into the segment's first pooled row)
 #pragma unroll
-          for (int k = 0; k < 16; ++k) vmax[k] = hmax2_u32(vmax[k], h[k]);
+          for (int k = 0; k < kEpiCols / 2; ++k) vmax[k] = hmax2_u32(vmax[k], h[k]);
           close = true;
         }
 #pragma unroll
-        for (int k = 0; k < 16; ++k) carry[k] = h[k];
+        for (int k = 0; k < kEpiCols / 2; ++k) carry[k] = h[k];
         carry_ok = true;
       } else {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) vmax[k] = carry_ok ? hmax2_u32(carry[k], h[k]) : h[k];
+        for (int k = 0; k < kEpiCols / 2; ++k) vmax[k] = carry_ok ? hmax2_u32(carry[k], h[k]) : h[k];
         close = oy == p.OH - 1;  // an odd-height map's last pooled row has no row below
       }
-      if (!close) continue;  // uniform over the epilogue warps: depends on oy and the segment only
+      // `close` depends on oy and the segment only, so every epilogue warp
+      // reaches the barrier below equally often (whatever `ok` is)
+      if (!close) continue;
       // horizontal 3-wide max at even ox, once per pooled row; lane 0's left
       // neighbour (ox - 1) is lane 31 of the previous quarter, exchanged
       // through shared memory (double-buffered by pooled-row parity, so one
       // barrier per pooled row suffices)
-      uint32_t* eg = edge + ((prow & 1) * 8 + q * 2 + hc) * 16;
+      uint32_t* eg = edge + ((prow & 1) * kEpiWarps + warp) * (kEpiCols / 2);
       if (lane == 31) {
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-          reinterpret_cast<uint4*>(eg)[s] = make_uint4(vmax[4 * s], vmax[4 * s + 1], vmax[4 * s + 2], vmax[4 * s + 3]);
+        reinterpret_cast<uint4*>(eg)[0] = make_uint4(vmax[0], vmax[1], vmax[2], vmax[3]);
+        reinterpret_cast<uint4*>(eg)[1] = make_uint4(vmax[4], vmax[5], vmax[6], vmax[7]);
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-      const uint32_t* eprev = edge + ((prow & 1) * 8 + (q > 0 ? q - 1 : 0) * 2 + hc) * 16;
-      ++prow;
-      uint32_t o[16];
+      uint32_t left[kEpiCols / 2];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        uint32_t left = __shfl_up_sync(0xffffffffu, vmax[k], 1);
-        const uint32_t right = __shfl_down_sync(0xffffffffu, vmax[k], 1);
-        if (lane == 0) left = q > 0 ? eprev[k] : kNegInf2;
-        o[k] = hmax3_u32(left, vmax[k], right);
+      for (int k = 0; k < kEpiCols / 2; ++k) left[k] = __shfl_up_sync(0xffffffffu, vmax[k], 1);
+      if (lane == 0) {
+        if (q > 0) {
+          const uint4* ep = reinterpret_cast<const uint4*>(edge + ((prow & 1) * kEpiWarps + warp - 1) * (kEpiCols / 2));
+          const uint4 e0 = ep[0], e1 = ep[1];
+          left[0] = e0.x; left[1] = e0.y; left[2] = e0.z; left[3] = e0.w;
+          left[4] = e1.x; left[5] = e1.y; left[6] = e1.z; left[7] = e1.w;
+        } else {
+#pragma unroll
+          for (int k = 0; k < kEpiCols / 2; ++k) left[k] = kNegInf2;
+        }
       }
-      if (ok && xvalid && (ox & 1) == 0)
-        store_row32(p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0, o, c0,
-                    p.Cs_out);
+      ++prow;
+      uint32_t o[kEpiCols / 2];
+#pragma unroll
+      for (int k = 0; k < kEpiCols / 2; ++k)
+        o[k] = hmax2_u32(hmax2_u32(left[k], vmax[k]), __shfl_down_sync(0xffffffffu, vmax[k], 1));
+      if (!(ok && xvalid && (ox & 1) == 0)) continue;
+      if (ACT == 1) {
+#pragma unroll
+        for (int k = 0; k < kEpiCols / 2; ++k) o[k] = hmax2_u32(o[k], 0u);
+      } else if (ACT == 2) {
+#pragma unroll
+        for (int k = 0; k < kEpiCols / 2; ++k) {
+          const float2 f = __half22float2(*reinterpret_cast<__half2*>(&o[k]));
+          o[k] = pack2(act_f<2>(f.x), act_f<2>(f.y));
+        }
+      }
+      if (pad) {
+#pragma unroll
+        for (int k = 0; k < kEpiCols / 2; ++k) {
+          if (c0 + 2 * k >= p.Cout) o[k] &= 0xFFFF0000u;  // pad channels stay zero
+          if (c0 + 2 * k + 1 >= p.Cout) o[k] &= 0x0000FFFFu;
+        }
+      }
+      __half* dst = p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0;
+#pragma unroll
+      for (int s = 0; s < kEpiCols / 8; ++s)
+        if (c0 + 8 * s < p.Cs_out)
+          *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(o[4 * s], o[4 * s + 1], o[4 * s + 2], o[4 * s + 3]);
     }
   }
 }

@@ -27,10 +27,15 @@ enum : int {
   kErrWaitAccum = 3,   // epilogue gave up waiting for the accumulator
 };
 
-// One try_wait may suspend for a hardware-defined interval before it
-// returns false; 1<<22 attempts bound a lost arrival to a few seconds.  The
+// Every try_wait carries a suspend-time hint: the waiting thread is suspended
+// until the phase completes or the hint runs out, instead of polling.  Without
+// the hint a try_wait returns after a short hardware-defined interval, and
+// the polling threads (MMA issuers, producers, epilogue warps waiting on an
+// accumulator) take issue slots from the warps that share their scheduler.
+// kMaxWaitIters rounds bound a lost arrival to a few seconds at most.  The
 // kernels take their limit as a launch parameter (this value by default), so
 // that a test can shorten it and make a withheld arrival expire quickly.
+constexpr uint32_t kWaitSuspendNs = 1000;
 constexpr uint32_t kMaxWaitIters = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -65,10 +70,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kWaitSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -94,10 +99,10 @@ __device__ __forceinline__ bool mbar_try_wait_relaxed(uint64_t* bar, uint32_t pa
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.relaxed.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.relaxed.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kWaitSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -246,6 +251,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
         "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
         "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+// 32 lanes x 16 columns of fp32 from TMEM into 16 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
