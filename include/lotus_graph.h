@@ -61,6 +61,28 @@ int lotus_graph_forward_sync(lotus_graph* g);
  * reports such an error at the next waiting call. */
 int lotus_graph_synchronize(lotus_graph* g);
 
+/* Pipelined inference from host memory (the serving path).  Enqueues, for one
+ * batch: the copy of `host_in` (input-shape fp32 elements) to the device on a
+ * host->device copy stream, the forward pass on the graph stream once that
+ * copy has landed, and the copy of the output to `host_out` (output-shape
+ * fp32 elements) on a device->host copy stream.  Two sets of device input and
+ * output buffers alternate between consecutive submissions, so the input copy
+ * of batch i+1 and the output copy of batch i overlap the forward of batch i.
+ * Returns without waiting; both host buffers must stay valid (and should be
+ * pinned, or the copies are not asynchronous) until lotus_graph_synchronize
+ * returns.  The first call sets the pipeline up (allocates slot 1's buffers
+ * and captures one CUDA graph per slot).  *slot (may be NULL) receives the
+ * slot the batch used.  The reference has no counterpart: its
+ * Graph::InitialiseInput / Forward / Output (source/graph.cpp:114-130) copy,
+ * run and read back one batch at a time. */
+int lotus_graph_submit(lotus_graph* g, const float* host_in, float* host_out, int* slot);
+/* Copy streams of the pipelined path (which: 0 host->device, 1 device->host),
+ * e.g. to bracket submissions with CUDA events. */
+cudaStream_t lotus_graph_copy_stream(lotus_graph* g, int which);
+/* Device output buffer of pipeline slot 0 or 1 (slot 0 is the graph's own
+ * output buffer), valid on the graph stream after that slot's forward. */
+float* lotus_graph_slot_output(lotus_graph* g, int slot);
+
 /* Introspection for profiling and tests. */
 int lotus_graph_layer_count(const lotus_graph* g);
 const char* lotus_graph_layer_name(const lotus_graph* g, int i);

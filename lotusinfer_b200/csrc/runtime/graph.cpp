@@ -45,6 +45,18 @@ Graph::Graph(const std::string& param_path, const std::string& bin_path, uint32_
 }
 
 Graph::~Graph() {
+  if (pipe_) {
+    for (cudaStream_t s : {pipe_->h2d, pipe_->d2h})
+      if (s) {
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+      }
+    for (int k = 0; k < 2; ++k) {
+      if (pipe_->exec[k]) cudaGraphExecDestroy(pipe_->exec[k]);
+      for (cudaEvent_t e : {pipe_->h2d_done[k], pipe_->fwd_done[k], pipe_->d2h_done[k]})
+        if (e) cudaEventDestroy(e);
+    }
+  }
   if (exec_) cudaGraphExecDestroy(exec_);
   if (stream_) {
     cudaStreamSynchronize(stream_);
@@ -417,13 +429,97 @@ void Graph::Forward() {
 
 void Graph::Synchronize() {
   CudaCheck(cudaSetDevice(device_), "cudaSetDevice");
+  if (pipe_) CudaCheck(cudaStreamSynchronize(pipe_->h2d), "graph synchronize (input copies)");
   CudaCheck(cudaStreamSynchronize(stream_), "graph synchronize");
+  if (pipe_) CudaCheck(cudaStreamSynchronize(pipe_->d2h), "graph synchronize (output copies)");
   // a kernel whose bounded wait ran out skipped its output tiles: report it
   // instead of handing back wrong results as a success
   const int dev_err = lotus_impl::read_device_error();
   if (dev_err != 0)
     throw std::runtime_error("a kernel's bounded wait expired (device error code " + std::to_string(dev_err) +
                              "); the outputs of this forward are invalid");
+}
+
+void Graph::SetupPipe() {
+  auto p = std::make_unique<Pipe>();
+  auto in_op = operands_.at(input_operand_);
+  auto out_op = operands_.at(output_operand_);
+  p->in[0] = in_op->tensor_;
+  p->out[0] = out_op->tensor_;
+  p->in[1] = Tensor(p->in[0].Shape(), p->in[0].Fmt());
+  p->out[1] = Tensor(p->out[0].Shape(), p->out[0].Fmt());
+  CudaCheck(cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking), "cudaStreamCreate");
+  CudaCheck(cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking), "cudaStreamCreate");
+  for (int k = 0; k < 2; ++k)
+    for (cudaEvent_t* e : {&p->h2d_done[k], &p->fwd_done[k], &p->d2h_done[k]})
+      CudaCheck(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate");
+  // kernels set their launch attributes on their first (eager) launch, which
+  // must not happen inside a capture
+  if (eager_runs_ == 0) {
+    RunLayers(stream_);
+    ++eager_runs_;
+  }
+  // one captured forward per slot, with the input and output operands bound
+  // to that slot's buffers
+  for (int k = 0; k < 2; ++k) {
+    in_op->tensor_ = p->in[k];
+    out_op->tensor_ = p->out[k];
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      try {
+        RunLayers(stream_);
+      } catch (...) {
+        cudaStreamEndCapture(stream_, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        in_op->tensor_ = p->in[0];
+        out_op->tensor_ = p->out[0];
+        throw;
+      }
+      e = cudaStreamEndCapture(stream_, &graph);
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&p->exec[k], graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    in_op->tensor_ = p->in[0];
+    out_op->tensor_ = p->out[0];
+    CudaCheck(e, "pipeline graph capture");
+  }
+  pipe_ = std::move(p);
+}
+
+int Graph::Submit(const float* host_in, float* host_out) {
+  CudaCheck(cudaSetDevice(device_), "cudaSetDevice");
+  if (!pipe_) SetupPipe();
+  Pipe& p = *pipe_;
+  const int k = static_cast<int>(p.submitted & 1);
+  const bool reuse = p.submitted >= 2;  // slot k was used by submission n-2
+  // input copy, once the forward that last read this slot's input is done
+  if (reuse) CudaCheck(cudaStreamWaitEvent(p.h2d, p.fwd_done[k], 0), "wait");
+  CudaCheck(cudaMemcpyAsync(p.in[k].Data(), host_in, p.in[k].Bytes(), cudaMemcpyDefault, p.h2d), "input copy");
+  CudaCheck(cudaEventRecord(p.h2d_done[k], p.h2d), "record");
+  // forward, once its input landed and the output copy that last read this
+  // slot's output is done
+  CudaCheck(cudaStreamWaitEvent(stream_, p.h2d_done[k], 0), "wait");
+  if (reuse) CudaCheck(cudaStreamWaitEvent(stream_, p.d2h_done[k], 0), "wait");
+  CudaCheck(cudaGraphLaunch(p.exec[k], stream_), "graph launch");
+  CudaCheck(cudaEventRecord(p.fwd_done[k], stream_), "record");
+  // output copy
+  CudaCheck(cudaStreamWaitEvent(p.d2h, p.fwd_done[k], 0), "wait");
+  CudaCheck(cudaMemcpyAsync(host_out, p.out[k].Data(), p.out[k].Bytes(), cudaMemcpyDefault, p.d2h), "output copy");
+  CudaCheck(cudaEventRecord(p.d2h_done[k], p.d2h), "record");
+  ++p.submitted;
+  return k;
+}
+
+cudaStream_t Graph::CopyStream(int which) {
+  CudaCheck(cudaSetDevice(device_), "cudaSetDevice");
+  if (!pipe_) SetupPipe();
+  return which == 0 ? pipe_->h2d : pipe_->d2h;
+}
+
+float* Graph::SlotOutput(int slot) {
+  if (slot == 0 || !pipe_) return OutputTensor().DataF32();
+  return pipe_->out[1].DataF32();
 }
 
 std::vector<float> Graph::ProfileLayers(int reps) {

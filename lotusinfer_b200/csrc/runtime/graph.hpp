@@ -47,9 +47,20 @@ class Graph {
   void Forward();
   // Enqueues the forward pass on `stream` (nullptr = the graph's own stream).
   void ForwardAsync(cudaStream_t stream = nullptr);
-  // Waits for the graph stream; throws if a kernel reported an expired
-  // bounded wait (its outputs are then invalid).
+  // Waits for the graph stream and the pipeline's copy streams; throws if a
+  // kernel reported an expired bounded wait (its outputs are then invalid).
   void Synchronize();
+  // Pipelined inference from host memory: host->device copy of `host_in` on a
+  // copy stream, the forward on the graph stream once it landed, and the
+  // device->host copy of the output into `host_out` on a second copy stream.
+  // Two sets of device input/output buffers alternate, so the copies of one
+  // batch overlap the forward of the previous one.  Returns the slot (0/1)
+  // this batch used; does not wait.
+  int Submit(const float* host_in, float* host_out);
+  // Copy stream of the pipelined path: 0 host->device, 1 device->host.
+  cudaStream_t CopyStream(int which);
+  // Device output buffer of pipeline slot 0/1 (slot 0 is the graph's output).
+  float* SlotOutput(int slot);
 
   Tensor& InputTensor() { return operands_.at(input_operand_)->tensor_; }
   Tensor& OutputTensor() { return operands_.at(output_operand_)->tensor_; }
@@ -87,6 +98,18 @@ class Graph {
   int stem_s2d_ = 1, stem_pad_h_ = 0, stem_pad_w_ = 0;
   std::vector<uint32_t> stem_shape_;
   std::shared_ptr<void> workspace_;  // split-K scratch shared by the layers (one stream, one layer at a time)
+
+  // pipelined path (Submit): slot 1's buffers, one captured forward per slot,
+  // the copy streams and the events that order them
+  struct Pipe {
+    Tensor in[2], out[2];
+    cudaGraphExec_t exec[2] = {nullptr, nullptr};
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t h2d_done[2] = {}, fwd_done[2] = {}, d2h_done[2] = {};
+    uint64_t submitted = 0;
+  };
+  void SetupPipe();
+  std::unique_ptr<Pipe> pipe_;
 };
 
 }  // namespace lotus

@@ -118,6 +118,32 @@ int lotus_graph_synchronize(lotus_graph* g) {
   return lotus_impl::set_error(LOTUS_OK, "");
 }
 
+int lotus_graph_submit(lotus_graph* g, const float* host_in, float* host_out, int* slot) {
+  if (!g || !host_in || !host_out) return lotus_impl::set_error(LOTUS_ERR_INVALID, "graph_submit: null pointer");
+  try {
+    const int k = g->g->Submit(host_in, host_out);
+    if (slot) *slot = k;
+  } catch (const std::exception& e) {
+    return lotus_impl::set_error(LOTUS_ERR_CUDA, std::string("graph_submit: ") + e.what());
+  }
+  return lotus_impl::set_error(LOTUS_OK, "");
+}
+
+cudaStream_t lotus_graph_copy_stream(lotus_graph* g, int which) {
+  if (!g || (which != 0 && which != 1)) return nullptr;
+  try {
+    return g->g->CopyStream(which);
+  } catch (const std::exception& e) {
+    lotus_impl::set_error(LOTUS_ERR_CUDA, std::string("graph_copy_stream: ") + e.what());
+    return nullptr;
+  }
+}
+
+float* lotus_graph_slot_output(lotus_graph* g, int slot) {
+  if (!g || (slot != 0 && slot != 1)) return nullptr;
+  return g->g->SlotOutput(slot);
+}
+
 int lotus_graph_layer_count(const lotus_graph* g) { return g ? static_cast<int>(g->g->Layers().size()) : -1; }
 
 const char* lotus_graph_layer_name(const lotus_graph* g, int i) {

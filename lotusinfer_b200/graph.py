@@ -45,6 +45,9 @@ GRAPH_SIGNATURES = {
     "lotus_graph_profile_layers": (_I, [_V, _I, _FP]),
     "lotus_graph_operand": (_V, [_V, ctypes.c_char_p, _IP, _I64P, _IP]),
     "lotus_graph_layer_weight": (_V, [_V, _I, ctypes.POINTER(ctypes.c_size_t)]),
+    "lotus_graph_submit": (_I, [_V, _V, _V, _IP]),
+    "lotus_graph_copy_stream": (_V, [_V, _I]),
+    "lotus_graph_slot_output": (_V, [_V, _I]),
 }
 
 NO_CUDA_GRAPH = 1
@@ -133,6 +136,23 @@ class Graph:
     def get_output_into(self, host_ptr: int, count: int, stream: Optional[int] = None) -> None:
         abi.check(_lib().lotus_graph_get_output(self._h, ctypes.c_void_p(host_ptr), count,
                                                 ctypes.c_void_p(stream) if stream else None))
+
+    def submit(self, host_in_ptr: int, host_out_ptr: int) -> int:
+        """Pipelined batch from host memory (lotus_graph_submit): returns the
+        slot used; the host buffers must stay alive until synchronize()."""
+        slot = ctypes.c_int()
+        abi.check(_lib().lotus_graph_submit(self._h, ctypes.c_void_p(host_in_ptr), ctypes.c_void_p(host_out_ptr),
+                                            ctypes.byref(slot)))
+        return slot.value
+
+    def copy_stream(self, which: int) -> int:
+        s = _lib().lotus_graph_copy_stream(self._h, int(which))
+        if not s:
+            raise LotusError(-3, abi.last_error())
+        return int(s)
+
+    def slot_output(self, slot: int) -> int:
+        return int(_lib().lotus_graph_slot_output(self._h, int(slot)))
 
     def forward(self, stream: Optional[int] = None) -> None:
         abi.check(_lib().lotus_graph_forward(self._h, ctypes.c_void_p(stream) if stream else None))

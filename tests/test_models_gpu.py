@@ -205,3 +205,22 @@ def test_resnet18_stem_pool_fusion(model_dir):
     np.testing.assert_array_equal(a, b)
     g1.close()
     g2.close()
+
+
+def test_pipelined_submit_equals_forward(model_dir):
+    """lotus_graph_submit (two alternating buffer slots, copy streams) returns
+    exactly what the plain set_input / forward / get_output sequence does."""
+    import torch
+    from lotusinfer_b200 import synth
+    g, _, _ = _graph("resnet18", model_dir, 4)
+    xs = [synth.synthetic_input("resnet18", 4, seed=s) for s in (7, 8, 9)]
+    want = [g.run(x) for x in xs]
+    hin = [torch.from_numpy(x).pin_memory() for x in xs]
+    hout = [torch.empty((4, 1000), dtype=torch.float32).pin_memory() for _ in range(5)]
+    order = [0, 1, 2, 0, 1]
+    slots = [g.submit(hin[i].data_ptr(), hout[j].data_ptr()) for j, i in enumerate(order)]
+    g.synchronize()
+    assert slots == [0, 1, 0, 1, 0]
+    for j, i in enumerate(order):
+        np.testing.assert_array_equal(hout[j].numpy(), want[i])
+    g.close()
