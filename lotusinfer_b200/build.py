@@ -3,7 +3,8 @@
 Compiles every source under csrc/ with nvcc for ``sm_100a`` only, in
 parallel, into ``_build/`` and links ``liblotus_b200.so`` next to this file,
 so the library travels with the source tree.  Objects are rebuilt when their
-source or any header under csrc/ or include/ is newer.
+source or a header they include (nvcc's dependency file next to the object)
+is newer; without a dependency file, when any header is newer.
 
     python -m lotusinfer_b200.build [--force]
 """
@@ -52,6 +53,26 @@ def _obj(src: str) -> str:
     return os.path.join(BUILD, rel + ".o")
 
 
+def _deps(obj: str):
+    """Files listed in the object's dependency file, or None without one."""
+    d = obj[:-2] + ".d"
+    if not os.path.exists(d):
+        return None
+    txt = open(d).read().replace("\\\n", " ")
+    files = txt.split(":", 1)[1].split() if ":" in txt else []
+    return [f for f in files if f.strip()]
+
+
+def _stale(src: str, obj: str, hdr_time: float) -> bool:
+    if not os.path.exists(obj):
+        return True
+    t = os.path.getmtime(obj)
+    deps = _deps(obj)
+    if deps is None:
+        return t < max(os.path.getmtime(src), hdr_time)
+    return any(not os.path.exists(f) or os.path.getmtime(f) > t for f in [src] + deps)
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     nvcc = _nvcc()
@@ -59,8 +80,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     jobs = []
     for src in _sources():
         obj = _obj(src)
-        if force or not os.path.exists(obj) or os.path.getmtime(obj) < max(os.path.getmtime(src), hdr_time):
-            jobs.append([nvcc] + NVCC_FLAGS + ["-c", src, "-o", obj])
+        if force or _stale(src, obj, hdr_time):
+            jobs.append([nvcc] + NVCC_FLAGS + ["-MD", "-MF", obj[:-2] + ".d", "-c", src, "-o", obj])
 
     def run(cmd):
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -46,14 +46,14 @@ Graph::Graph(const std::string& param_path, const std::string& bin_path, uint32_
 
 Graph::~Graph() {
   if (pipe_) {
-    for (cudaStream_t s : {pipe_->h2d, pipe_->d2h})
+    for (cudaStream_t s : {pipe_->h2d, pipe_->h2d_b, pipe_->d2h})
       if (s) {
         cudaStreamSynchronize(s);
         cudaStreamDestroy(s);
       }
     for (int k = 0; k < 2; ++k) {
       if (pipe_->exec[k]) cudaGraphExecDestroy(pipe_->exec[k]);
-      for (cudaEvent_t e : {pipe_->h2d_done[k], pipe_->fwd_done[k], pipe_->d2h_done[k]})
+      for (cudaEvent_t e : {pipe_->h2d_done[k], pipe_->h2d_b_done[k], pipe_->fwd_done[k], pipe_->d2h_done[k]})
         if (e) cudaEventDestroy(e);
     }
   }
@@ -429,7 +429,10 @@ void Graph::Forward() {
 
 void Graph::Synchronize() {
   CudaCheck(cudaSetDevice(device_), "cudaSetDevice");
-  if (pipe_) CudaCheck(cudaStreamSynchronize(pipe_->h2d), "graph synchronize (input copies)");
+  if (pipe_) {
+    CudaCheck(cudaStreamSynchronize(pipe_->h2d), "graph synchronize (input copies)");
+    CudaCheck(cudaStreamSynchronize(pipe_->h2d_b), "graph synchronize (input copies)");
+  }
   CudaCheck(cudaStreamSynchronize(stream_), "graph synchronize");
   if (pipe_) CudaCheck(cudaStreamSynchronize(pipe_->d2h), "graph synchronize (output copies)");
   // a kernel whose bounded wait ran out skipped its output tiles: report it
@@ -450,8 +453,9 @@ void Graph::SetupPipe() {
   p->out[1] = Tensor(p->out[0].Shape(), p->out[0].Fmt());
   CudaCheck(cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking), "cudaStreamCreate");
   CudaCheck(cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking), "cudaStreamCreate");
+  CudaCheck(cudaStreamCreateWithFlags(&p->h2d_b, cudaStreamNonBlocking), "cudaStreamCreate");
   for (int k = 0; k < 2; ++k)
-    for (cudaEvent_t* e : {&p->h2d_done[k], &p->fwd_done[k], &p->d2h_done[k]})
+    for (cudaEvent_t* e : {&p->h2d_done[k], &p->h2d_b_done[k], &p->fwd_done[k], &p->d2h_done[k]})
       CudaCheck(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate");
   // kernels set their launch attributes on their first (eager) launch, which
   // must not happen inside a capture
@@ -493,13 +497,25 @@ int Graph::Submit(const float* host_in, float* host_out) {
   Pipe& p = *pipe_;
   const int k = static_cast<int>(p.submitted & 1);
   const bool reuse = p.submitted >= 2;  // slot k was used by submission n-2
-  // input copy, once the forward that last read this slot's input is done
-  if (reuse) CudaCheck(cudaStreamWaitEvent(p.h2d, p.fwd_done[k], 0), "wait");
-  CudaCheck(cudaMemcpyAsync(p.in[k].Data(), host_in, p.in[k].Bytes(), cudaMemcpyDefault, p.h2d), "input copy");
+  // input copy, once the forward that last read this slot's input is done;
+  // its two halves go on two streams so that two copy engines move them
+  if (reuse) {
+    CudaCheck(cudaStreamWaitEvent(p.h2d, p.fwd_done[k], 0), "wait");
+    CudaCheck(cudaStreamWaitEvent(p.h2d_b, p.fwd_done[k], 0), "wait");
+  }
+  const size_t bytes = p.in[k].Bytes();
+  const size_t half = (bytes / 2 + 4095) / 4096 * 4096;
+  char* dst = static_cast<char*>(p.in[k].Data());
+  const char* src = reinterpret_cast<const char*>(host_in);
+  CudaCheck(cudaMemcpyAsync(dst, src, std::min(half, bytes), cudaMemcpyDefault, p.h2d), "input copy");
+  if (bytes > half)
+    CudaCheck(cudaMemcpyAsync(dst + half, src + half, bytes - half, cudaMemcpyDefault, p.h2d_b), "input copy");
   CudaCheck(cudaEventRecord(p.h2d_done[k], p.h2d), "record");
+  CudaCheck(cudaEventRecord(p.h2d_b_done[k], p.h2d_b), "record");
   // forward, once its input landed and the output copy that last read this
   // slot's output is done
   CudaCheck(cudaStreamWaitEvent(stream_, p.h2d_done[k], 0), "wait");
+  CudaCheck(cudaStreamWaitEvent(stream_, p.h2d_b_done[k], 0), "wait");
   if (reuse) CudaCheck(cudaStreamWaitEvent(stream_, p.d2h_done[k], 0), "wait");
   CudaCheck(cudaGraphLaunch(p.exec[k], stream_), "graph launch");
   CudaCheck(cudaEventRecord(p.fwd_done[k], stream_), "record");

@@ -105,7 +105,8 @@ class Graph {
     Tensor in[2], out[2];
     cudaGraphExec_t exec[2] = {nullptr, nullptr};
     cudaStream_t h2d = nullptr, d2h = nullptr;
-    cudaEvent_t h2d_done[2] = {}, fwd_done[2] = {}, d2h_done[2] = {};
+    cudaStream_t h2d_b = nullptr;  // second input-copy stream: each input copy is split over two copy engines
+    cudaEvent_t h2d_done[2] = {}, h2d_b_done[2] = {}, fwd_done[2] = {}, d2h_done[2] = {};
     uint64_t submitted = 0;
   };
   void SetupPipe();
