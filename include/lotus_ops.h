@@ -232,6 +232,23 @@ int lotus_nhwc_f16_to_nchw_f32(const void* x, float* y, int n, int c, int h, int
 int lotus_space_to_depth_f16(const float* x, void* y, int n, int c, int h, int w, int factor, int pad_h, int pad_w,
                              int out_h, int out_w, cudaStream_t stream);
 
+/* Input preprocessing of the reference's classification demo
+ * (demo/image_classification.cpp:9-44, done there on the CPU with OpenCV):
+ * n decoded 8-bit BGR images (HWC, all src_h x src_w, rows of src_w*3 bytes,
+ * device memory) -> bilinear resize to resize_h x resize_w with the
+ * cv::resize INTER_LINEAR geometry (half-pixel centres, source index clamped
+ * to the edge) -> BGR to RGB -> /255 -> centre crop crop_h x crop_w at
+ * (max(0, resize/2 - crop/2)) -> (x - mean[c]) / std[c] -> NCHW fp32
+ * [n, 3, crop_h, crop_w] in dst, the graph input format.  mean / std: 3 floats
+ * each in RGB order, or NULL for the reference's ImageNet constants
+ * (0.485, 0.456, 0.406) / (0.229, 0.224, 0.225).  The resize is evaluated in
+ * fp32 without rounding to 8 bits in between (OpenCV's 8-bit path does), so
+ * results differ from the demo by at most one 8-bit step before the
+ * normalisation.  The demo's 256 -> 224 pipeline is resize 256 x 256, crop
+ * 224 x 224. */
+int lotus_preprocess_bgr_u8(const uint8_t* src, int n, int src_h, int src_w, int resize_h, int resize_w, int crop_h,
+                            int crop_w, const float* mean, const float* stdv, float* dst, cudaStream_t stream);
+
 /* Last error of the calling thread, "" if none. */
 const char* lotus_last_error_string(void);
 

@@ -78,6 +78,7 @@ SIGNATURES = {
     "lotus_nchw_f32_to_nhwc_f16": (_I, [_V, _V, _I, _I, _I, _I, _V]),
     "lotus_nhwc_f16_to_nchw_f32": (_I, [_V, _V, _I, _I, _I, _I, _V]),
     "lotus_space_to_depth_f16": (_I, [_V, _V, _I, _I, _I, _I, _I, _I, _I, _I, _I, _V]),
+    "lotus_preprocess_bgr_u8": (_I, [_V, _I, _I, _I, _I, _I, _I, _I, _V, _V, _V, _V]),
     "lotus_last_error_string": (ctypes.c_char_p, []),
     "lotus_device_error": (_I, []),
     "lotus_launch_count": (_U64, []),

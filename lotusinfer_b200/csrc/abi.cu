@@ -523,6 +523,24 @@ int lotus_conv2d_maxpool_fwd(const void* x, const void* w_packed, const float* b
   return ok();
 }
 
+int lotus_preprocess_bgr_u8(const uint8_t* src, int n, int src_h, int src_w, int resize_h, int resize_w, int crop_h,
+                            int crop_w, const float* mean, const float* stdv, float* dst, cudaStream_t stream) {
+  if (!src || !dst) return fail(LOTUS_ERR_INVALID, "preprocess: null src or dst");
+  if (n <= 0 || src_h <= 0 || src_w <= 0 || resize_h <= 0 || resize_w <= 0 || crop_h <= 0 || crop_w <= 0)
+    return fail(LOTUS_ERR_INVALID, "preprocess: sizes must be positive");
+  if (crop_h > resize_h || crop_w > resize_w) return fail(LOTUS_ERR_INVALID, "preprocess: crop larger than the resize");
+  if (static_cast<int64_t>(n) * src_h * src_w * 3 > (int64_t(1) << 40))
+    return fail(LOTUS_ERR_UNSUPPORTED, "preprocess: input too large");
+  static const float kMean[3] = {0.485f, 0.456f, 0.406f};
+  static const float kStd[3] = {0.229f, 0.224f, 0.225f};
+  const float* m = mean ? mean : kMean;
+  const float* sd = stdv ? stdv : kStd;
+  for (int c = 0; c < 3; ++c)
+    if (!(sd[c] != 0.f)) return fail(LOTUS_ERR_INVALID, "preprocess: std must be non-zero");
+  return cuda_status(launch_preprocess(src, n, src_h, src_w, resize_h, resize_w, crop_h, crop_w, m, sd, dst, stream),
+                     "preprocess");
+}
+
 int lotus_adaptive_avgpool2d_fwd(const void* x, void* y, int n, int c, int h, int w, int oh, int ow, int act,
                                  int out_f32, cudaStream_t stream) {
   if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(LOTUS_ERR_INVALID, "adaptive_avgpool2d: bad pointer");

@@ -104,6 +104,10 @@ cudaError_t launch_tconv_direct(const void* x, const void* wp, int k_pad, const 
                                 int csi, int h, int w_, int cout, int cso, int oh, int ow, int kh, int kw, int sh,
                                 int sw, int ph, int pw, int act, cudaStream_t s);
 
+// preprocess.cu
+cudaError_t launch_preprocess(const uint8_t* src, int n, int h, int w, int rh, int rw, int ch, int cw,
+                              const float* mean, const float* stdv, float* dst, cudaStream_t s);
+
 // gemv.cu
 cudaError_t launch_gemv(const void* w, int w_f16, int ldw, const void* x, int x_f16, int ldx, const float* bias,
                         void* y, int y_f16, int ldy, int batch, int h_out, int w_in, int act, cudaStream_t s);

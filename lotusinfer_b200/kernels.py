@@ -242,3 +242,14 @@ def concat_channels(a: torch.Tensor, ca: int, b: torch.Tensor, cb: int) -> torch
     y = torch.empty((n, h, w, channel_stride(ca + cb)), dtype=torch.float16, device=a.device)
     check(abi.lib().lotus_concat_channels_fwd(_ptr(a), ca, _ptr(b), cb, _ptr(y), n, h, w, _stream()))
     return y
+
+
+# --------------------------------------------------------------------- input preprocessing
+def preprocess_bgr_u8(images: torch.Tensor, resize_hw=(256, 256), crop_hw=(224, 224)) -> torch.Tensor:
+    """[n, h, w, 3] uint8 BGR device images -> [n, 3, crop_h, crop_w] fp32
+    (lotus_preprocess_bgr_u8 with the reference's ImageNet constants)."""
+    n, h, w, _ = images.shape
+    y = torch.empty((n, 3) + tuple(crop_hw), dtype=torch.float32, device=images.device)
+    check(abi.lib().lotus_preprocess_bgr_u8(_ptr(images.contiguous()), n, h, w, resize_hw[0], resize_hw[1], crop_hw[0],
+                                            crop_hw[1], None, None, _ptr(y), _stream()))
+    return y

@@ -244,3 +244,61 @@ def run_graph(param_path: str, bin_path: str, x: np.ndarray, weights: Optional[D
         else:
             raise NotImplementedError(t)
     raise RuntimeError("graph has no pnnx.Output")
+
+
+IMAGENET_MEAN = (0.485, 0.456, 0.406)
+IMAGENET_STD = (0.229, 0.224, 0.225)
+
+
+def preprocess_bgr_u8(images, resize_hw=(256, 256), crop_hw=(224, 224), mean=IMAGENET_MEAN, std=IMAGENET_STD):
+    """Input preprocessing of the reference's classification demo
+    (demo/image_classification.cpp:9-44): 8-bit BGR HWC images [n, h, w, 3]
+    -> bilinear resize (cv::resize INTER_LINEAR geometry: half-pixel centres,
+    source index clamped to the edge) -> RGB -> /255 -> centre crop ->
+    (x - mean) / std, planar [n, 3, crop_h, crop_w] fp32.  Computed in float32
+    with every operation rounded on its own (no fused multiply-add), in the
+    order the GPU kernel uses; OpenCV's 8-bit path rounds the resized value to
+    uint8 with 11-bit fixed-point weights, which this float restatement does
+    not (it stays within one 8-bit step of it)."""
+    imgs = np.asarray(images)
+    if imgs.ndim == 3:
+        imgs = imgs[None]
+    n, h, w, _ = imgs.shape
+    rh, rw = resize_hw
+    ch, cw = crop_hw
+    y0, x0 = max(0, rh // 2 - ch // 2), max(0, rw // 2 - cw // 2)
+    f32 = np.float32
+
+    def axis(n_src, n_dst, first, count):
+        scale = f32(n_src) / f32(n_dst)
+        d = np.arange(first, first + count, dtype=np.float32)
+        f = (d + f32(0.5)) * scale - f32(0.5)
+        s = np.floor(f)
+        a = (f - s).astype(np.float32)
+        i0 = s.astype(np.int64)
+        lo = i0 < 0
+        a[lo] = 0
+        i0[lo] = 0
+        hi = i0 >= n_src - 1
+        a[hi] = 0
+        i0[hi] = n_src - 1
+        i1 = np.minimum(i0 + 1, n_src - 1)
+        return i0, i1, a
+
+    yi0, yi1, ay = axis(h, rh, y0, ch)
+    xi0, xi1, ax = axis(w, rw, x0, cw)
+    out = np.empty((n, 3, ch, cw), np.float32)
+    one = f32(1.0)
+    inv255 = f32(1.0 / 255.0)
+    for c in range(3):
+        src = imgs[..., 2 - c].astype(np.float32)  # BGR -> RGB
+        p00 = src[:, yi0][:, :, xi0]
+        p01 = src[:, yi0][:, :, xi1]
+        p10 = src[:, yi1][:, :, xi0]
+        p11 = src[:, yi1][:, :, xi1]
+        axr, ayr = ax[None, None, :], ay[None, :, None]
+        top = (one - axr) * p00 + axr * p01
+        bot = (one - axr) * p10 + axr * p11
+        v = ((one - ayr) * top + ayr * bot) * inv255
+        out[:, c] = (v - f32(mean[c])) / f32(std[c])
+    return out

@@ -434,3 +434,25 @@ def test_conv2d_maxpool_matches_separate_conv_and_pool():
     sep = K.maxpool2d(conv, 64, 3, 2, 1)
     assert torch.equal(fused, sep)
     _no_device_error()
+
+
+def test_preprocess_matches_oracle_and_opencv():
+    """GPU preprocessing (resize 256, RGB, /255, centre crop 224, normalise)
+    against the fp32 oracle (same operation order: within fp32 rounding) and
+    against OpenCV's output of the reference demo's pipeline (within one
+    8-bit step)."""
+    import os
+    K = _k()
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "preprocess_cv2.npz"))
+    for name in ("down_320x240", "up_150x200"):
+        img = d[name + "_bgr"]
+        got = K.preprocess_bgr_u8(_gpu(img[None])).cpu().numpy()
+        np.testing.assert_allclose(got, oracle.preprocess_bgr_u8(img), rtol=0, atol=2e-6)
+        steps = np.abs(got[0] - d[name + "_out"]) * 255.0 * np.array(oracle.IMAGENET_STD, np.float32)[:, None, None]
+        assert steps.max() <= 1.0, (name, float(steps.max()))
+    # a batch of camera-sized images
+    rng = _rng(5)
+    imgs = rng.integers(0, 256, (8, 375, 500, 3), dtype=np.uint8)
+    got = K.preprocess_bgr_u8(_gpu(imgs)).cpu().numpy()
+    np.testing.assert_allclose(got, oracle.preprocess_bgr_u8(imgs), rtol=0, atol=2e-6)
+    _no_device_error()
