@@ -30,18 +30,20 @@
 //               row the horizontal 3-wide max by warp shuffles (lane 0's
 //               left neighbour comes from the previous quarter through
 //               shared memory), then the activation of the pooled pixel;
-//   warp 16     TMEM allocation, MMA issuer 0 (even tiles);
+//   warp 16     TMEM allocation, MMA issuer 0;
 //   warp 17     TMA producer: the weights once, then input rows in order;
-//   warp 18     MMA issuer 1 (odd tiles).
+//   warp 18     MMA issuer 1 (tiles go round robin over the issuers; four
+//               issuers, one per scheduler, measured slower: 0.185 vs 0.175 ms).
 // Each CTA owns a contiguous range of output units (pooled rows, or conv
 // rows without the pool) over the whole batch, walked as per-image
 // segments; with the pool a segment also computes the conv row just above
 // its first pooled row (the shared row of two pooled windows).
 //
 // Barrier protocol (all waits bounded): rfull[slot] (TMA bytes), rempty[slot]
-// (count 2: each issuer commits once per load after its last MMA reading it;
-// an issuer waits on every load of the sequence in order, so a slot can only
-// be refilled after both issuers have observed its previous load), tfull /
+// (count n_iss: each issuer commits once per load after its last MMA reading
+// it; an issuer waits on every load of the sequence in order, so a slot can
+// only be refilled after every issuer has observed its previous load; with
+// kh + n_iss - 1 <= kRowSlots the loads in flight fit the ring), tfull /
 // tempty per TMEM accumulator (8 x 64 columns), wfull for the weights.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -70,8 +72,17 @@ constexpr int kRowMaxKh = kRowSlots - 2;       // a tile's loads plus the next t
 constexpr int kWBlockBytes = 64 * 128;         // one 64-wide K block of 64 weight rows
 constexpr int kEpiWarps = 16;                  // 4 per TMEM lane quarter, 16 columns each
 constexpr int kEpiCols = 64 / (kEpiWarps / 4);
-constexpr int kIssuer0 = kEpiWarps, kProducer = kEpiWarps + 1, kIssuer1 = kEpiWarps + 2;
-constexpr int kThreads = (kEpiWarps + 3) * 32;
+// MMA issuers: warp kIssuer0 (which also allocates TMEM) and the three warps
+// after the producer; one thread issues at most one tcgen05.mma per ~80
+// cycles, so tiles go round robin over up to four issuers, one per scheduler
+constexpr int kMaxIssuers = 2;
+constexpr int kIssuer0 = kEpiWarps, kProducer = kEpiWarps + 1;
+constexpr int kThreads = (kEpiWarps + 1 + kMaxIssuers) * 32;
+__device__ __forceinline__ int issuer_of(int warp) {
+  if (warp == kIssuer0) return 0;
+  if (warp > kProducer && warp <= kProducer + kMaxIssuers - 1) return warp - kProducer;
+  return -1;
+}
 
 struct RowParams {
   const float* bias;
@@ -81,6 +92,7 @@ struct RowParams {
   int PH, PW;        // pooled size (pool == 1)
   int units;         // N * (pool ? PH : OH)
   int w_bytes;       // kh * kWBlockBytes
+  int n_iss;         // MMA issuers in use (tiles lt with lt % n_iss == i go to issuer i)
   uint32_t wait_limit;
 };
 
@@ -322,13 +334,13 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
     mbar_init(wfull, 1);
     for (int s = 0; s < kRowSlots; ++s) {
       mbar_init(&rfull[s], 1);
-      mbar_init(&rempty[s], 2);
+      mbar_init(&rempty[s], p.n_iss);
     }
     for (int b = 0; b < kRowAcc; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
-    mbar_init(mma_done, 2);
+    mbar_init(mma_done, kMaxIssuers);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -379,9 +391,12 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       for (int64_t j = static_cast<int64_t>(L) - 1; j >= 0 && j >= static_cast<int64_t>(L) - kRowSlots; --j)
         mbar_wait(&rfull[j % kRowSlots], static_cast<uint32_t>(j / kRowSlots) & 1, kErrWaitFull, p.wait_limit);
     }
-  } else if (warp == kIssuer0 || warp == kIssuer1) {
-    if (lane == 0) {
-      const int issuer = warp == kIssuer0 ? 0 : 1;
+  } else if (issuer_of(warp) >= 0) {
+    if (lane == 0 && issuer_of(warp) >= p.n_iss) {
+      umma_commit(mma_done);  // an issuer left idle by a tall kernel (see n_iss)
+      mbar_wait(mma_done, 0, kErrWaitFull, p.wait_limit);
+    } else if (lane == 0) {
+      const int issuer = issuer_of(warp);
       constexpr uint32_t idesc = make_idesc_f16_m128(64);
       // no shared-memory loads in this loop (they would wait behind queued
       // MMAs); waits are relaxed, every one bounded
@@ -395,7 +410,7 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
         const int ntiles = sg.hi - sg.lo + 1;
         const uint32_t nloads = static_cast<uint32_t>(ntiles + p.kh - 1);
         for (int j = 0; j < ntiles && ok; ++j, ++lt) {
-          if ((lt & 1) != issuer) continue;
+          if (lt % p.n_iss != issuer) continue;
           const int ab = lt % kRowAcc;
           if (!mbar_wait_relaxed(&tempty[ab], ((lt / kRowAcc) & 1) ^ 1, kErrWaitAccum, p.wait_limit)) {
             ok = false;
@@ -423,8 +438,8 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
               umma_f16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (r | k) != 0 ? 1u : 0u);
           }
           umma_commit(&tfull[ab]);
-          // this issuer's next tile (j + 2) reads loads from Lseg + j + 2 on
-          const uint32_t rel_to = std::min(Lseg + static_cast<uint32_t>(j + 1), next_wait - 1);
+          // this issuer's next tile (j + n_iss) reads loads from Lseg + j + n_iss on
+          const uint32_t rel_to = std::min(Lseg + static_cast<uint32_t>(j + p.n_iss - 1), next_wait - 1);
           for (; next_rel <= rel_to; ++next_rel) umma_commit(&rempty[next_rel % kRowSlots]);
         }
         if (!ok) break;
@@ -539,6 +554,9 @@ int conv_row_launch(const ConvRowArgs& a, cudaStream_t stream, const char** err)
   p.units = a.N * (a.pool ? p.PH : p.OH);
   p.w_bytes = a.kh * kWBlockBytes;
   p.wait_limit = wait_limit_from_env();
+  // every issuer waits on each load in order, so a tile's kh loads plus the
+  // loads of the other issuers' tiles in flight must fit the ring
+  p.n_iss = std::min(kMaxIssuers, kRowSlots - a.kh + 1);
 
   CUtensorMap mw, mx;
   if (make_weight_map(&mw, a) != 0) {
