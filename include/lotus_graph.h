@@ -27,6 +27,8 @@ typedef struct lotus_graph lotus_graph;
 #define LOTUS_GRAPH_NO_RESIDUAL_FUSION 2 /* flags: keep pnnx.Expression add as its own kernel */
 #define LOTUS_GRAPH_NO_S2D_STEM 4        /* flags: run a strided 3-channel stem conv directly */
 #define LOTUS_GRAPH_NO_POOL_FUSION 8     /* flags: keep a max pool after a conv as its own kernel */
+#define LOTUS_GRAPH_NO_CONCAT_FUSION 16  /* flags: copy torch.cat halves with a concat kernel */
+#define LOTUS_GRAPH_NO_MEMORY_PLAN 32    /* flags: give every operand its own device buffer */
 
 /* Graph(param, bin, batch) of the reference (source/graph.cpp:44-111) on
  * `device` (-1 = current). */
@@ -90,6 +92,10 @@ const char* lotus_graph_layer_type(const lotus_graph* g, int i);
 double lotus_graph_layer_flops(const lotus_graph* g, int i);
 double lotus_graph_layer_bytes(const lotus_graph* g, int i);
 int lotus_graph_launches_per_forward(const lotus_graph* g);
+/* Device bytes held by the graph's operands (activations, input and output;
+ * weights and the split-K workspace not included).  With the memory plan,
+ * operands whose lifetimes do not overlap share buffers. */
+size_t lotus_graph_activation_bytes(const lotus_graph* g);
 /* Device pointer, storage format (0 NCHW fp32, 1 NHWC fp16 with channel
  * stride roundup(C, 8)) and logical NCHW shape of a named operand; NULL if
  * the operand does not exist or was folded away. */

@@ -97,6 +97,17 @@ size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d);
 int lotus_conv2d_fwd_ws(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                         const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* lotus_conv2d_fwd_ws writing a channel slice of a wider NHWC fp16 tensor
+ * (LOTUS_OUT_NHWC_F16 only): y points at the slice's first channel (16-byte
+ * aligned) and consecutive output pixels are y_pixel_stride elements apart (a
+ * multiple of 8, >= roundup(c_out, 8)); only the slice's channels are written
+ * (a residual, if any, keeps its own dense stride).  The graph uses it to
+ * write a conv's output straight into its half of a torch.cat buffer
+ * (reference source/layer/concatenate.cpp:20-35 copies it there instead). */
+int lotus_conv2d_fwd_slice(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                           int y_pixel_stride, const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream);
+
 /* lotus_conv2d_fwd_ws without a caller workspace, for callers that cannot
  * allocate device memory: cudaMalloc / cudaFree can synchronise the device and
  * can fail, so code that runs inside a latency-critical serving loop, inside a
@@ -136,6 +147,15 @@ int lotus_tconv2d_prepack(const float* w_iokk, void* w_packed, const lotus_tconv
 /* x NHWC fp16 [n,h,w,Cs_in] -> y NHWC fp16 [n,oh,ow,Cs_out]. */
 int lotus_tconv2d_fwd(const void* x, const void* w_packed, const float* bias, void* y, const lotus_tconv2d_desc* d,
                       cudaStream_t stream);
+/* lotus_tconv2d_fwd writing a channel slice of a wider NHWC fp16 tensor: y
+ * points at the slice's first channel (16-byte aligned) and consecutive output
+ * pixels are y_pixel_stride elements apart (a multiple of 8, >=
+ * roundup(c_out, 8)); only the slice's channels are written.  The graph uses
+ * it to write a transposed conv's output straight into its half of a
+ * torch.cat buffer (reference source/layer/concatenate.cpp:20-35 copies it
+ * there instead). */
+int lotus_tconv2d_fwd_slice(const void* x, const void* w_packed, const float* bias, void* y, int y_pixel_stride,
+                            const lotus_tconv2d_desc* d, cudaStream_t stream);
 
 /* Linear y[m, n] = act(sum_k x[m, k] * W[n, k] + b[n]), the reference Gemm
  * (source/operator/gemm_tensorcore.cu:18-169, called from
@@ -179,6 +199,12 @@ typedef struct lotus_pool2d_desc {
 } lotus_pool2d_desc;
 int lotus_maxpool2d_out_hw(const lotus_pool2d_desc* d, int* oh, int* ow);
 int lotus_maxpool2d_fwd(const void* x, void* y, const lotus_pool2d_desc* d, cudaStream_t stream);
+/* Max pooling of a channel slice of a wider NHWC fp16 tensor: x points at the
+ * slice's first channel and consecutive pixels are x_pixel_stride elements
+ * apart (a multiple of 8, >= roundup(c, 8)); y as lotus_maxpool2d_fwd.  Lets
+ * a pool read the encoder half of a U-Net concatenation buffer in place. */
+int lotus_maxpool2d_fwd_strided(const void* x, int x_pixel_stride, void* y, const lotus_pool2d_desc* d,
+                                cudaStream_t stream);
 
 /* Convolution with the max pool that follows it fused into its epilogue:
  * y = maxpool3x3/2/pad1(act(conv(x, w) + bias)), NHWC fp16 in and out

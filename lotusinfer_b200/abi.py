@@ -57,10 +57,12 @@ SIGNATURES = {
     "lotus_conv2d_workspace_bytes": (_S, [_CD]),
     "lotus_conv2d_fwd_ws": (_I, [_V, _V, _V, _V, _V, _CD, _V, _S, _V]),
     "lotus_conv2d_fwd_noalloc": (_I, [_V, _V, _V, _V, _V, _CD, _V]),
+    "lotus_conv2d_fwd_slice": (_I, [_V, _V, _V, _V, _V, _I, _CD, _V, _S, _V]),
     "lotus_tconv2d_out_hw": (_I, [_TD, _IP, _IP]),
     "lotus_tconv2d_packed_weight_bytes": (_S, [_TD]),
     "lotus_tconv2d_prepack": (_I, [_V, _V, _TD, _V]),
     "lotus_tconv2d_fwd": (_I, [_V, _V, _V, _V, _TD, _V]),
+    "lotus_tconv2d_fwd_slice": (_I, [_V, _V, _V, _V, _I, _TD, _V]),
     "lotus_linear_packed_weight_bytes": (_S, [_I, _I]),
     "lotus_linear_prepack": (_I, [_V, _V, _I, _I, _I, _I, _I, _V]),
     "lotus_linear_fwd": (_I, [_V, _V, _V, _V, _I, _I, _I, _I, _I, _V]),
@@ -70,6 +72,7 @@ SIGNATURES = {
     "lotus_gemv_bias_fwd": (_I, [_V, _I, _V, _I, _V, _V, _I, _I, _I, _I, _I, _V]),
     "lotus_maxpool2d_out_hw": (_I, [_PD, _IP, _IP]),
     "lotus_maxpool2d_fwd": (_I, [_V, _V, _PD, _V]),
+    "lotus_maxpool2d_fwd_strided": (_I, [_V, _I, _V, _PD, _V]),
     "lotus_conv2d_maxpool_supported": (_I, [_CD, _PD]),
     "lotus_conv2d_maxpool_fwd": (_I, [_V, _V, _V, _V, _CD, _PD, _V]),
     "lotus_adaptive_avgpool2d_fwd": (_I, [_V, _V, _I, _I, _I, _I, _I, _I, _I, _I, _V]),

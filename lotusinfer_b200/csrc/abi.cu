@@ -142,10 +142,14 @@ static ConvTcArgs conv_args(const void* x, const void* w_packed, const float* bi
 }
 
 static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
-                         const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                         const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                         int y_stride = 0) {
   int oh, ow;
   const int st = check_conv_desc(d, &oh, &ow);
   if (st != LOTUS_OK) return st;
+  if (y_stride != 0 && (d->out_kind != LOTUS_OUT_NHWC_F16 || y_stride < cs_of(d->c_out) || y_stride % 8 != 0))
+    return fail(LOTUS_ERR_INVALID,
+                "conv2d: an output pixel stride needs the NHWC fp16 output, a multiple of 8 and >= roundup(c_out, 8)");
   if (!x || !w_packed || !y) return fail(LOTUS_ERR_INVALID, "conv2d: null x, w or y");
   if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y) || (residual && !aligned16(residual)))
     return fail(LOTUS_ERR_INVALID, "conv2d: x, w, y and residual must be 16-byte aligned");
@@ -157,6 +161,7 @@ static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias,
   ConvTcArgs a = conv_args(x, w_packed, bias, residual, y, d, oh, ow);
   a.ws = static_cast<float*>(workspace);
   a.ws_bytes = workspace ? workspace_bytes : 0;
+  a.y_stride = y_stride;
   const char* err = "";
   const int r = conv_tc_launch(a, stream, &err);
   if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
@@ -171,6 +176,13 @@ int lotus_conv2d_fwd(const void* x, const void* w_packed, const float* bias, con
 int lotus_conv2d_fwd_ws(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                         const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   return conv_fwd_impl(x, w_packed, bias, residual, y, d, workspace, workspace_bytes, stream);
+}
+
+int lotus_conv2d_fwd_slice(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
+                           int y_pixel_stride, const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream) {
+  if (y_pixel_stride <= 0) return fail(LOTUS_ERR_INVALID, "conv2d_slice: pixel stride must be positive");
+  return conv_fwd_impl(x, w_packed, bias, residual, y, d, workspace, workspace_bytes, stream, y_pixel_stride);
 }
 
 int lotus_conv2d_fwd_noalloc(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
@@ -252,8 +264,8 @@ int lotus_tconv2d_prepack(const float* w, void* w_packed, const lotus_tconv2d_de
       launch_tconv_prepack(w, w_packed, d->c_in, d->c_out, d->kh, d->kw, cs, round64(cs), stream), "tconv2d_prepack");
 }
 
-int lotus_tconv2d_fwd(const void* x, const void* w_packed, const float* bias, void* y, const lotus_tconv2d_desc* d,
-                      cudaStream_t stream) {
+static int tconv_fwd_impl(const void* x, const void* w_packed, const float* bias, void* y, int y_stride,
+                          const lotus_tconv2d_desc* d, cudaStream_t stream) {
   int oh, ow;
   const int st = check_tconv(d, &oh, &ow);
   if (st != LOTUS_OK) return st;
@@ -261,18 +273,21 @@ int lotus_tconv2d_fwd(const void* x, const void* w_packed, const float* bias, vo
   if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y))
     return fail(LOTUS_ERR_INVALID, "tconv2d: x, w and y must be 16-byte aligned");
   const int cs_in = cs_of(d->c_in), cs_out = cs_of(d->c_out);
+  if (y_stride == 0) y_stride = cs_out;
+  if (y_stride < cs_out || y_stride % 8 != 0)
+    return fail(LOTUS_ERR_INVALID, "tconv2d: output pixel stride must be a multiple of 8 and >= roundup(c_out, 8)");
   const int k_pad = round64(cs_in);
   const size_t out_pixels = static_cast<size_t>(d->n) * oh * ow;
   const bool no_overlap = d->stride_h >= d->kh && d->stride_w >= d->kw;
   if (!no_overlap) {
-    return cuda_status(launch_tconv_direct(x, w_packed, k_pad, bias, y, d->n, d->c_in, cs_in, d->h, d->w, d->c_out,
-                                           cs_out, oh, ow, d->kh, d->kw, d->stride_h, d->stride_w, d->pad_h, d->pad_w,
-                                           d->act, stream),
+    return cuda_status(launch_tconv_direct(x, w_packed, k_pad, bias, y, y_stride, d->n, d->c_in, cs_in, d->h, d->w,
+                                           d->c_out, cs_out, oh, ow, d->kh, d->kw, d->stride_h, d->stride_w, d->pad_h,
+                                           d->pad_w, d->act, stream),
                        "tconv2d(direct)");
   }
   const bool full_cover = d->stride_h == d->kh && d->stride_w == d->kw && d->out_pad_h == 0 && d->out_pad_w == 0;
   if (!full_cover || cs_out != d->c_out) {
-    const cudaError_t e = launch_tconv_fill_bias(y, bias, d->c_out, cs_out, out_pixels, d->act, stream);
+    const cudaError_t e = launch_tconv_fill_bias(y, y_stride, bias, d->c_out, cs_out, out_pixels, d->act, stream);
     if (e != cudaSuccess) return cuda_status(e, "tconv2d(fill)");
   }
   ConvTcArgs a{};
@@ -306,10 +321,22 @@ int lotus_tconv2d_fwd(const void* x, const void* w_packed, const float* bias, vo
   a.t_pw = d->pad_w;
   a.t_kw = d->kw;
   a.t_cout = d->c_out;
+  a.y_stride = y_stride;
   const char* err = "";
   const int r = conv_tc_launch(a, stream, &err);
   if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("tconv2d: ") + err);
   return ok();
+}
+
+int lotus_tconv2d_fwd(const void* x, const void* w_packed, const float* bias, void* y, const lotus_tconv2d_desc* d,
+                      cudaStream_t stream) {
+  return tconv_fwd_impl(x, w_packed, bias, y, 0, d, stream);
+}
+
+int lotus_tconv2d_fwd_slice(const void* x, const void* w_packed, const float* bias, void* y, int y_pixel_stride,
+                            const lotus_tconv2d_desc* d, cudaStream_t stream) {
+  if (y_pixel_stride <= 0) return fail(LOTUS_ERR_INVALID, "tconv2d_slice: pixel stride must be positive");
+  return tconv_fwd_impl(x, w_packed, bias, y, y_pixel_stride, d, stream);
 }
 
 // ------------------------------------------------------------------ linear
@@ -451,15 +478,28 @@ int lotus_maxpool2d_out_hw(const lotus_pool2d_desc* d, int* oh, int* ow) {
   return ok();
 }
 
-int lotus_maxpool2d_fwd(const void* x, void* y, const lotus_pool2d_desc* d, cudaStream_t stream) {
+static int maxpool_impl(const void* x, int x_stride, void* y, const lotus_pool2d_desc* d, cudaStream_t stream) {
   int oh, ow;
   const int st = lotus_maxpool2d_out_hw(d, &oh, &ow);
   if (st != LOTUS_OK) return st;
   if (d->act < 0 || d->act > 2) return fail(LOTUS_ERR_INVALID, "maxpool2d: unknown activation");
   if (!x || !y || !aligned16(x) || !aligned16(y)) return fail(LOTUS_ERR_INVALID, "maxpool2d: bad x or y pointer");
-  return cuda_status(launch_maxpool(x, y, d->n, d->c, cs_of(d->c), d->h, d->w, oh, ow, d->kh, d->kw, d->stride_h,
-                                    d->stride_w, d->pad_h, d->pad_w, d->act, stream),
+  if (x_stride == 0) x_stride = cs_of(d->c);
+  if (x_stride < cs_of(d->c) || x_stride % 8 != 0)
+    return fail(LOTUS_ERR_INVALID, "maxpool2d: input pixel stride must be a multiple of 8 and >= roundup(c, 8)");
+  return cuda_status(launch_maxpool(x, x_stride, y, d->n, d->c, cs_of(d->c), d->h, d->w, oh, ow, d->kh, d->kw,
+                                    d->stride_h, d->stride_w, d->pad_h, d->pad_w, d->act, stream),
                      "maxpool2d");
+}
+
+int lotus_maxpool2d_fwd(const void* x, void* y, const lotus_pool2d_desc* d, cudaStream_t stream) {
+  return maxpool_impl(x, 0, y, d, stream);
+}
+
+int lotus_maxpool2d_fwd_strided(const void* x, int x_pixel_stride, void* y, const lotus_pool2d_desc* d,
+                                cudaStream_t stream) {
+  if (x_pixel_stride <= 0) return fail(LOTUS_ERR_INVALID, "maxpool2d_strided: pixel stride must be positive");
+  return maxpool_impl(x, x_pixel_stride, y, d, stream);
 }
 
 // Row-conv arguments of a conv (+ pool) request, or an error status.

@@ -103,7 +103,8 @@ struct ConvTcParams {
   int OH, OW;
   int kh, kw, sh, sw, ph, pw;
   int Cout;      // GEMM N (columns with real outputs)
-  int Cs_out;    // pixel stride of the NHWC fp16 output
+  int Cs_out;    // channels written per output pixel (roundup(Cout, 8)); the residual's pixel stride
+  int y_stride;  // pixel stride of the NHWC fp16 output (>= Cs_out: a channel slice of a wider tensor)
   int M;
   int KB;        // number of 64-wide K blocks
   int act;
@@ -323,7 +324,7 @@ __device__ __forceinline__ void epi_store_nhwc(const ConvTcParams& p, const uint
     const uint4 val = st[r * 4 + ((c ^ (r >> 1)) & 3)];
     const int col = n0 + cl + c * 8;
     if (em_r >= 0 && (full || col < p.Cs_out))
-      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em_r) * p.Cs_out + col) = val;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em_r) * p.y_stride + col) = val;
   }
   __syncwarp();  // the buffer is rewritten by the next chunk
 }
@@ -349,7 +350,7 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
                                           const float* sb, bool full, const uint4* res, int sc_n, int sc_iy,
                                           int sc_ix) {
   if (OUT == 0) {
-    __half* yrow = reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em) * p.Cs_out + n0;
+    __half* yrow = reinterpret_cast<__half*>(p.y) + static_cast<int64_t>(em) * p.y_stride + n0;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const int c = cl + g * 8;  // column inside the tile
@@ -417,7 +418,7 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
         const int ox = sc_ix * p.t_sw + kx - p.t_pw;
         if ((unsigned)oy >= (unsigned)p.t_oh || (unsigned)ox >= (unsigned)p.t_ow) continue;
         __half* ypix = reinterpret_cast<__half*>(p.y) +
-                       ((static_cast<int64_t>(sc_n) * p.t_oh + oy) * p.t_ow + ox) * p.Cs_out;
+                       ((static_cast<int64_t>(sc_n) * p.t_oh + oy) * p.t_ow + ox) * p.y_stride;
         float f[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) f[j] = act_t<ACT>(__uint_as_float(v[g * 8 + j]) + bias_of(p, sb, n0, co + j));
@@ -434,7 +435,7 @@ __device__ __forceinline__ void epi_chunk(const ConvTcParams& p, const uint32_t 
           const int ox2 = sc_ix * p.t_sw + kx2 - p.t_pw;
           if ((unsigned)oy2 >= (unsigned)p.t_oh || (unsigned)ox2 >= (unsigned)p.t_ow) continue;
           __half* yp = reinterpret_cast<__half*>(p.y) +
-                       ((static_cast<int64_t>(sc_n) * p.t_oh + oy2) * p.t_ow + ox2) * p.Cs_out;
+                       ((static_cast<int64_t>(sc_n) * p.t_oh + oy2) * p.t_ow + ox2) * p.y_stride;
           yp[c2] = __float2half_rn(act_t<ACT>(__uint_as_float(v[g * 8 + j]) + bias_of(p, sb, n0, c2)));
         }
       }
@@ -1357,7 +1358,8 @@ uint32_t wait_limit_from_env() {
 // fp16 output (pad channels written as zero) or fp32 rows.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int ws_rows, int ws_ld,
                                      const float* __restrict__ bias, const __half* __restrict__ residual,
-                                     void* __restrict__ y, int M, int cout, int cs_out, int act, int out_kind) {
+                                     void* __restrict__ y, int M, int cout, int cs_out, int y_stride, int act,
+                                     int out_kind) {
   const int groups = out_kind == 0 ? cs_out / 8 : (cout + 7) / 8;
   const int total = M * groups;  // < 2^31, checked by the launcher
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -1389,7 +1391,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
       o[j] = c < cout ? apply_act(v, act) : 0.f;
     }
     if (out_kind == 0) {
-      *reinterpret_cast<uint4*>(static_cast<__half*>(y) + static_cast<size_t>(m) * cs_out + c0) =
+      *reinterpret_cast<uint4*>(static_cast<__half*>(y) + static_cast<size_t>(m) * y_stride + c0) =
           make_uint4(pack_half2(o[0], o[1]), pack_half2(o[2], o[3]), pack_half2(o[4], o[5]), pack_half2(o[6], o[7]));
     } else {
       float* yr = static_cast<float*>(y) + static_cast<size_t>(m) * cout;
@@ -1470,6 +1472,7 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, s
   p.pw = a.pw;
   p.Cout = a.n_cols;
   p.Cs_out = a.Cs_out;
+  p.y_stride = a.y_stride > 0 ? a.y_stride : a.Cs_out;
   p.M = a.M;
   p.KB = a.k_pad / kBlockK;
   p.act = a.act;
@@ -1606,7 +1609,7 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, s
     const unsigned grid = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, static_cast<size_t>(num_sms()) * 8));
     splitk_reduce_kernel<<<grid, 256, 0, stream>>>(p.ws, p.ksplit, p.ws_rows, p.ws_ld, a.bias,
                                                    static_cast<const __half*>(a.residual), a.y, a.M, a.n_cols,
-                                                   a.Cs_out, a.act, a.out_kind);
+                                                   a.Cs_out, p.y_stride, a.act, a.out_kind);
     note_launch();
     e = cudaGetLastError();
   }

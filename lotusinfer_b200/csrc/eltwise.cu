@@ -62,8 +62,8 @@ __global__ void concat_vec_kernel(const uint4* __restrict__ a, int ga, const uin
   }
 }
 
-__global__ void tconv_fill_bias_kernel(__half* __restrict__ y, const float* __restrict__ bias, int cout, int cs,
-                                       size_t pixels, int act) {
+__global__ void tconv_fill_bias_kernel(__half* __restrict__ y, int ys, const float* __restrict__ bias, int cout,
+                                       int cs, size_t pixels, int act) {
   const int groups = cs / 8;
   const size_t total = pixels * groups;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
@@ -75,14 +75,15 @@ __global__ void tconv_fill_bias_kernel(__half* __restrict__ y, const float* __re
       const int c = g * 8 + j;
       f[j] = c < cout ? act_fn(bias ? bias[c] : 0.f, act) : 0.f;
     }
-    reinterpret_cast<uint4*>(y)[i] = pack8(f);
+    reinterpret_cast<uint4*>(y + (i / groups) * ys)[g] = pack8(f);
   }
 }
 
 // Output-stationary transposed convolution for any stride/kernel/padding.
 // Weights are the GEMM-prepacked rows ((ky*kw + kx)*cout + co) x k_pad.
 __global__ void tconv_direct_kernel(const __half* __restrict__ x, const __half* __restrict__ wp, int k_pad,
-                                    const float* __restrict__ bias, __half* __restrict__ y, int n, int cin, int csi,
+                                    const float* __restrict__ bias, __half* __restrict__ y, int ys, int n, int cin,
+                                    int csi,
                                     int h, int w, int cout, int cso, int oh, int ow, int kh, int kw, int sh, int sw,
                                     int ph, int pw, int act) {
   const size_t total = static_cast<size_t>(n) * oh * ow * cso;
@@ -95,7 +96,7 @@ __global__ void tconv_direct_kernel(const __half* __restrict__ x, const __half* 
     const int oy = static_cast<int>(t % oh);
     const int img = static_cast<int>(t / oh);
     if (co >= cout) {
-      y[i] = __float2half_rn(0.f);
+      y[pix * ys + co] = __float2half_rn(0.f);
       continue;
     }
     float acc = bias ? bias[co] : 0.f;
@@ -114,7 +115,7 @@ __global__ void tconv_direct_kernel(const __half* __restrict__ x, const __half* 
         for (int ci = 0; ci < cin; ++ci) acc += __half2float(xp[ci]) * __half2float(wr[ci]);
       }
     }
-    y[i] = __float2half_rn(act_fn(acc, act));
+    y[pix * ys + co] = __float2half_rn(act_fn(acc, act));
   }
 }
 
@@ -141,21 +142,22 @@ cudaError_t launch_concat(const void* a, int csa, const void* b, int csb, void* 
   return cudaGetLastError();
 }
 
-cudaError_t launch_tconv_fill_bias(void* y, const float* bias, int cout, int cs, size_t pixels, int act,
+cudaError_t launch_tconv_fill_bias(void* y, int y_stride, const float* bias, int cout, int cs, size_t pixels, int act,
                                    cudaStream_t s) {
-  tconv_fill_bias_kernel<<<grid_for(pixels * (cs / 8), 256), 256, 0, s>>>(static_cast<__half*>(y), bias, cout, cs,
-                                                                          pixels, act);
+  tconv_fill_bias_kernel<<<grid_for(pixels * (cs / 8), 256), 256, 0, s>>>(static_cast<__half*>(y), y_stride, bias,
+                                                                          cout, cs, pixels, act);
   note_launch();
   return cudaGetLastError();
 }
 
-cudaError_t launch_tconv_direct(const void* x, const void* wp, int k_pad, const float* bias, void* y, int n, int cin,
-                                int csi, int h, int w_, int cout, int cso, int oh, int ow, int kh, int kw, int sh,
-                                int sw, int ph, int pw, int act, cudaStream_t s) {
+cudaError_t launch_tconv_direct(const void* x, const void* wp, int k_pad, const float* bias, void* y, int y_stride,
+                                int n, int cin, int csi, int h, int w_, int cout, int cso, int oh, int ow, int kh,
+                                int kw, int sh, int sw, int ph, int pw, int act, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * oh * ow * cso;
   tconv_direct_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half*>(x),
                                                            static_cast<const __half*>(wp), k_pad, bias,
-                                                           static_cast<__half*>(y), n, cin, csi, h, w_, cout, cso, oh,
+                                                           static_cast<__half*>(y), y_stride, n, cin, csi, h, w_,
+                                                           cout, cso, oh,
                                                            ow, kh, kw, sh, sw, ph, pw, act);
   note_launch();
   return cudaGetLastError();

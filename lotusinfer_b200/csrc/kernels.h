@@ -33,6 +33,7 @@ struct ConvTcArgs {
   int t_oh, t_ow, t_sh, t_sw, t_ph, t_pw, t_kw, t_cout;
   float* ws = nullptr;    // split-K workspace (fp32) or null
   size_t ws_bytes = 0;
+  int y_stride = 0;       // pixel stride of an NHWC fp16 output (0 = Cs_out)
 };
 
 // Launches the conv / GEMM kernel (and the split-K reduction when it splits).
@@ -88,8 +89,9 @@ cudaError_t launch_space_to_depth(const float* x, void* y, int n, int c, int h, 
 cudaError_t launch_nhwc_to_nchw(const void* x, float* y, int n, int c, int h, int w, int cs, cudaStream_t s);
 
 // pool.cu
-cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow, int kh, int kw,
-                           int sh, int sw, int ph, int pw, int act, cudaStream_t s);
+// x_stride: input pixel stride (elements; a channel slice of a wider tensor), cs: output pixel stride
+cudaError_t launch_maxpool(const void* x, int x_stride, void* y, int n, int c, int cs, int h, int w, int oh, int ow,
+                           int kh, int kw, int sh, int sw, int ph, int pw, int act, cudaStream_t s);
 cudaError_t launch_adaptive_avgpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow,
                                     int act, int out_f32, cudaStream_t s);
 
@@ -98,11 +100,11 @@ cudaError_t launch_add_act(const void* a, const void* b, void* y, size_t pixels,
                            cudaStream_t s);
 cudaError_t launch_concat(const void* a, int csa, const void* b, int csb, void* y, int ca, int cb, int csy,
                           size_t pixels, cudaStream_t s);
-cudaError_t launch_tconv_fill_bias(void* y, const float* bias, int cout, int cs, size_t pixels, int act,
+cudaError_t launch_tconv_fill_bias(void* y, int y_stride, const float* bias, int cout, int cs, size_t pixels, int act,
                                    cudaStream_t s);
-cudaError_t launch_tconv_direct(const void* x, const void* wp, int k_pad, const float* bias, void* y, int n, int cin,
-                                int csi, int h, int w_, int cout, int cso, int oh, int ow, int kh, int kw, int sh,
-                                int sw, int ph, int pw, int act, cudaStream_t s);
+cudaError_t launch_tconv_direct(const void* x, const void* wp, int k_pad, const float* bias, void* y, int y_stride,
+                                int n, int cin, int csi, int h, int w_, int cout, int cso, int oh, int ow, int kh,
+                                int kw, int sh, int sw, int ph, int pw, int act, cudaStream_t s);
 
 // preprocess.cu
 cudaError_t launch_preprocess(const uint8_t* src, int n, int h, int w, int rh, int rw, int ch, int cw,

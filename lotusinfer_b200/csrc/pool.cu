@@ -26,8 +26,9 @@ using namespace lotus_dev;
 // unrolled and in flight together (with runtime kh/kw each load waits for the
 // loop control of the one before); KS = 0: any window.
 template <typename IT, int KS>
-__global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __restrict__ y, int n, int c, int cs, int h,
-                                    int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int act) {
+__global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, int xs, __half* __restrict__ y, int n, int c, int cs,
+                                    int h, int w, int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw,
+                                    int act) {
   if (KS > 0) {
     kh = KS;
     kw = KS;
@@ -46,7 +47,7 @@ __global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __rest
 #pragma unroll
     for (int j = 0; j < 8; ++j) m[j] = -INFINITY;
     const int y0 = oy * sh - ph, x0 = ox * sw - pw;
-    const __half* xb = x + static_cast<IT>(img) * h * w * cs + g * 8;
+    const __half* xb = x + static_cast<IT>(img) * h * w * xs + g * 8;
 #pragma unroll
     for (int r = 0; r < (KS > 0 ? KS : kh); ++r) {
       const int iy = y0 + r;
@@ -56,7 +57,7 @@ __global__ void maxpool_nhwc_kernel(const __half* __restrict__ x, __half* __rest
         const int ix = x0 + s;
         if (ix < 0 || ix >= w) continue;
         float f[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (static_cast<IT>(iy) * w + ix) * cs)), f);
+        unpack8(__ldg(reinterpret_cast<const uint4*>(xb + (static_cast<IT>(iy) * w + ix) * xs)), f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) m[j] = fmaxf(m[j], f[j]);
       }
@@ -161,19 +162,22 @@ __global__ void __launch_bounds__(256) adaptive_avgpool_window_kernel(const __ha
   }
 }
 
-cudaError_t launch_maxpool(const void* x, void* y, int n, int c, int cs, int h, int w, int oh, int ow, int kh, int kw,
-                           int sh, int sw, int ph, int pw, int act, cudaStream_t s) {
+cudaError_t launch_maxpool(const void* x, int x_stride, void* y, int n, int c, int cs, int h, int w, int oh, int ow,
+                           int kh, int kw, int sh, int sw, int ph, int pw, int act, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
-  const bool small = static_cast<size_t>(n) * h * w * cs < (1u << 31) && total < (1u << 31);
+  const bool small = static_cast<size_t>(n) * h * w * x_stride < (1u << 31) && total < (1u << 31);
   if (small && kh == 3 && kw == 3)
     maxpool_nhwc_kernel<int, 3><<<grid_for(total, 256, 32), 256, 0, s>>>(
-        static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
+        static_cast<const __half*>(x), x_stride, static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph,
+        pw, act);
   else if (small)
     maxpool_nhwc_kernel<int, 0><<<grid_for(total, 256, 32), 256, 0, s>>>(
-        static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
+        static_cast<const __half*>(x), x_stride, static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph,
+        pw, act);
   else
     maxpool_nhwc_kernel<size_t, 0><<<grid_for(total, 256), 256, 0, s>>>(
-        static_cast<const __half*>(x), static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph, pw, act);
+        static_cast<const __half*>(x), x_stride, static_cast<__half*>(y), n, c, cs, h, w, oh, ow, kh, kw, sh, sw, ph,
+        pw, act);
   note_launch();
   return cudaGetLastError();
 }

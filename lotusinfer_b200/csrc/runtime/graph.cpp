@@ -1,6 +1,7 @@
 #include "graph.hpp"
 
 #include <algorithm>
+#include <functional>
 #include <queue>
 #include <set>
 #include <stdexcept>
@@ -333,11 +334,14 @@ void Graph::Build(const std::string& param_path, const std::string& bin_path) {
     }
     const auto& s = shapes.at(n);
     const bool f32 = (n == input_operand_) || (n == output_operand_);
-    if (!aliased.count(n)) opnd->tensor_ = Tensor(s, f32 ? Format::kNCHW_F32 : Format::kNHWC_F16);
+    if (!aliased.count(n)) opnd->tensor_ = Tensor::Unallocated(s, f32 ? Format::kNCHW_F32 : Format::kNHWC_F16);
     operands_[n] = opnd;
   }
 
   TopoSortLayers();
+  std::map<std::string, std::pair<std::string, uint32_t>> slice_of;  // operand -> (concat operand, first channel)
+  if (opt_.fuse_concat) FuseConcats(&slice_of);
+  PlanMemory(slice_of);
   // bind in order so flatten aliases exist before their consumers bind
   for (auto& l : topo_sorted_layers_) l->Bind(operands_);
   // one split-K workspace for the layer that wants the most
@@ -350,6 +354,133 @@ void Graph::Build(const std::string& param_path, const std::string& bin_path) {
     for (auto& l : topo_sorted_layers_) l->SetWorkspace(p, ws);
   }
   CudaCheck(cudaStreamSynchronize(stream_), "graph build");
+}
+
+std::shared_ptr<Layer> Graph::ProducerOf(const std::string& operand) const {
+  for (auto& l : topo_sorted_layers_)
+    for (auto& o : l->outputs_name_)
+      if (o == operand) return l;
+  return nullptr;
+}
+
+void Graph::FuseConcats(std::map<std::string, std::pair<std::string, uint32_t>>* slice_of) {
+  // torch.cat(a, b) along channels with both halves produced by a conv or a
+  // transposed conv: the producers write straight into their channel slice of
+  // the concat buffer (NHWC: a pixel-stride change), and the concat launches
+  // nothing.  Other readers of a half must take a strided input: max pools
+  // (the U-Net encoder output feeds both the next level's pool and the
+  // decoder's concat).  The reference copies both halves into the concat
+  // operand per sample (source/layer/concatenate.cpp:20-35).
+  auto writes_slices = [](const std::shared_ptr<Layer>& l) {
+    if (auto c = std::dynamic_pointer_cast<Conv2dLayer>(l)) return !c->HasPool();
+    return std::dynamic_pointer_cast<TransposedConv2dLayer>(l) != nullptr;
+  };
+  for (auto& l : topo_sorted_layers_) {
+    auto cat = std::dynamic_pointer_cast<CatLayer>(l);
+    if (!cat) continue;
+    const std::string a = cat->inputs_name_.at(0), b = cat->inputs_name_.at(1), y = cat->outputs_name_.at(0);
+    if (a == b || a == input_operand_ || b == input_operand_ || y == output_operand_) continue;
+    if (slice_of->count(a) || slice_of->count(b) || slice_of->count(y)) continue;
+    const Tensor& ta = operands_.at(a)->tensor_;
+    const Tensor& tb = operands_.at(b)->tensor_;
+    const Tensor& ty = operands_.at(y)->tensor_;
+    if (ta.Fmt() != Format::kNHWC_F16 || tb.Fmt() != Format::kNHWC_F16 || ty.Fmt() != Format::kNHWC_F16) continue;
+    if (ta.DimSize() != 4 || tb.DimSize() != 4 || ty.DimSize() != 4 || ta.Dim(1) % 8 != 0) continue;
+    if (!writes_slices(ProducerOf(a)) || !writes_slices(ProducerOf(b))) continue;
+    bool other_readers_ok = true;
+    for (auto& r : topo_sorted_layers_) {
+      if (r == l) continue;
+      for (auto& in : r->inputs_name_)
+        if ((in == a || in == b) && !std::dynamic_pointer_cast<Maxpool2dLayer>(r)) other_readers_ok = false;
+    }
+    if (!other_readers_ok) continue;
+    (*slice_of)[a] = {y, 0};
+    (*slice_of)[b] = {y, ta.Dim(1)};
+    cat->SetFused();
+  }
+}
+
+void Graph::PlanMemory(const std::map<std::string, std::pair<std::string, uint32_t>>& slice_of) {
+  // Storage roots: operands with storage of their own (channel slices live in
+  // their concat buffer, flatten outputs alias their input).  A root is live
+  // from the first layer that writes it (or a slice of it) to the last layer
+  // that reads it (or an alias or slice of it), in the order the layers run.
+  // With the plan on, a root takes the smallest free block of at least its
+  // size whose last reader ran strictly before the root's first writer (the
+  // layers run one after another on one stream, replayed from one CUDA
+  // graph), else a new block.  The graph input and output keep their own
+  // buffers (the caller copies into and out of them).  The reference
+  // allocates every operand separately (source/graph.cpp:50-82).
+  std::map<std::string, std::string> alias_of;
+  for (auto& l : topo_sorted_layers_)
+    if (std::dynamic_pointer_cast<FlattenLayer>(l)) alias_of[l->outputs_name_.at(0)] = l->inputs_name_.at(0);
+  std::function<std::string(const std::string&)> root = [&](const std::string& n) -> std::string {
+    auto s = slice_of.find(n);
+    if (s != slice_of.end()) return root(s->second.first);
+    auto a = alias_of.find(n);
+    if (a != alias_of.end()) return root(a->second);
+    return n;
+  };
+  std::map<std::string, int> first, last;
+  for (size_t i = 0; i < topo_sorted_layers_.size(); ++i) {
+    const int ii = static_cast<int>(i);
+    for (auto& o : topo_sorted_layers_[i]->outputs_name_) {
+      const std::string r = root(o);
+      if (!first.count(r)) first[r] = ii;
+      last[r] = std::max(last.count(r) ? last[r] : ii, ii);
+    }
+    for (auto& in : topo_sorted_layers_[i]->inputs_name_) {
+      const std::string r = root(in);
+      last[r] = std::max(last.count(r) ? last[r] : ii, ii);
+    }
+  }
+  std::vector<std::string> roots;
+  for (auto& kv : operands_)
+    if (!slice_of.count(kv.first) && !alias_of.count(kv.first)) roots.push_back(kv.first);
+  std::stable_sort(roots.begin(), roots.end(), [&](const std::string& x, const std::string& y) {
+    const int fx = first.count(x) ? first.at(x) : -1, fy = first.count(y) ? first.at(y) : -1;
+    return fx < fy;
+  });
+  struct Block {
+    std::shared_ptr<void> mem;
+    size_t bytes;
+    int free_after;
+  };
+  std::vector<Block> blocks;
+  auto alloc = [](size_t bytes) {
+    void* p = nullptr;
+    CudaCheck(cudaMalloc(&p, bytes ? bytes : 16), "cudaMalloc(activations)");
+    return std::shared_ptr<void>(p, [](void* q) { cudaFree(q); });
+  };
+  activation_bytes_ = 0;
+  for (auto& r : roots) {
+    Tensor& t = operands_.at(r)->tensor_;
+    const size_t need = (t.Bytes() + 255) / 256 * 256;
+    const bool dedicated = r == input_operand_ || r == output_operand_ || !first.count(r);
+    if (!opt_.plan_memory || dedicated) {
+      t.BindStorage(alloc(need), 0);
+      activation_bytes_ += need;
+      continue;
+    }
+    Block* best = nullptr;
+    for (auto& b : blocks)
+      if (b.free_after < first.at(r) && b.bytes >= need && (!best || b.bytes < best->bytes)) best = &b;
+    if (!best) {
+      blocks.push_back(Block{alloc(need), need, -1});
+      activation_bytes_ += need;
+      best = &blocks.back();
+    }
+    best->free_after = last.at(r);
+    t.BindStorage(best->mem, 0);
+  }
+  // channel slices, parents first (a slice's parent is a root or a slice)
+  std::function<void(const std::string&)> bind_slice = [&](const std::string& n) {
+    const auto& sv = slice_of.at(n);
+    if (slice_of.count(sv.first)) bind_slice(sv.first);
+    Tensor& t = operands_.at(n)->tensor_;
+    t = operands_.at(sv.first)->tensor_.ChannelSlice(sv.second, t.Dim(1));
+  };
+  for (auto& kv : slice_of) bind_slice(kv.first);
 }
 
 void Graph::TopoSortLayers() {

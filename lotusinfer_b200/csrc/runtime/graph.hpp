@@ -32,6 +32,8 @@ class Graph {
     bool fuse_residual = true;   // fold conv -> add (-> ReLU) into the conv epilogue
     bool s2d_stem = true;        // run a strided few-channel stem conv over the space-to-depth input
     bool fuse_pool = true;       // fold a 3x3/2 max pool into the conv that feeds it, where the fused kernel applies
+    bool fuse_concat = true;     // producers of a torch.cat write their channel slice of it in place
+    bool plan_memory = true;     // operands whose lifetimes do not overlap share device memory
   };
 
   Graph(const std::string& param_path, const std::string& bin_path, uint32_t batch_size);
@@ -77,10 +79,15 @@ class Graph {
   }
   // Library kernel launches per Forward.
   int LaunchesPerForward() const;
+  // Device bytes held by the operands (activations, graph input and output).
+  size_t ActivationBytes() const { return activation_bytes_; }
 
  private:
   void Build(const std::string& param_path, const std::string& bin_path);
   void TopoSortLayers();
+  std::shared_ptr<Layer> ProducerOf(const std::string& operand) const;
+  void FuseConcats(std::map<std::string, std::pair<std::string, uint32_t>>* slice_of);
+  void PlanMemory(const std::map<std::string, std::pair<std::string, uint32_t>>& slice_of);
   void RunLayers(cudaStream_t s);
 
   std::map<std::string, std::shared_ptr<Layer>> layers_;
@@ -98,6 +105,7 @@ class Graph {
   int stem_s2d_ = 1, stem_pad_h_ = 0, stem_pad_w_ = 0;
   std::vector<uint32_t> stem_shape_;
   std::shared_ptr<void> workspace_;  // split-K scratch shared by the layers (one stream, one layer at a time)
+  size_t activation_bytes_ = 0;
 
   // pipelined path (Submit): slot 1's buffers, one captured forward per slot,
   // the copy streams and the events that order them

@@ -41,6 +41,8 @@ lotus_graph* lotus_graph_create(const char* param_path, const char* bin_path, in
     o.fuse_residual = (flags & LOTUS_GRAPH_NO_RESIDUAL_FUSION) == 0;
     o.s2d_stem = (flags & LOTUS_GRAPH_NO_S2D_STEM) == 0;
     o.fuse_pool = (flags & LOTUS_GRAPH_NO_POOL_FUSION) == 0;
+    o.fuse_concat = (flags & LOTUS_GRAPH_NO_CONCAT_FUSION) == 0;
+    o.plan_memory = (flags & LOTUS_GRAPH_NO_MEMORY_PLAN) == 0;
     std::unique_ptr<lotus::Graph> graph(new lotus::Graph(param_path, bin_path, static_cast<uint32_t>(batch), o));
     auto* h = new lotus_graph;
     h->g = std::move(graph);
@@ -181,6 +183,8 @@ const void* lotus_graph_layer_weight(const lotus_graph* g, int i, size_t* bytes)
 }
 
 int lotus_graph_launches_per_forward(const lotus_graph* g) { return g ? g->g->LaunchesPerForward() : -1; }
+
+size_t lotus_graph_activation_bytes(const lotus_graph* g) { return g ? g->g->ActivationBytes() : 0; }
 
 int lotus_graph_profile_layers(lotus_graph* g, int reps, float* ms) {
   if (!g || !ms || reps <= 0) return lotus_impl::set_error(LOTUS_ERR_INVALID, "graph_profile_layers: bad arguments");

@@ -167,6 +167,9 @@ void Conv2dLayer::Bind(const OperandMap& operands) {
   const Tensor& y = outputs_[0]->tensor_;
   if (x.Fmt() != Format::kNHWC_F16 || y.Fmt() != Format::kNHWC_F16 || x.DimSize() != 4 || y.DimSize() != 4)
     throw std::runtime_error(name_ + ": conv expects NHWC fp16 4-D operands");
+  if (!x.Dense()) throw std::runtime_error(name_ + ": conv input must be a dense tensor");
+  if (!y.Dense() && (has_pool_ || !residual_name_.empty()))
+    throw std::runtime_error(name_ + ": a pooled or residual conv cannot write a channel slice");
   desc_.n = x.Dim(0);
   desc_.h = x.Dim(2);
   desc_.w = x.Dim(3);
@@ -198,8 +201,16 @@ void Conv2dLayer::Forward(cudaStream_t stream) {
     return;
   }
   const void* res = residual_name_.empty() ? nullptr : inputs_.back()->tensor_.Data();
+  const Tensor& y = outputs_[0]->tensor_;
+  if (!y.Dense()) {  // a channel slice of a concat buffer
+    LotusCheck(lotus_conv2d_fwd_slice(inputs_[0]->tensor_.Data(), w_packed_.get(),
+                                      static_cast<const float*>(bias_.get()), res, y.Data(),
+                                      static_cast<int>(y.PixelStride()), &desc_, workspace_, workspace_bytes_, stream),
+               name_);
+    return;
+  }
   LotusCheck(lotus_conv2d_fwd_ws(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
-                                 res, outputs_[0]->tensor_.Data(), &desc_, workspace_, workspace_bytes_, stream),
+                                 res, y.Data(), &desc_, workspace_, workspace_bytes_, stream),
              name_);
 }
 
@@ -239,6 +250,7 @@ void TransposedConv2dLayer::Bind(const OperandMap& operands) {
   Layer::Bind(operands);
   const Tensor& x = inputs_[0]->tensor_;
   const Tensor& y = outputs_[0]->tensor_;
+  if (!x.Dense()) throw std::runtime_error(name_ + ": transposed conv input must be a dense tensor");
   desc_.n = x.Dim(0);
   desc_.h = x.Dim(2);
   desc_.w = x.Dim(3);
@@ -251,8 +263,16 @@ void TransposedConv2dLayer::Bind(const OperandMap& operands) {
 }
 
 void TransposedConv2dLayer::Forward(cudaStream_t stream) {
+  const Tensor& y = outputs_[0]->tensor_;
+  if (!y.Dense()) {  // a channel slice of a concat buffer
+    LotusCheck(lotus_tconv2d_fwd_slice(inputs_[0]->tensor_.Data(), w_packed_.get(),
+                                       static_cast<const float*>(bias_.get()), y.Data(),
+                                       static_cast<int>(y.PixelStride()), &desc_, stream),
+               name_);
+    return;
+  }
   LotusCheck(lotus_tconv2d_fwd(inputs_[0]->tensor_.Data(), w_packed_.get(), static_cast<const float*>(bias_.get()),
-                               outputs_[0]->tensor_.Data(), &desc_, stream),
+                               y.Data(), &desc_, stream),
              name_);
 }
 
@@ -339,7 +359,14 @@ void Maxpool2dLayer::Bind(const OperandMap& operands) {
 }
 
 void Maxpool2dLayer::Forward(cudaStream_t stream) {
-  LotusCheck(lotus_maxpool2d_fwd(inputs_[0]->tensor_.Data(), outputs_[0]->tensor_.Data(), &desc_, stream), name_);
+  const Tensor& x = inputs_[0]->tensor_;
+  if (!x.Dense()) {  // the encoder half of a concat buffer
+    LotusCheck(lotus_maxpool2d_fwd_strided(x.Data(), static_cast<int>(x.PixelStride()), outputs_[0]->tensor_.Data(),
+                                           &desc_, stream),
+               name_);
+    return;
+  }
+  LotusCheck(lotus_maxpool2d_fwd(x.Data(), outputs_[0]->tensor_.Data(), &desc_, stream), name_);
 }
 
 AdaptiveAvgpool2dLayer::AdaptiveAvgpool2dLayer(const pnnx::Operator& op, int oh, int ow) : oh_(oh), ow_(ow) {
@@ -413,6 +440,7 @@ CatLayer::CatLayer(const pnnx::Operator& op) {
 }
 
 void CatLayer::Forward(cudaStream_t stream) {
+  if (fused_) return;
   const Tensor& a = inputs_[0]->tensor_;
   const Tensor& b = inputs_[1]->tensor_;
   LotusCheck(lotus_concat_channels_fwd(a.Data(), a.Dim(1), b.Data(), b.Dim(1), outputs_[0]->tensor_.Data(), a.Dim(0),

@@ -232,6 +232,14 @@ class CatLayer : public Layer {
  public:
   explicit CatLayer(const pnnx::Operator& op);
   void Forward(cudaStream_t stream) override;
+  // Both halves are written in place by their producers: nothing to launch.
+  void SetFused() { fused_ = true; }
+  bool Fused() const { return fused_; }
+  int Launches() const override { return fused_ ? 0 : 1; }
+  double Bytes() const override { return fused_ ? 0.0 : Layer::Bytes(); }
+
+ private:
+  bool fused_ = false;
 };
 
 }  // namespace lotus

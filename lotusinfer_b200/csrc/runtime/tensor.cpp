@@ -66,6 +66,7 @@ uint32_t Tensor::ChannelStride() const {
 
 Tensor Tensor::Element(uint32_t i) const {
   if (shape_.empty() || i >= shape_[0]) throw std::runtime_error("Element: index out of range");
+  if (!Dense()) throw std::runtime_error("Element: not supported on a channel slice");
   Tensor t;
   t.shape_ = shape_;
   t.shape_[0] = 1;
@@ -77,6 +78,7 @@ Tensor Tensor::Element(uint32_t i) const {
 }
 
 Tensor Tensor::View(const std::vector<uint32_t>& shape, Format fmt) const {
+  if (!Dense()) throw std::runtime_error("View: not supported on a channel slice");
   Tensor t;
   t.shape_ = shape;
   t.fmt_ = fmt;
@@ -85,6 +87,32 @@ Tensor Tensor::View(const std::vector<uint32_t>& shape, Format fmt) const {
   t.bytes_ = StorageBytes(shape, fmt);
   if (t.bytes_ > bytes_) throw std::runtime_error("View larger than storage");
   return t;
+}
+
+Tensor Tensor::ChannelSlice(uint32_t c0, uint32_t c) const {
+  if (fmt_ != Format::kNHWC_F16 || shape_.size() != 4) throw std::runtime_error("ChannelSlice: needs a 4-D NHWC tensor");
+  if (c0 % 8 != 0 || c == 0 || c0 + c > shape_[1]) throw std::runtime_error("ChannelSlice: bad channel range");
+  Tensor t;
+  t.shape_ = {shape_[0], c, shape_[2], shape_[3]};
+  t.fmt_ = fmt_;
+  t.data_ = data_;
+  t.offset_ = offset_ + static_cast<size_t>(c0) * 2;
+  t.bytes_ = StorageBytes(t.shape_, fmt_);  // the slice's own (dense-equivalent) bytes
+  t.pixel_stride_ = PixelStride();
+  return t;
+}
+
+Tensor Tensor::Unallocated(const std::vector<uint32_t>& shape, Format fmt) {
+  Tensor t;
+  t.shape_ = shape;
+  t.fmt_ = fmt;
+  t.bytes_ = StorageBytes(shape, fmt);
+  return t;
+}
+
+void Tensor::BindStorage(std::shared_ptr<void> data, size_t offset) {
+  data_ = std::move(data);
+  offset_ = offset;
 }
 
 }  // namespace lotus

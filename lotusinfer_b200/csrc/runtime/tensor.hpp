@@ -52,6 +52,20 @@ class Tensor {
   Tensor Element(uint32_t i) const;
   // Alias with a different logical shape and format (no copy).
   Tensor View(const std::vector<uint32_t>& shape, Format fmt) const;
+  // Channels [c0, c0 + c) of a 4-D NHWC fp16 tensor as a tensor of its own:
+  // same storage, the slice's first channel as its start, consecutive pixels
+  // PixelStride() elements apart (c0 must be a multiple of 8).
+  Tensor ChannelSlice(uint32_t c0, uint32_t c) const;
+  // Elements between consecutive pixels of an NHWC fp16 tensor: the channel
+  // stride of a dense tensor, the parent's for a channel slice.
+  uint32_t PixelStride() const { return pixel_stride_ ? pixel_stride_ : ChannelStride(); }
+  bool Dense() const { return pixel_stride_ == 0 || pixel_stride_ == ChannelStride(); }
+
+  // A tensor with a shape but no storage yet (the graph's memory planner binds
+  // it), and the binding: `bytes` of `data` starting at byte `offset` must
+  // cover StorageBytes(shape, fmt).
+  static Tensor Unallocated(const std::vector<uint32_t>& shape, Format fmt);
+  void BindStorage(std::shared_ptr<void> data, size_t offset);
 
   static size_t StorageBytes(const std::vector<uint32_t>& shape, Format fmt);
 
@@ -61,6 +75,7 @@ class Tensor {
   std::shared_ptr<void> data_;
   size_t offset_ = 0;
   size_t bytes_ = 0;
+  uint32_t pixel_stride_ = 0;  // 0: dense
 };
 
 }  // namespace lotus

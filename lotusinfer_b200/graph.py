@@ -48,12 +48,15 @@ GRAPH_SIGNATURES = {
     "lotus_graph_submit": (_I, [_V, _V, _V, _IP]),
     "lotus_graph_copy_stream": (_V, [_V, _I]),
     "lotus_graph_slot_output": (_V, [_V, _I]),
+    "lotus_graph_activation_bytes": (_S, [_V]),
 }
 
 NO_CUDA_GRAPH = 1
 NO_RESIDUAL_FUSION = 2
 NO_S2D_STEM = 4
 NO_POOL_FUSION = 8
+NO_CONCAT_FUSION = 16
+NO_MEMORY_PLAN = 32
 
 _bound = False
 
@@ -82,9 +85,11 @@ def _cuda_copy(dst: int, src: int, nbytes: int) -> None:
 
 class Graph:
     def __init__(self, param_path: str, bin_path: str, batch: int, device: int = -1, cuda_graph: bool = True,
-                 fuse_residual: bool = True, s2d_stem: bool = True, fuse_pool: bool = True):
+                 fuse_residual: bool = True, s2d_stem: bool = True, fuse_pool: bool = True, fuse_concat: bool = True,
+                 plan_memory: bool = True):
         flags = ((0 if cuda_graph else NO_CUDA_GRAPH) | (0 if fuse_residual else NO_RESIDUAL_FUSION) |
-                 (0 if s2d_stem else NO_S2D_STEM) | (0 if fuse_pool else NO_POOL_FUSION))
+                 (0 if s2d_stem else NO_S2D_STEM) | (0 if fuse_pool else NO_POOL_FUSION) |
+                 (0 if fuse_concat else NO_CONCAT_FUSION) | (0 if plan_memory else NO_MEMORY_PLAN))
         L = _lib()
         h = L.lotus_graph_create(param_path.encode(), bin_path.encode(), int(batch), int(device), flags)
         if not h:
@@ -227,6 +232,9 @@ class Graph:
         t = torch.empty(nb.value // 2, dtype=torch.float16, device="cuda")
         _cuda_copy(t.data_ptr(), int(ptr), nb.value)
         return t.cpu().numpy()
+
+    def activation_bytes(self) -> int:
+        return int(_lib().lotus_graph_activation_bytes(self._h))
 
     def launches_per_forward(self) -> int:
         return int(_lib().lotus_graph_launches_per_forward(self._h))
