@@ -289,11 +289,16 @@ def run_model(args):
     ms = _events_ms(g.forward, passes, s)
     flops = sum(l["flops"] for l in g.layers())
     peak, _, _, peak_src = _peaks()
+    layers = g.layers()
+    layer_ms = g.profile_layers(3) if not args.eager else []
     print(json.dumps({"model": args.model, "batch": args.batch, "mode": "eager" if args.eager else "cuda-graph",
                       "passes": passes, "ms_per_forward": ms, "images_per_s": args.batch / ms * 1e3,
                       "gflop_per_forward": flops / 1e9, "tflops": flops / ms / 1e9,
                       "frac_tensor_peak": flops / ms / 1e9 / peak, "peak_source": peak_src,
-                      "launches_per_forward": g.launches_per_forward()}), flush=True)
+                      "launches_per_forward": g.launches_per_forward(),
+                      "activation_mbytes": g.activation_bytes() / 1e6,
+                      "layer_ms": {l["name"]: [round(t, 4), round(l["flops"] / t / 1e9, 1) if t > 0 else 0]
+                                   for t, l in zip(layer_ms, layers)}}), flush=True)
     g.close()
     assert abi.device_error() == 0
     return 0
@@ -504,6 +509,7 @@ def main():
                        "precision": "fp16 operands, fp32 accumulate (TMEM), fp16 activations"},
             "roofline": roofline, "clocks": clocks, "e2e": e2e,
             "gpu_launches": g.launches_per_forward() * args.steps,
+            "activation_mbytes": g.activation_bytes() / 1e6,
             "layer_ms": {l["name"]: round(t, 4) for t, l in zip(layer_ms, layers)}}
     if rank == 0:
         # correctness at the benchmarked configuration: the first images of the
