@@ -17,34 +17,49 @@
 // and whose next dimension steps ONE pixel (an overlapping stride) lands a
 // whole input row as 128 rows of 128 bytes, 128B-swizzled: exactly the
 // K-major A operand of kernel row r for every position of the tile, with a
-// 1024-byte-aligned start.  Input rows live in a ring of kRowSlots slots;
-// output row oy reads slots of input rows oy .. oy+kh-1, so every input row
-// is loaded once per CTA segment and serves kh output rows.
+// 1024-byte-aligned start.
 //
-// Roles (608 threads):
+// Stacked weights: input row y feeds output rows y, y-1, .., y-kh+1 through
+// kernel rows 0..kh-1.  The kh weight blocks W_0..W_{kh-1} (64 rows each) lie
+// one after the other in shared memory, i.e. they form one B operand of
+// N = kh * 64 rows, so ONE set of 4 MMAs (K = 64 in steps of 16) per input
+// row computes all kh partial products.  The accumulators sit in a TMEM ring
+// of 8 blocks of 64 columns at DESCENDING positions: tile t (the t-th output
+// row of the CTA) uses block P(t) = 7 - t % 8, so the blocks of tiles
+// y, y-1, .., y-kh+1 are P(y), P(y)+1, .., P(y)+kh-1 (mod 8), contiguous
+// except where the window wraps past block 7, where the MMA is split in two.
+// Each input row is loaded once per CTA segment and read by one MMA group;
+// every accumulator is zeroed by the epilogue (tcgen05.st) when it is
+// drained, so every MMA accumulates.  For one output row the partial
+// products are summed in kernel-row order, then K order, as a plain
+// kernel-row loop would.
+//
+// Roles (576 threads):
 //   warps 0-15  epilogue: warp w drains TMEM lane quarter w%4, columns
-//               16*(w/4) .. +15.  Without the pool: bias, activation, fp16
-//               store of the conv row.  With the pool: fp16(acc + bias), its
-//               vertical max carried in registers from row to row (a thread
-//               always holds the same ox and channels), then once per pooled
-//               row the horizontal 3-wide max by warp shuffles (lane 0's
-//               left neighbour comes from the previous quarter through
-//               shared memory), then the activation of the pooled pixel;
-//   warp 16     TMEM allocation, MMA issuer 0;
-//   warp 17     TMA producer: the weights once, then input rows in order;
-//   warp 18     MMA issuer 1 (tiles go round robin over the issuers; four
-//               issuers, one per scheduler, measured slower: 0.185 vs 0.175 ms).
+//               16*(w/4) .. +15, then zeroes them.  Without the pool: bias,
+//               activation, fp16 store of the conv row.  With the pool:
+//               fp16(acc + bias), its vertical max carried in registers from
+//               row to row (a thread always holds the same ox and channels),
+//               then once per pooled row the horizontal 3-wide max by warp
+//               shuffles (lane 0's left neighbour comes from the previous
+//               quarter through shared memory), then the activation of the
+//               pooled pixel;
+//   warp 16     TMEM allocation, MMA issuer;
+//   warp 17     TMA producer: the weights once, then input rows in order.
 // Each CTA owns a contiguous range of output units (pooled rows, or conv
 // rows without the pool) over the whole batch, walked as per-image
 // segments; with the pool a segment also computes the conv row just above
 // its first pooled row (the shared row of two pooled windows).
 //
 // Barrier protocol (all waits bounded): rfull[slot] (TMA bytes), rempty[slot]
-// (count n_iss: each issuer commits once per load after its last MMA reading
-// it; an issuer waits on every load of the sequence in order, so a slot can
-// only be refilled after every issuer has observed its previous load; with
-// kh + n_iss - 1 <= kRowSlots the loads in flight fit the ring), tfull /
-// tempty per TMEM accumulator (8 x 64 columns), wfull for the weights.
+// (committed after the MMAs reading the row), tempty[block] (16 epilogue
+// arrivals: drained and zeroed; the first phase completes after the initial
+// zeroing), tfull[block] (committed after the last MMA of the tile's last
+// input row), wfull for the weights.  The issuer waits for a block only at
+// the first input row of its tile; the tiles sharing an MMA window were all
+// acquired before, and block P(t) is reused by tile t+8 only after tile t
+// was drained and tile t+1 loaded (the release waits one tile), which needs
+// the MMAs of input rows up to t+kh < t+8.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -66,23 +81,20 @@ namespace {
 
 constexpr int kRowSlots = 8;                   // input-row ring
 constexpr int kRowPos = 128;                   // positions (A rows) per tile
+constexpr int kRowBox = 32;                    // positions per TMA box (one TMEM lane quarter)
+constexpr int kRowMaxQPool = (kRowBox - 2) / 2;  // pooled columns per quarter (window centres on odd lanes)
 constexpr int kSlotBytes = kRowPos * 128;      // one input row: 128 rows x 128 B
-constexpr int kRowAcc = 8;                     // TMEM accumulators of 64 columns
-constexpr int kRowMaxKh = kRowSlots - 2;       // a tile's loads plus the next tile's fit the ring
+constexpr int kRowAcc = 8;                     // TMEM accumulator blocks of 64 columns
+constexpr int kRowMaxKh = 6;                   // the MMA window (kh blocks) leaves two blocks for the epilogue
 constexpr int kWBlockBytes = 64 * 128;         // one 64-wide K block of 64 weight rows
 constexpr int kEpiWarps = 16;                  // 4 per TMEM lane quarter, 16 columns each
 constexpr int kEpiCols = 64 / (kEpiWarps / 4);
-// MMA issuers: warp kIssuer0 (which also allocates TMEM) and the three warps
-// after the producer; one thread issues at most one tcgen05.mma per ~80
-// cycles, so tiles go round robin over up to four issuers, one per scheduler
-constexpr int kMaxIssuers = 2;
-constexpr int kIssuer0 = kEpiWarps, kProducer = kEpiWarps + 1;
-constexpr int kThreads = (kEpiWarps + 1 + kMaxIssuers) * 32;
-__device__ __forceinline__ int issuer_of(int warp) {
-  if (warp == kIssuer0) return 0;
-  if (warp > kProducer && warp <= kProducer + kMaxIssuers - 1) return warp - kProducer;
-  return -1;
-}
+constexpr int kIssuer = kEpiWarps, kProducer = kEpiWarps + 1;
+constexpr int kThreads = (kEpiWarps + 2) * 32;
+
+// TMEM block of the CTA's t-th tile (descending, so one input row's MMA
+// window over tiles y .. y-kh+1 is ascending and contiguous up to a wrap)
+__device__ __forceinline__ int acc_block(int t) { return (kRowAcc - 1) - (t & (kRowAcc - 1)); }
 
 struct RowParams {
   const float* bias;
@@ -92,21 +104,19 @@ struct RowParams {
   int PH, PW;        // pooled size (pool == 1)
   int units;         // N * (pool ? PH : OH)
   int w_bytes;       // kh * kWBlockBytes
-  int n_iss;         // MMA issuers in use (tiles lt with lt % n_iss == i go to issuer i)
+  int qpool, qspan;  // pool: pooled columns per lane quarter, conv columns between quarters (2 * qpool)
   uint32_t wait_limit;
 };
 
 // Shared-memory layout (from the 1024-aligned base): weights, input-row ring,
-// barriers, misc words, bias, the epilogue's edge-exchange buffer.
+// barriers, misc words, bias.
 constexpr int kMaxWBytes = kRowMaxKh * kWBlockBytes;
 constexpr int kRingOff = kMaxWBytes;  // weights first (only w_bytes of it used)
 constexpr int kBarOff = kRingOff + kRowSlots * kSlotBytes;
 constexpr int kNumBars = 1 + 2 * kRowSlots + 2 * kRowAcc + 1;
 constexpr int kMiscOff = kBarOff + kNumBars * 8;
 constexpr int kBiasOff = (kMiscOff + 16 + 15) & ~15;
-constexpr int kEdgeOff = kBiasOff + 64 * 4;
-constexpr int kEdgeBytes = 2 * kEpiWarps * kEpiCols * 2;  // [pooled-row parity][warp][16 fp16]
-constexpr int kSmemBytes = kEdgeOff + kEdgeBytes + 1024;
+constexpr int kSmemBytes = kBiasOff + 64 * 4 + 1024;
 static_assert(kSmemBytes <= 232448, "row kernel shared memory above 227 KB");
 
 // One segment of a CTA's units: image n, conv rows lo..hi.
@@ -156,61 +166,86 @@ constexpr uint32_t kNegInf2 = 0xFC00FC00u;  // two fp16 -inf
 // Epilogue warps.  Each thread keeps its 16 bias values in registers.
 // Without the pool: act(acc + bias) -> fp16 store of the conv row.  With the
 // pool: fp16(acc + bias) per conv row, the 3x3 window max on those fp16
-// values (vertical in registers, horizontal by shuffles once per pooled row),
-// then the activation of the pooled value.  Rounding to fp16 and the
+// values (vertical in registers, horizontal by warp shuffles once per pooled
+// row), then the activation of the pooled value.  Rounding to fp16 and the
 // ReLU / identity activations are non-decreasing and ReLU commutes with the
 // rounding, so this equals pooling the conv output the unfused kernels store,
 // bit for bit (a sigmoid activation is applied to the rounded maximum).
+//
+// With the pool each TMEM lane quarter q holds its own overlapping range of
+// conv columns, ox = qspan * q - 1 + lane (the producer lands A rows that
+// way), so all three columns of every window it pools lie in the same warp:
+// odd lanes 1, 3, .., qspan - 1 are the window centres (even ox) of pooled
+// columns qpool * q .. qpool * q + qpool - 1.  Columns outside the conv map
+// (ox = -1 on the left, ox >= OW) are the pool's -inf padding.  No warp
+// waits for another.
+//
+// A drained accumulator block is zeroed with tcgen05.st right after it is
+// read and released (wait::st, arrival on tempty) one tile later, after the
+// next tile's TMEM load: the store completes under this tile's arithmetic.
+// fp32 bias adds use the packed two-lane add (same rounding as two scalar
+// adds).
 template <int ACT>
-__device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint64_t* tfull, uint64_t* tempty,
+__device__ __forceinline__ void epilogue(const RowParams& p, uint64_t* tfull, uint64_t* tempty, const float* s_bias,
                                          volatile int* abort_flag, uint32_t tmem_base, int u0, int u1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3, cg = warp >> 2;
-  const int ox = q * 32 + lane;
-  const bool xvalid = ox < p.OW;
+  const int ox = p.pool ? p.qspan * q - 1 + lane : kRowBox * q + lane;
+  const bool xvalid = ox >= 0 && ox < p.OW;
+  const int px = p.qpool * q + (lane >> 1);  // pooled column centred here (odd lanes)
+  const bool centre = (lane & 1) != 0 && (lane >> 1) < p.qpool && px < p.PW;
   const int c0 = cg * kEpiCols;
   const bool pad = c0 + kEpiCols > p.Cout;  // this warp's columns reach past Cout (warp-uniform)
-  const bool odd_w = (p.OW & 1) != 0;       // the last pooled column has no right neighbour
-  float bias[kEpiCols];
-  {
-    const float* s_bias = reinterpret_cast<const float*>(smem + kBiasOff);
+  float2 bias[kEpiCols / 2];
 #pragma unroll
-    for (int k = 0; k < kEpiCols; ++k) bias[k] = s_bias[c0 + k];
-  }
-  uint32_t* edge = reinterpret_cast<uint32_t*>(smem + kEdgeOff);
+  for (int k = 0; k < kEpiCols / 2; ++k) bias[k] = make_float2(s_bias[c0 + 2 * k], s_bias[c0 + 2 * k + 1]);
   const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
   uint32_t carry[kEpiCols / 2], vmax[kEpiCols / 2];
 #pragma unroll
   for (int k = 0; k < kEpiCols / 2; ++k) carry[k] = vmax[k] = kNegInf2;
-  int lt = 0, prow = 0;
+  // every accumulator block starts at zero (the MMAs always accumulate)
+#pragma unroll 1
+  for (int b = 0; b < kRowAcc; ++b) tmem_st_zero_32x32b_x16(tmem_base + t_lane + b * 64 + c0);
+  tmem_st_wait();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0)
+    for (int b = 0; b < kRowAcc; ++b) mbar_arrive(&tempty[b]);
+  int lt = 0;
+  int pend = -1;  // block whose zeros are in flight, released after the next load
   int u = u0;
   Seg sg;
   while (next_seg(p, u, u1, sg)) {
     bool carry_ok = false;
     for (int oy = sg.lo; oy <= sg.hi; ++oy, ++lt) {
-      const int ab = lt % kRowAcc;
+      const int ab = acc_block(lt);
       bool ok = true;
       if (lane == 0) ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / kRowAcc) & 1, kErrWaitAccum, p.wait_limit);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       tc_fence_after();
       uint32_t r[kEpiCols];
+      const uint32_t ta = tmem_base + t_lane + ab * 64 + c0;
       if (ok) {
-        tmem_ld_32x32b_x16(tmem_base + t_lane + ab * 64 + c0, r);
+        tmem_ld_32x32b_x16(ta, r);
         tmem_ld_wait();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&tempty[ab]);
-        if (!ok) *abort_flag = 1;
+      if (pend >= 0) {  // the previous tile's block: its zeros are written
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[pend]);
       }
+      if (ok) tmem_st_zero_32x32b_x16(ta);  // ready for tile lt + kRowAcc
+      pend = ab;
+      if (lane == 0 && !ok) *abort_flag = 1;
       if (!p.pool) {
         if (ok && xvalid) {
           uint32_t h[kEpiCols / 2];
 #pragma unroll
           for (int k = 0; k < kEpiCols / 2; ++k) {
-            float f0 = act_f<ACT>(__uint_as_float(r[2 * k]) + bias[2 * k]);
-            float f1 = act_f<ACT>(__uint_as_float(r[2 * k + 1]) + bias[2 * k + 1]);
+            const float2 v = __fadd2_rn(make_float2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])), bias[k]);
+            float f0 = act_f<ACT>(v.x);
+            float f1 = act_f<ACT>(v.y);
             if (pad && c0 + 2 * k >= p.Cout) f0 = 0.f;  // pad channels stay zero
             if (pad && c0 + 2 * k + 1 >= p.Cout) f1 = 0.f;
             h[k] = pack2(f0, f1);
@@ -221,90 +256,74 @@ __device__ __forceinline__ void epilogue(const RowParams& p, uint8_t* smem, uint
             if (c0 + 8 * s < p.Cs_out)
               *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(h[4 * s], h[4 * s + 1], h[4 * s + 2], h[4 * s + 3]);
         }
-        continue;
-      }
-      // fp16(acc + bias) of this conv row (garbage when !ok: never stored)
-      uint32_t h[kEpiCols / 2];
-#pragma unroll
-      for (int k = 0; k < kEpiCols / 2; ++k)
-        h[k] = pack2(__uint_as_float(r[2 * k]) + bias[2 * k], __uint_as_float(r[2 * k + 1]) + bias[2 * k + 1]);
-      if (odd_w && !xvalid) {
-#pragma unroll
-        for (int k = 0; k < kEpiCols / 2; ++k) h[k] = kNegInf2;
-      }
-      // vertical max first, in registers (a thread always holds the same ox
-      // and channels): carried row 2py-1, then 2py, then 2py+1
-      bool close = false;  // this row completes a pooled row of the segment
-      if (oy & 1) {
-        if (oy != sg.lo) {  // (else it only carries into the segment's first pooled row)
-#pragma unroll
-          for (int k = 0; k < kEpiCols / 2; ++k) vmax[k] = hmax2_u32(vmax[k], h[k]);
-          close = true;
-        }
-#pragma unroll
-        for (int k = 0; k < kEpiCols / 2; ++k) carry[k] = h[k];
-        carry_ok = true;
       } else {
+        // fp16(acc + bias) of this conv row; -inf outside the map (garbage
+        // when !ok: never stored)
+        uint32_t h[kEpiCols / 2];
 #pragma unroll
-        for (int k = 0; k < kEpiCols / 2; ++k) vmax[k] = carry_ok ? hmax2_u32(carry[k], h[k]) : h[k];
-        close = oy == p.OH - 1;  // an odd-height map's last pooled row has no row below
-      }
-      // `close` depends on oy and the segment only, so every epilogue warp
-      // reaches the barrier below equally often (whatever `ok` is)
-      if (!close) continue;
-      // horizontal 3-wide max at even ox, once per pooled row; lane 0's left
-      // neighbour (ox - 1) is lane 31 of the previous quarter, exchanged
-      // through shared memory (double-buffered by pooled-row parity, so one
-      // barrier per pooled row suffices)
-      uint32_t* eg = edge + ((prow & 1) * kEpiWarps + warp) * (kEpiCols / 2);
-      if (lane == 31) {
-        reinterpret_cast<uint4*>(eg)[0] = make_uint4(vmax[0], vmax[1], vmax[2], vmax[3]);
-        reinterpret_cast<uint4*>(eg)[1] = make_uint4(vmax[4], vmax[5], vmax[6], vmax[7]);
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-      uint32_t left[kEpiCols / 2];
+        for (int k = 0; k < kEpiCols / 2; ++k) {
+          const float2 v = __fadd2_rn(make_float2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])), bias[k]);
+          h[k] = xvalid ? pack2(v.x, v.y) : kNegInf2;
+        }
+        // vertical max first, in registers (a thread always holds the same
+        // ox and channels): carried row 2py-1, then 2py, then 2py+1
+        bool close = false;  // this row completes a pooled row of the segment
+        if (oy & 1) {
+          if (oy != sg.lo) {  // (else it only carries into the segment's first pooled row)
 #pragma unroll
-      for (int k = 0; k < kEpiCols / 2; ++k) left[k] = __shfl_up_sync(0xffffffffu, vmax[k], 1);
-      if (lane == 0) {
-        if (q > 0) {
-          const uint4* ep = reinterpret_cast<const uint4*>(edge + ((prow & 1) * kEpiWarps + warp - 1) * (kEpiCols / 2));
-          const uint4 e0 = ep[0], e1 = ep[1];
-          left[0] = e0.x; left[1] = e0.y; left[2] = e0.z; left[3] = e0.w;
-          left[4] = e1.x; left[5] = e1.y; left[6] = e1.z; left[7] = e1.w;
+            for (int k = 0; k < kEpiCols / 2; ++k) vmax[k] = hmax2_u32(vmax[k], h[k]);
+            close = true;
+          }
+#pragma unroll
+          for (int k = 0; k < kEpiCols / 2; ++k) carry[k] = h[k];
+          carry_ok = true;
         } else {
 #pragma unroll
-          for (int k = 0; k < kEpiCols / 2; ++k) left[k] = kNegInf2;
+          for (int k = 0; k < kEpiCols / 2; ++k) vmax[k] = carry_ok ? hmax2_u32(carry[k], h[k]) : h[k];
+          close = oy == p.OH - 1;  // an odd-height map's last pooled row has no row below
+        }
+        if (close) {
+          // horizontal 3-wide max at the centre lanes (ox - 1, ox, ox + 1 are
+          // lanes l - 1, l, l + 1 of this warp)
+          uint32_t o[kEpiCols / 2];
+#pragma unroll
+          for (int k = 0; k < kEpiCols / 2; ++k)
+            o[k] = hmax2_u32(hmax2_u32(__shfl_up_sync(0xffffffffu, vmax[k], 1), vmax[k]),
+                             __shfl_down_sync(0xffffffffu, vmax[k], 1));
+          if (ok && centre) {
+            if (ACT == 1) {
+#pragma unroll
+              for (int k = 0; k < kEpiCols / 2; ++k) o[k] = hmax2_u32(o[k], 0u);
+            } else if (ACT == 2) {
+#pragma unroll
+              for (int k = 0; k < kEpiCols / 2; ++k) {
+                const float2 f = __half22float2(*reinterpret_cast<__half2*>(&o[k]));
+                o[k] = pack2(act_f<2>(f.x), act_f<2>(f.y));
+              }
+            }
+            if (pad) {
+#pragma unroll
+              for (int k = 0; k < kEpiCols / 2; ++k) {
+                if (c0 + 2 * k >= p.Cout) o[k] &= 0xFFFF0000u;  // pad channels stay zero
+                if (c0 + 2 * k + 1 >= p.Cout) o[k] &= 0x0000FFFFu;
+              }
+            }
+            __half* dst = p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + px) * p.Cs_out + c0;
+#pragma unroll
+            for (int s = 0; s < kEpiCols / 8; ++s)
+              if (c0 + 8 * s < p.Cs_out)
+                *reinterpret_cast<uint4*>(dst + 8 * s) =
+                    make_uint4(o[4 * s], o[4 * s + 1], o[4 * s + 2], o[4 * s + 3]);
+          }
         }
       }
-      ++prow;
-      uint32_t o[kEpiCols / 2];
-#pragma unroll
-      for (int k = 0; k < kEpiCols / 2; ++k)
-        o[k] = hmax2_u32(hmax2_u32(left[k], vmax[k]), __shfl_down_sync(0xffffffffu, vmax[k], 1));
-      if (!(ok && xvalid && (ox & 1) == 0)) continue;
-      if (ACT == 1) {
-#pragma unroll
-        for (int k = 0; k < kEpiCols / 2; ++k) o[k] = hmax2_u32(o[k], 0u);
-      } else if (ACT == 2) {
-#pragma unroll
-        for (int k = 0; k < kEpiCols / 2; ++k) {
-          const float2 f = __half22float2(*reinterpret_cast<__half2*>(&o[k]));
-          o[k] = pack2(act_f<2>(f.x), act_f<2>(f.y));
-        }
-      }
-      if (pad) {
-#pragma unroll
-        for (int k = 0; k < kEpiCols / 2; ++k) {
-          if (c0 + 2 * k >= p.Cout) o[k] &= 0xFFFF0000u;  // pad channels stay zero
-          if (c0 + 2 * k + 1 >= p.Cout) o[k] &= 0x0000FFFFu;
-        }
-      }
-      __half* dst = p.y + ((static_cast<int64_t>(sg.n) * p.PH + (oy >> 1)) * p.PW + (ox >> 1)) * p.Cs_out + c0;
-#pragma unroll
-      for (int s = 0; s < kEpiCols / 8; ++s)
-        if (c0 + 8 * s < p.Cs_out)
-          *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(o[4 * s], o[4 * s + 1], o[4 * s + 2], o[4 * s + 3]);
     }
+  }
+  if (pend >= 0) {
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tempty[pend]);
   }
 }
 
@@ -325,7 +344,8 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kMiscOff + 4);
   float* s_bias = reinterpret_cast<float*>(smem + kBiasOff);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warp index through a shuffle: the compiler then knows it is warp-uniform
+  const int tid = threadIdx.x, warp = __shfl_sync(0xffffffffu, tid >> 5, 0), lane = tid & 31;
   // this CTA's units [u0, u1) (pooled rows or conv rows over the batch)
   const int u0 = static_cast<int>(static_cast<int64_t>(p.units) * blockIdx.x / gridDim.x);
   const int u1 = static_cast<int>(static_cast<int64_t>(p.units) * (blockIdx.x + 1) / gridDim.x);
@@ -334,13 +354,13 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
     mbar_init(wfull, 1);
     for (int s = 0; s < kRowSlots; ++s) {
       mbar_init(&rfull[s], 1);
-      mbar_init(&rempty[s], p.n_iss);
+      mbar_init(&rempty[s], 1);
     }
     for (int b = 0; b < kRowAcc; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kEpiWarps);
     }
-    mbar_init(mma_done, kMaxIssuers);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -349,7 +369,7 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
-  if (warp == kIssuer0) {
+  if (warp == kIssuer) {
     tmem_alloc(tmem_slot, kRowAcc * 64);
     tmem_relinquish();
   }
@@ -360,11 +380,11 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
 
   if (warp < kEpiWarps) {
     if (p.act == 1)
-      epilogue<1>(p, smem, tfull, tempty, abort_flag, tmem_base, u0, u1);
+      epilogue<1>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
     else if (p.act == 0)
-      epilogue<0>(p, smem, tfull, tempty, abort_flag, tmem_base, u0, u1);
+      epilogue<0>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
     else
-      epilogue<2>(p, smem, tfull, tempty, abort_flag, tmem_base, u0, u1);
+      epilogue<2>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
   } else if (warp == kProducer) {
     if (lane == 0) {
       bool ok = true;
@@ -373,6 +393,7 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       uint32_t L = 0;
       int u = u0;
       Seg sg;
+      const int x0 = p.pool ? -1 : 0, qstep = p.pool ? p.qspan : kRowBox;
       while (ok && next_seg(p, u, u1, sg)) {
         for (int yin = sg.lo; yin <= sg.hi + p.kh - 1; ++yin, ++L) {
           const uint32_t slot = L % kRowSlots;
@@ -382,7 +403,11 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
             break;
           }
           mbar_arrive_expect_tx(&rfull[slot], kSlotBytes);
-          tma_load_4d(ring + slot * kSlotBytes, &tmap_x, &rfull[slot], 0, 0, yin, sg.n);
+          // one 32-position box per TMEM lane quarter (pixel -1 and pixels
+          // >= OW read as zeros)
+          for (int qq = 0; qq < kRowPos / kRowBox; ++qq)
+            tma_load_4d(ring + slot * kSlotBytes + qq * (kSlotBytes / 4), &tmap_x, &rfull[slot], 0, x0 + qq * qstep,
+                        yin, sg.n);
         }
       }
       if (!ok) *abort_flag = 1;
@@ -391,81 +416,68 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       for (int64_t j = static_cast<int64_t>(L) - 1; j >= 0 && j >= static_cast<int64_t>(L) - kRowSlots; --j)
         mbar_wait(&rfull[j % kRowSlots], static_cast<uint32_t>(j / kRowSlots) & 1, kErrWaitFull, p.wait_limit);
     }
-  } else if (issuer_of(warp) >= 0) {
-    if (lane == 0 && issuer_of(warp) >= p.n_iss) {
-      umma_commit(mma_done);  // an issuer left idle by a tall kernel (see n_iss)
-      mbar_wait(mma_done, 0, kErrWaitFull, p.wait_limit);
-    } else if (lane == 0) {
-      const int issuer = issuer_of(warp);
-      constexpr uint32_t idesc = make_idesc_f16_m128(64);
-      // no shared-memory loads in this loop (they would wait behind queued
-      // MMAs); waits are relaxed, every one bounded
-      bool ok = mbar_wait_relaxed(wfull, 0, kErrWaitFull, p.wait_limit);
-      uint32_t next_wait = 0, next_rel = 0, Lseg = 0;
-      int lt = 0;
-      int u = u0;
-      Seg sg;
-      const uint64_t b_base = make_sdesc_sw128(smem_u32(sW));
-      while (ok && next_seg(p, u, u1, sg)) {
-        const int ntiles = sg.hi - sg.lo + 1;
-        const uint32_t nloads = static_cast<uint32_t>(ntiles + p.kh - 1);
-        for (int j = 0; j < ntiles && ok; ++j, ++lt) {
-          if (lt % p.n_iss != issuer) continue;
-          const int ab = lt % kRowAcc;
-          if (!mbar_wait_relaxed(&tempty[ab], ((lt / kRowAcc) & 1) ^ 1, kErrWaitAccum, p.wait_limit)) {
-            ok = false;
-            break;
-          }
-          // every load up to the tile's last one, in order (including loads
-          // only the other issuer's tiles read)
-          const uint32_t last = Lseg + static_cast<uint32_t>(j + p.kh - 1);
-          for (; next_wait <= last; ++next_wait) {
-            if (!mbar_wait_relaxed(&rfull[next_wait % kRowSlots], (next_wait / kRowSlots) & 1, kErrWaitFull,
-                                   p.wait_limit)) {
-              ok = false;
-              break;
-            }
-          }
+  } else if (warp == kIssuer) {
+    // The whole warp runs this loop (every value in it is warp-uniform);
+    // one elected lane issues the MMAs and commits.  No shared-memory loads
+    // here (they would wait behind queued MMAs); waits are relaxed, every one
+    // bounded.
+    bool ok = __all_sync(0xffffffffu, mbar_wait_relaxed(wfull, 0, kErrWaitFull, p.wait_limit));
+    uint32_t L = 0;  // input rows consumed (ring position)
+    int lt0 = 0;     // the segment's first tile
+    int u = u0;
+    Seg sg;
+    const uint64_t b_base = make_sdesc_sw128(smem_u32(sW));
+    while (ok && next_seg(p, u, u1, sg)) {
+      const int ntiles = sg.hi - sg.lo + 1;
+      for (int i = 0; i < ntiles + p.kh - 1; ++i, ++L) {
+        // input row sg.lo + i; it feeds tiles lt0 + i - j for kernel rows
+        // j in [j_lo, j_hi] (the tiles of this segment)
+        const int ly = lt0 + i;
+        if (i < ntiles) {  // tile ly's block: drained and zeroed
+          ok = __all_sync(0xffffffffu, mbar_wait_relaxed(&tempty[acc_block(ly)], (ly / kRowAcc) & 1, kErrWaitAccum,
+                                                         p.wait_limit));
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t d_tmem = tmem_base + ab * 64;
-          for (int r = 0; r < p.kh; ++r) {
-            const uint32_t L = Lseg + static_cast<uint32_t>(j + r);
-            const uint64_t a_desc = make_sdesc_sw128(smem_u32(ring + (L % kRowSlots) * kSlotBytes));
-            const uint64_t b_desc = b_base + static_cast<uint32_t>(r * (kWBlockBytes >> 4));
+        }
+        const uint32_t slot = L % kRowSlots;
+        ok = __all_sync(0xffffffffu, mbar_wait_relaxed(&rfull[slot], (L / kRowSlots) & 1, kErrWaitFull, p.wait_limit));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t a_desc = make_sdesc_sw128(smem_u32(ring + slot * kSlotBytes));
+        const int j_hi = min(p.kh - 1, i);
+        const int blk0 = acc_block(ly);
+        for (int j = max(0, i - (ntiles - 1)); j <= j_hi;) {
+          // a run of blocks that neither wraps past block 7 nor exceeds N = 256
+          const int blk = (blk0 + j) & (kRowAcc - 1);
+          const int len = min(min(j_hi - j + 1, kRowAcc - blk), 4);
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(blk * 64);
+          const uint64_t b_desc = b_base + static_cast<uint32_t>(j * (kWBlockBytes >> 4));
+          const uint32_t idesc = make_idesc_f16_m128(static_cast<uint32_t>(len * 64));
+          if (elect_one()) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)  // K step = 32 bytes = 2 start-address units
-              umma_f16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (r | k) != 0 ? 1u : 0u);
+              umma_f16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, 1u);
           }
-          umma_commit(&tfull[ab]);
-          // this issuer's next tile (j + n_iss) reads loads from Lseg + j + n_iss on
-          const uint32_t rel_to = std::min(Lseg + static_cast<uint32_t>(j + p.n_iss - 1), next_wait - 1);
-          for (; next_rel <= rel_to; ++next_rel) umma_commit(&rempty[next_rel % kRowSlots]);
+          __syncwarp();
+          j += len;
         }
-        if (!ok) break;
-        // segment end: observe and release the rest of its loads
-        const uint32_t end = Lseg + nloads - 1;
-        for (; next_wait <= end; ++next_wait) {
-          if (!mbar_wait_relaxed(&rfull[next_wait % kRowSlots], (next_wait / kRowSlots) & 1, kErrWaitFull,
-                                 p.wait_limit)) {
-            ok = false;
-            break;
-          }
+        if (elect_one()) {
+          umma_commit(&rempty[slot]);
+          if (i >= p.kh - 1) umma_commit(&tfull[acc_block(ly - (p.kh - 1))]);  // its last input row
         }
-        if (!ok) break;
-        for (; next_rel <= end; ++next_rel) umma_commit(&rempty[next_rel % kRowSlots]);
-        Lseg += nloads;
+        __syncwarp();
       }
-      if (!ok) *abort_flag = 1;
-      // every MMA of both issuers has completed once mma_done fires
-      umma_commit(mma_done);
-      mbar_wait(mma_done, 0, kErrWaitFull, p.wait_limit);
+      lt0 += ntiles;
     }
+    if (!ok && lane == 0) *abort_flag = 1;
+    // every MMA has completed once mma_done fires
+    if (elect_one()) umma_commit(mma_done);
+    __syncwarp();
+    mbar_wait(mma_done, 0, kErrWaitFull, p.wait_limit);
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kIssuer0) {
+  if (warp == kIssuer) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, kRowAcc * 64);
@@ -475,15 +487,16 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
 // Input rows of the NHWC activation as 64-value runs: element (e, x, y, n)
 // is x[n, y, x + e / Cs_in, e % Cs_in], so dimension 0 (64 contiguous fp16 =
 // kw pixels) overlaps the next pixel's run (stride Cs_in * 2 bytes).  Box
-// {64, 128, 1, 1} = 16 KB, 128B swizzle (inner box = swizzle span); x < OW
-// keeps every run inside its image row and x >= OW reads zeros.
+// {64, 32, 1, 1} = 4 KB (one TMEM lane quarter's A rows), 128B swizzle (inner
+// box = swizzle span); x < OW keeps every run inside its image row, x >= OW
+// and x = -1 read zeros.
 int make_row_map(CUtensorMap* map, const ConvRowArgs& a, int ow) {
   auto enc = encode_tiled();
   if (!enc) return -1;
   const cuuint64_t px = static_cast<cuuint64_t>(a.Cs_in) * 2;
   cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(ow), static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.N)};
   cuuint64_t strides[3] = {px, px * a.W, px * a.W * a.H};
-  cuuint32_t box[4] = {64, kRowPos, 1, 1};
+  cuuint32_t box[4] = {64, kRowBox, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -529,6 +542,10 @@ int conv_row_check(const ConvRowArgs& a, const char** err) {
     *err = "row conv: unknown pool";
     return -2;
   }
+  if (a.pool == 1 && (ow - 1) / 2 + 1 > (kRowPos / kRowBox) * kRowMaxQPool) {
+    *err = "row conv: pooled rows longer than 60 pixels";
+    return -2;
+  }
   if (static_cast<int64_t>(a.N) * (a.H - a.kh + 1) > 0x7FFFFFFF) {
     *err = "row conv: too many rows";
     return -2;
@@ -553,10 +570,9 @@ int conv_row_launch(const ConvRowArgs& a, cudaStream_t stream, const char** err)
   p.PW = (p.OW - 1) / 2 + 1;
   p.units = a.N * (a.pool ? p.PH : p.OH);
   p.w_bytes = a.kh * kWBlockBytes;
+  p.qpool = (p.PW + (kRowPos / kRowBox) - 1) / (kRowPos / kRowBox);
+  p.qspan = 2 * p.qpool;
   p.wait_limit = wait_limit_from_env();
-  // every issuer waits on each load in order, so a tile's kh loads plus the
-  // loads of the other issuers' tiles in flight must fit the ring
-  p.n_iss = std::min(kMaxIssuers, kRowSlots - a.kh + 1);
 
   CUtensorMap mw, mx;
   if (make_weight_map(&mw, a) != 0) {

@@ -124,3 +124,9 @@ def test_conv2d_maxpool_support_query():
     assert L.lotus_conv2d_maxpool_supported(ctypes.byref(ok), ctypes.byref(pool2)) == -2
     wrong_in = Pool2dDesc(256, 64, 111, 112, 3, 3, 2, 2, 1, 1, 0)
     assert L.lotus_conv2d_maxpool_supported(ctypes.byref(ok), ctypes.byref(wrong_in)) == -1
+    # with the pool, conv rows up to 120 pixels (60 pooled columns, 15 per TMEM lane quarter)
+    for ow, want in ((120, 0), (121, -2), (128, -2)):
+        c = Conv2dDesc(2, 12, 40, ow + 3, 64, 4, 4, 1, 1, 0, 0, 1, 0)
+        pl = Pool2dDesc(2, 64, 37, ow, 3, 3, 2, 2, 1, 1, 0)
+        assert L.lotus_conv2d_maxpool_supported(ctypes.byref(c), ctypes.byref(pl)) == want, ow
+        assert L.lotus_conv2d_maxpool_supported(ctypes.byref(c), None) == 0, ow

@@ -396,6 +396,13 @@ ROW_CASES = [
     ("cin32_kw2_sigmoid_pool", 2, 32, 9, 30, 64, (2, 2), 2, True),
     ("cin8_kw8_kh5_conv_only", 2, 8, 16, 40, 24, (5, 8), 1, False),
     ("one_row_per_image_pool", 5, 16, 4, 50, 64, (4, 4), 1, True),  # OH = 1
+    # the tallest kernel: 6-block MMA windows split at block 7 and at N = 256
+    ("cin16_kw4_kh6_conv_only", 3, 16, 14, 70, 32, (6, 4), 1, False),
+    ("cin16_kw4_kh6_pool", 2, 16, 23, 33, 64, (6, 4), 0, True),
+    ("cin16_kw4_kh1_pool", 3, 16, 9, 60, 64, (1, 4), 1, True),
+    # the widest pooled rows: 120 conv columns, 60 pooled, 15 per TMEM lane quarter
+    ("ow120_pool", 2, 12, 10, 123, 64, (4, 4), 1, True),
+    ("ow128_conv_only", 2, 12, 6, 131, 48, (4, 4), 0, False),
 ]
 
 
@@ -419,12 +426,16 @@ def test_conv2d_maxpool_row_kernel(case):
     _no_device_error()
 
 
-def test_conv2d_maxpool_matches_separate_conv_and_pool():
+@pytest.mark.parametrize("batch", [4, 64])
+def test_conv2d_maxpool_matches_separate_conv_and_pool(batch):
     """Fused result equals the library's own conv followed by its max pool,
-    bit for bit (same fp16 rounding of the conv output, max is exact)."""
+    bit for bit (same fp16 rounding of the conv output, max is exact); the
+    row kernel's conv rows alone equal the general conv kernel's.  At batch
+    64 each persistent CTA runs ~48 conv rows, so the input-row ring and the
+    TMEM accumulator ring wrap several times."""
     K = _k()
     rng = _rng(11)
-    x = rng.uniform(-1, 1, (4, 12, 115, 115)).astype(np.float32)
+    x = rng.uniform(-1, 1, (batch, 12, 115, 115)).astype(np.float32)
     wt = rng.normal(0, np.sqrt(2.0 / 192), (64, 12, 4, 4)).astype(np.float32)
     b = rng.uniform(-0.1, 0.1, 64).astype(np.float32)
     xg = K.to_nhwc(_gpu(x))
@@ -433,6 +444,8 @@ def test_conv2d_maxpool_matches_separate_conv_and_pool():
     conv = K.conv2d(xg, 12, wp, _gpu(b), 64, 4, 1, 0, 1)
     sep = K.maxpool2d(conv, 64, 3, 2, 1)
     assert torch.equal(fused, sep)
+    rows = K.conv2d_maxpool(xg, 12, wp, _gpu(b), 64, 4, 1, pool=False)
+    assert torch.equal(rows, conv)
     _no_device_error()
 
 
