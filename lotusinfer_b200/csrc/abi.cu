@@ -11,6 +11,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include <cuda_runtime.h>
@@ -141,6 +142,22 @@ static ConvTcArgs conv_args(const void* x, const void* w_packed, const float* bi
   return a;
 }
 
+// The row-stacked kernel takes 64-channel stride-1 layers (ResNet stage 1)
+// when the batch gives every SM at least two output rows of work; smaller
+// launches go to the general kernel, which can split K.  LOTUS_CONV_ROWS=0
+// or 1 forces the choice (tests); a forced general-kernel staging mode
+// (LOTUS_CONV_AMODE) implies 0.
+static bool use_rows_conv(const ConvTcArgs& a, int n) {
+  const char* err = "";
+  if (conv_rows_check(a, n, &err) != 0) return false;
+  const char* env = std::getenv("LOTUS_CONV_ROWS");
+  if (env != nullptr && env[0] == '0') return false;
+  if (env == nullptr && std::getenv("LOTUS_CONV_AMODE") != nullptr) return false;  // a forced general-kernel path
+  if (env != nullptr && env[0] == '1') return true;
+  const int ipt = a.OW + a.kw - 1 <= 64 ? 2 : 1;
+  return static_cast<long>((n + ipt - 1) / ipt) * a.OH >= 2L * num_sms();
+}
+
 static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                          const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream,
                          int y_stride = 0) {
@@ -163,6 +180,11 @@ static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias,
   a.ws_bytes = workspace ? workspace_bytes : 0;
   a.y_stride = y_stride;
   const char* err = "";
+  if (use_rows_conv(a, d->n)) {
+    const int rr = conv_rows_launch(a, d->n, stream, &err);
+    if (rr != 0) return fail(rr == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
+    return ok();
+  }
   const int r = conv_tc_launch(a, stream, &err);
   if (r != 0) return fail(r == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
   return ok();

@@ -34,7 +34,7 @@
 // products are summed in kernel-row order, then K order, as a plain
 // kernel-row loop would.
 //
-// Roles (576 threads):
+// Roles (608 threads):
 //   warps 0-15  epilogue: warp w drains TMEM lane quarter w%4, columns
 //               16*(w/4) .. +15, then zeroes them.  Without the pool: bias,
 //               activation, fp16 store of the conv row.  With the pool:
@@ -44,8 +44,12 @@
 //               shuffles (lane 0's left neighbour comes from the previous
 //               quarter through shared memory), then the activation of the
 //               pooled pixel;
-//   warp 16     TMEM allocation, MMA issuer;
-//   warp 17     TMA producer: the weights once, then input rows in order.
+//   warp 16     TMEM allocation, MMA issuer (it waits on no mbarrier);
+//   warp 17     TMA producer: the weights once, then input rows in order;
+//   warp 18     the gate: the MMAs' mbarrier waits (tile block drained and
+//               zeroed, input row landed), one named-barrier hand-off to the
+//               issuer per input row (an mbarrier wait in the issuing warp is
+//               held behind its queued MMAs).
 // Each CTA owns a contiguous range of output units (pooled rows, or conv
 // rows without the pool) over the whole batch, walked as per-image
 // segments; with the pool a segment also computes the conv row just above
@@ -55,7 +59,7 @@
 // (committed after the MMAs reading the row), tempty[block] (16 epilogue
 // arrivals: drained and zeroed; the first phase completes after the initial
 // zeroing), tfull[block] (committed after the last MMA of the tile's last
-// input row), wfull for the weights.  The issuer waits for a block only at
+// input row), wfull for the weights.  The gate waits for a block only at
 // the first input row of its tile; the tiles sharing an MMA window were all
 // acquired before, and block P(t) is reused by tile t+8 only after tile t
 // was drained and tile t+1 loaded (the release waits one tile), which needs
@@ -89,8 +93,9 @@ constexpr int kRowMaxKh = 6;                   // the MMA window (kh blocks) lea
 constexpr int kWBlockBytes = 64 * 128;         // one 64-wide K block of 64 weight rows
 constexpr int kEpiWarps = 16;                  // 4 per TMEM lane quarter, 16 columns each
 constexpr int kEpiCols = 64 / (kEpiWarps / 4);
-constexpr int kIssuer = kEpiWarps, kProducer = kEpiWarps + 1;
-constexpr int kThreads = (kEpiWarps + 2) * 32;
+constexpr int kIssuer = kEpiWarps, kProducer = kEpiWarps + 1, kGate = kEpiWarps + 2;
+constexpr int kThreads = (kEpiWarps + 3) * 32;
+constexpr uint32_t kRowBar = 1;  // named barrier of the gate / issuer hand-off (0 is __syncthreads)
 
 // TMEM block of the CTA's t-th tile (descending, so one input row's MMA
 // window over tiles y .. y-kh+1 is ascending and contiguous up to a wrap)
@@ -416,32 +421,54 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       for (int64_t j = static_cast<int64_t>(L) - 1; j >= 0 && j >= static_cast<int64_t>(L) - kRowSlots; --j)
         mbar_wait(&rfull[j % kRowSlots], static_cast<uint32_t>(j / kRowSlots) & 1, kErrWaitFull, p.wait_limit);
     }
+  } else if (warp == kGate) {
+    // Does every mbarrier wait the MMAs need and hands each input row to the
+    // issuer through a named barrier (an mbarrier wait in the issuing warp
+    // would be held behind its queued MMAs): the tile the row starts is
+    // drained and zeroed, the row's slot is full.  One hand-off per input
+    // row, also after an error (then with ok = false), so the two warps
+    // always meet the same number of times.
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait(wfull, 0, kErrWaitFull, p.wait_limit);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    uint32_t L = 0;
+    int lt0 = 0;
+    int u = u0;
+    Seg sg;
+    while (next_seg(p, u, u1, sg)) {
+      const int ntiles = sg.hi - sg.lo + 1;
+      for (int i = 0; i < ntiles + p.kh - 1; ++i, ++L) {
+        const int ly = lt0 + i;
+        if (lane == 0 && ok) {
+          if (i < ntiles) ok = mbar_wait(&tempty[acc_block(ly)], (ly / kRowAcc) & 1, kErrWaitAccum, p.wait_limit);
+          if (ok) ok = mbar_wait(&rfull[L % kRowSlots], (L / kRowSlots) & 1, kErrWaitFull, p.wait_limit);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok && lane == 0) *abort_flag = 1;
+        bar_red_and(kRowBar, 64, ok);
+      }
+      lt0 += ntiles;
+    }
   } else if (warp == kIssuer) {
-    // The whole warp runs this loop (every value in it is warp-uniform);
-    // one elected lane issues the MMAs and commits.  No shared-memory loads
-    // here (they would wait behind queued MMAs); waits are relaxed, every one
-    // bounded.
-    bool ok = __all_sync(0xffffffffu, mbar_wait_relaxed(wfull, 0, kErrWaitFull, p.wait_limit));
+    // The whole warp runs this loop (every value in it is warp-uniform); one
+    // elected lane issues the MMAs and commits.  It waits on nothing but the
+    // gate's per-row hand-off.
+    bool ok = true;
     uint32_t L = 0;  // input rows consumed (ring position)
     int lt0 = 0;     // the segment's first tile
     int u = u0;
     Seg sg;
     const uint64_t b_base = make_sdesc_sw128(smem_u32(sW));
-    while (ok && next_seg(p, u, u1, sg)) {
+    while (next_seg(p, u, u1, sg)) {
       const int ntiles = sg.hi - sg.lo + 1;
       for (int i = 0; i < ntiles + p.kh - 1; ++i, ++L) {
         // input row sg.lo + i; it feeds tiles lt0 + i - j for kernel rows
         // j in [j_lo, j_hi] (the tiles of this segment)
-        const int ly = lt0 + i;
-        if (i < ntiles) {  // tile ly's block: drained and zeroed
-          ok = __all_sync(0xffffffffu, mbar_wait_relaxed(&tempty[acc_block(ly)], (ly / kRowAcc) & 1, kErrWaitAccum,
-                                                         p.wait_limit));
-          if (!ok) break;
-        }
-        const uint32_t slot = L % kRowSlots;
-        ok = __all_sync(0xffffffffu, mbar_wait_relaxed(&rfull[slot], (L / kRowSlots) & 1, kErrWaitFull, p.wait_limit));
-        if (!ok) break;
+        ok = bar_red_and(kRowBar, 64, true) && ok;
+        if (!ok) continue;
         tc_fence_after();
+        const int ly = lt0 + i;
+        const uint32_t slot = L % kRowSlots;
         const uint64_t a_desc = make_sdesc_sw128(smem_u32(ring + slot * kSlotBytes));
         const int j_hi = min(p.kh - 1, i);
         const int blk0 = acc_block(ly);
@@ -468,7 +495,6 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       }
       lt0 += ntiles;
     }
-    if (!ok && lane == 0) *abort_flag = 1;
     // every MMA has completed once mma_done fires
     if (elect_one()) umma_commit(mma_done);
     __syncwarp();

@@ -1672,7 +1672,8 @@ int read_device_error() {
   // one and clear them all
   const int a = read_own_device_error();
   const int b = conv_row_read_device_error();
-  return a != 0 ? a : b;
+  const int c = conv_rows_read_device_error();
+  return a != 0 ? a : b != 0 ? b : c;
 }
 
 }  // namespace lotus_impl

@@ -76,6 +76,15 @@ int conv_row_check(const ConvRowArgs& a, const char** err);
 int conv_row_launch(const ConvRowArgs& a, cudaStream_t stream, const char** err);
 int conv_row_read_device_error();
 
+// conv_rows.cu: the row-stacked conv for stride-1 convs over 64-channel
+// pixels (kernels up to 3x3, padding below the kernel size, <= 64 output
+// channels, output rows <= 128 pixels, dense NHWC fp16 output, optional
+// residual): ResNet stage 1.  `n` is the batch.  check: 0 when it takes the
+// shape, else -2 with the reason in *err.
+int conv_rows_check(const ConvTcArgs& a, int n, const char** err);
+int conv_rows_launch(const ConvTcArgs& a, int n, cudaStream_t stream, const char** err);
+int conv_rows_read_device_error();
+
 // pack.cu
 cudaError_t launch_conv_prepack(const float* w, void* wp, int cout, int cin, int kh, int kw, int cs_in, int k_pad,
                                 cudaStream_t s);

@@ -129,6 +129,24 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// Named-barrier AND-reduction over `count` threads (whole warps, converged):
+// every participant blocks until all have arrived and gets the AND of their
+// `v`.  A named barrier is not a shared-memory operation, so a thread with
+// tcgen05.mma instructions in flight passes it without waiting for them
+// (an mbarrier wait from that thread is held behind them).
+__device__ __forceinline__ bool bar_red_and(uint32_t id, uint32_t count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------- cp.async
 // 16-byte global->shared copy; `src_bytes` = 0 writes 16 zero bytes.
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {

@@ -153,6 +153,68 @@ def test_conv2d_halo_many_tiles_per_cta(case, monkeypatch):
     _no_device_error()
 
 
+ROWS_CASES = [
+    # id, n, c, h, w, cout, (kh, kw), (ph, pw), act, residual: 64-channel
+    # stride-1 layers on the row-stacked kernel (forced with LOTUS_CONV_ROWS=1)
+    ("rows_stage1_like_residual_odd_batch", 3, 64, 12, 12, 64, (3, 3), (1, 1), 1, True),
+    ("rows_cout40_sigmoid", 2, 64, 9, 20, 40, (3, 3), (1, 1), 2, False),
+    ("rows_1x1", 4, 64, 7, 7, 64, (1, 1), (0, 0), 0, False),
+    ("rows_2x2_pad1", 2, 64, 6, 10, 64, (2, 2), (1, 1), 1, False),
+    ("rows_pad0_one_image_a_tile_residual", 2, 64, 8, 102, 64, (3, 3), (0, 0), 1, True),  # OW = 100
+    ("rows_cin60_pad_channels", 2, 60, 10, 10, 64, (3, 3), (1, 1), 1, False),
+    ("rows_1x3_pad0x1", 3, 64, 5, 17, 24, (1, 3), (0, 1), 0, False),
+    ("rows_3x2_pad2x0", 2, 64, 9, 9, 64, (3, 2), (2, 0), 1, True),
+    # OW + kw - 1 = 64: the widest rows two images share; 65: one image a tile
+    ("rows_ow62_two_images", 3, 64, 5, 62, 64, (3, 3), (1, 1), 0, False),
+    ("rows_ow63_one_image", 3, 64, 5, 63, 64, (3, 3), (1, 1), 0, False),
+]
+
+
+@pytest.mark.parametrize("case", ROWS_CASES, ids=[c[0] for c in ROWS_CASES])
+def test_conv2d_rows_kernel_parity(case, monkeypatch):
+    monkeypatch.setenv("LOTUS_CONV_ROWS", "1")
+    K = _k()
+    _, n, c, h, w, cout, (kh, kw), (ph, pw), act, with_res = case
+    rng = _rng(zlib.crc32(case[0].encode()))
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / (c * kh * kw)), (cout, c, kh, kw)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, cout).astype(np.float32)
+    oh, ow = h + 2 * ph - kh + 1, w + 2 * pw - kw + 1
+    res = rng.normal(0, 1, (n, cout, oh, ow)).astype(np.float32) if with_res else None
+    want = oracle.conv2d(x, wt, b, (1, 1), (ph, pw), act, residual=res)
+    xg = K.to_nhwc(_gpu(x))
+    wp = K.conv2d_prepack(_gpu(wt), c)
+    rg = K.to_nhwc(_gpu(res)) if with_res else None
+    y = K.conv2d(xg, c, wp, _gpu(b), cout, (kh, kw), 1, (ph, pw), act, residual=rg)
+    assert_close(K.from_nhwc(y, cout).cpu().numpy(), want, what=case[0])
+    if y.shape[-1] != cout:
+        assert torch.count_nonzero(y[..., cout:]).item() == 0
+    _no_device_error()
+
+
+@pytest.mark.parametrize("with_res", [False, True], ids=["plain", "residual"])
+def test_conv2d_rows_kernel_matches_general_kernel(with_res, monkeypatch):
+    """ResNet-18 stage 1 at batch 256 (48 output rows per persistent CTA, so
+    the A-tile ring and the TMEM ring wrap many times): the row-stacked
+    kernel sums each pixel's taps in the general kernel's order, so the
+    outputs are equal bit for bit."""
+    K = _k()
+    g = torch.Generator(device=DEV).manual_seed(5 + with_res)
+    n, c, h, w = 256, 64, 56, 56
+    x = K.to_nhwc(torch.rand((n, c, h, w), device=DEV, generator=g) * 2 - 1)
+    wt = torch.randn((64, c, 3, 3), device=DEV, generator=g) * (2.0 / (c * 9)) ** 0.5
+    b = torch.rand(64, device=DEV, generator=g) * 0.2 - 0.1
+    res = K.to_nhwc(torch.randn((n, 64, h, w), device=DEV, generator=g)) if with_res else None
+    wp = K.conv2d_prepack(wt, c)
+    monkeypatch.setenv("LOTUS_CONV_ROWS", "1")
+    y_rows = K.conv2d(x, c, wp, b, 64, 3, 1, 1, 1, residual=res)
+    monkeypatch.setenv("LOTUS_CONV_ROWS", "0")
+    y_gen = K.conv2d(x, c, wp, b, 64, 3, 1, 1, 1, residual=res)
+    torch.cuda.synchronize()
+    assert torch.equal(y_rows, y_gen)
+    _no_device_error()
+
+
 SPLITK_CASES = [
     # id, n, c, h, w, cout, k, stride, pad, act, residual: output grids too
     # small to fill the GPU, so the K loop splits over CTAs
