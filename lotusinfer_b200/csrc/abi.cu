@@ -158,6 +158,27 @@ static bool use_rows_conv(const ConvTcArgs& a, int n) {
   return static_cast<long>((n + ipt - 1) / ipt) * a.OH >= 2L * num_sms();
 }
 
+// The CTA-pair kernel takes NHWC fp16 convs over 64-channel multiples with
+// at least 256 output channels (256-column pair tiles) when the launch fills
+// every SM pair at least once.  With 128-column tiles the A and B bytes per
+// unit of math outrun the load pipeline (measured slower than the general
+// kernel on ResNet stage 2), so narrower layers and smaller launches go to
+// the general kernel, which can also split K.  LOTUS_CONV_PAIR=0 or 1
+// forces the choice (1: 256 columns when Cout > 128, else 128); a forced
+// general-kernel staging mode (LOTUS_CONV_AMODE) implies 0.
+static int pair_conv_bn(const ConvTcArgs& a) {
+  const char* env = std::getenv("LOTUS_CONV_PAIR");
+  if (env != nullptr && env[0] == '0') return 0;
+  if (env == nullptr && std::getenv("LOTUS_CONV_AMODE") != nullptr) return 0;
+  const char* err = "";
+  if (conv_pair_check(a, 128, &err) != 0 || a.n_cols < 128) return 0;
+  if (env != nullptr && env[0] == '1') return a.n_cols > 128 ? 256 : 128;
+  if (a.n_cols < 256) return 0;
+  const long pairs = num_sms() / 2;
+  const long m_pairs = ((a.M + 127) / 128 + 1) / 2;
+  return m_pairs * ((a.n_cols + 255) / 256) >= pairs ? 256 : 0;
+}
+
 static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                          const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream,
                          int y_stride = 0) {
@@ -182,6 +203,11 @@ static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias,
   const char* err = "";
   if (use_rows_conv(a, d->n)) {
     const int rr = conv_rows_launch(a, d->n, stream, &err);
+    if (rr != 0) return fail(rr == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
+    return ok();
+  }
+  if (const int bn = pair_conv_bn(a)) {
+    const int rr = conv_pair_launch(a, bn, stream, &err);
     if (rr != 0) return fail(rr == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
     return ok();
   }

@@ -1,0 +1,650 @@
+// Implicit-GEMM convolution on CTA pairs (tcgen05 cta_group::2) for convs
+// over NHWC inputs whose channel count is a multiple of 64 (ResNet stages
+// 2-4: 3x3 stride 1 and 2, 1x1 stride 2), with the fused bias, residual and
+// activation epilogue and an NHWC fp16 output.
+//
+// Reference counterpart: source/operator/conv2d.cu:17-187 launched per
+// sample from source/layer/layer_conv2d.cu:43-70, the residual from the
+// Expression add + ReLU layer (source/layer/expression.cu:29-50).
+//
+// Why pairs.  A single-CTA tcgen05.mma (M = 128) reads its B operand (N rows
+// of 32 bytes per K = 16 step) from shared memory at ~60 bytes a cycle,
+// which keeps an N = 256 MMA at ~70% of the tensor rate and N = 128 at
+// ~55%.  An M = 256 MMA issued for a CTA pair computes two 128-row halves,
+// one per SM, and each SM supplies only half of B: per SM the A bytes stay
+// the same and the B bytes halve, while the math per SM is unchanged.
+//
+// GEMM view: M = N*OH*OW output pixels, N_gemm = Cout, K = kh*kw*Cs_in in
+// (tap, channel) order, A rows by im2col TMA, B = the prepacked K-major
+// weights.  A pair tile is 256 M rows x BN columns: CTA rank r holds M rows
+// 128r .. 128r+127 of it (its own A half, its own accumulator: 128 TMEM
+// lanes x BN columns) and weight rows (output channels) BN/2*r .. +BN/2-1
+// of the B operand.
+//
+// Roles (352 threads, both CTAs unless noted):
+//   warps 0-7  epilogue: warp w drains TMEM lane quarter w % 4, column half
+//              w / 4, in 32-column chunks: bias, residual, activation, fp16,
+//              staged through shared memory into coalesced row stores; then
+//              one arrival on the even CTA's tempty barrier;
+//   warp 8     TMEM allocation (cta_group::2, both CTAs); in the even CTA
+//              the MMA issuer: one M=256 MMA per K = 16 step, commits to the
+//              barriers of both CTAs;
+//   warp 9     TMA producer: this CTA's A half and B half of each stage, the
+//              bytes counted on the even CTA's full barrier;
+//   warp 10    (even CTA) the gate: waits on the even CTA's full and tempty
+//              barriers and hands each 64-wide K block to the issuer through
+//              named barriers (an mbarrier wait issued by the MMA-issuing
+//              thread is held behind its queued MMAs; a named barrier is
+//              not).  The hand-offs rotate over S + 1 barriers: the gate's
+//              wait for K block h needs stage h mod S emptied by the MMAs of
+//              block h - S, so the gate is never more than S blocks ahead and
+//              never arrives twice on one barrier before the issuer took it.
+//              After a failed wait the gate switches to bar.sync (lockstep)
+//              and keeps handing off, so the issuer never waits forever.
+// Every mbarrier wait is bounded.  Both CTAs meet at a cluster barrier after
+// set-up and before teardown (a CTA must not exit while its peer's MMAs read
+// its shared memory or its TMA signals the peer's barriers).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstdlib>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace lotus_impl {
+
+using namespace lotus_dev;
+
+namespace {
+
+constexpr int kBlockM = 128;                    // M rows per CTA
+constexpr int kBlockK = 64;                     // fp16 = one 128-byte swizzle row
+constexpr int kABytes = kBlockM * kBlockK * 2;  // 16 KB
+constexpr int kEpiWarps = 8;
+constexpr int kMmaWarp = 8, kTmaWarp = 9, kGateWarp = 10;
+constexpr int kThreads = 11 * 32;
+constexpr int kStgBytes = 32 * 64;              // per epilogue warp: 32 rows x 32 fp16
+constexpr int kBiasMax = 1024;
+constexpr int kHeadBytes = 1024;                // barriers and misc words
+constexpr int kSmemLimit = 232448;
+
+template <int BN>
+struct PairCfg {
+  static constexpr int kBHalf = BN / 2;                    // weight rows per CTA
+  static constexpr int kBBytes = kBHalf * kBlockK * 2;     // 8 or 16 KB
+  static constexpr int kStage = kABytes + kBBytes;
+  static constexpr int kFixed = 1024 + kHeadBytes + kBiasMax * 4 + kEpiWarps * kStgBytes;
+  static constexpr int kStages = std::min(8, (kSmemLimit - kFixed) / kStage);
+  static constexpr int kQueue = kStages + 1;               // named barriers 1 .. kQueue
+  static constexpr int kAcc = 512 / BN;                    // TMEM accumulators
+  static constexpr int kSmemBytes = kFixed + kStages * kStage;
+  static_assert(kQueue <= 15, "named barriers");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory");
+};
+
+struct PairParams {
+  const float* bias;
+  const __half* residual;  // NHWC like y or null
+  __half* y;
+  int M, Cout, Cs_out, y_stride, act;
+  int H, W, OH, OW, sh, sw, ph, pw, kh, kw, Cs_in;
+  int KB;           // 64-wide K blocks
+  int n_tiles;      // BN-column tiles
+  int m_tiles;      // 128-row M tiles
+  int pair_tiles;   // ceil(m_tiles / 2) * n_tiles
+  uint32_t wait_limit;
+};
+
+// ------------------------------------------------------------ cluster PTX
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t map_to(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kWaitSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int err_code, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+  atomicExch(&g_lotus_device_error, err_code);
+  return false;
+}
+__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ------------------------------------------------------------ pair tcgen05 / TMA
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[256 x N] (+)= A[256 x K] * B[N x K]^T over the pair: A rows 0-127 and B
+// rows 0..N/2-1 from the even CTA's shared memory, the rest from the odd
+// CTA's at the same offsets; D rows 0-127 in the even CTA's TMEM, 128-255 in
+// the odd CTA's.
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// One arrival on the barrier at shared::cluster address `bar` once every
+// pair MMA this thread issued so far is complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+// This CTA's half of a pair operand: the box lands in this CTA's shared
+// memory, the bytes are counted on the even CTA's barrier `bar` (a
+// shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_im2col_4d_pair(void* dst, const void* tmap, uint32_t bar, int c, int w,
+                                                        int h, int n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.im2col.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
+// Instruction descriptor, kind::f16, A = B = F16, D = F32, K-major, M = 256.
+__host__ __device__ constexpr uint32_t idesc_pair(uint32_t n) {
+  return (1u << 4) | ((n >> 3) << 17) | ((256u >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <int ACT>
+__device__ __forceinline__ float act_p(float v) {
+  if (ACT == 1) return fmaxf(v, 0.0f);
+  if (ACT == 2) return 1.0f / (1.0f + expf(-v));
+  return v;
+}
+
+// One 32-column chunk of this lane's accumulator row: (acc + bias) +
+// residual in fp32 (the general conv kernel's order), activation, fp16, pad
+// channels zero.  The chunk is staged in the warp's 32 x 64-byte buffer
+// (16-byte pieces XOR-swizzled by row) and stored as 8 rows x 64 contiguous
+// bytes per instruction.  Warp-collective.
+template <int ACT>
+__device__ __forceinline__ void store_chunk(const PairParams& p, const uint32_t (&v)[32], int em, bool valid,
+                                            int col0, const float* s_bias, uint8_t* stg, int lane) {
+  uint4* st = reinterpret_cast<uint4*>(stg);
+  const bool full = col0 + 32 <= p.Cout;
+  uint4 res[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    res[g] = make_uint4(0, 0, 0, 0);
+    if (p.residual != nullptr && valid && col0 + 8 * g < p.Cs_out)
+      res[g] = __ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out + col0 + 8 * g));
+  }
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int c = col0 + 8 * g;
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = s_bias[c + j] + __uint_as_float(v[8 * g + j]);
+    if (p.residual != nullptr) {
+      const __half2* rh = reinterpret_cast<const __half2*>(&res[g]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 rf = __half22float2(rh[j]);
+        f[2 * j] += rf.x;
+        f[2 * j + 1] += rf.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = act_p<ACT>(f[j]);
+    if (!full) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c + j >= p.Cout) f[j] = 0.f;  // pad channels stay zero
+    }
+    st[lane * 4 + ((g ^ (lane >> 1)) & 3)] =
+        make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]), pack_h2(f[6], f[7]));
+  }
+  __syncwarp();
+  const int row_em = valid ? em : -1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = 8 * i + (lane >> 2);  // staged row this lane stores
+    const int c = lane & 3;             // and its 16-byte piece
+    const int em_r = __shfl_sync(0xffffffffu, row_em, r);
+    const uint4 val = st[r * 4 + ((c ^ (r >> 1)) & 3)];
+    const int col = col0 + c * 8;
+    if (em_r >= 0 && col < p.Cs_out)
+      *reinterpret_cast<uint4*>(p.y + static_cast<int64_t>(em_r) * p.y_stride + col) = val;
+  }
+  __syncwarp();  // the buffer is rewritten by the next chunk
+}
+
+// Epilogue warps of both CTAs: this CTA's 128 rows of each pair tile.
+template <int BN, int ACT>
+__device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, uint64_t* tempty, const float* s_bias,
+                                         uint8_t* stg, uint32_t tmem_base, uint32_t rank, volatile int* abort_flag) {
+  using C = PairCfg<BN>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, half = warp >> 2;
+  const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+  const int pair0 = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  int lt = 0;
+  for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
+    const int mp = T / p.n_tiles, nt = T - mp * p.n_tiles;
+    const int em = ((2 * mp + static_cast<int>(rank)) * kBlockM) + q * 32 + lane;
+    const bool valid = em < p.M;
+    const int n0 = nt * BN;
+    const int ab = lt % C::kAcc;
+    bool ok = true;
+    if (lane == 0) ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAcc) & 1, kErrWaitAccum, p.wait_limit);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    tc_fence_after();
+#pragma unroll 1
+    for (int c = 0; c < C::kBHalf / 32; ++c) {
+      const int col = half * C::kBHalf + c * 32;  // column inside the tile
+      if (!ok || n0 + col >= p.Cs_out) continue;  // warp-uniform
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem_base + t_lane + static_cast<uint32_t>(ab * BN + col), v);
+      tmem_ld_wait();
+      store_chunk<ACT>(p, v, em, valid, n0 + col, s_bias, stg, lane);
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      // the accumulator ring lives on the even CTA's barriers
+      if (rank == 0)
+        mbar_arrive(&tempty[ab]);
+      else
+        mbar_arrive_remote(map_to(&tempty[ab], 0));
+      if (!ok) *abort_flag = 1;
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                 const PairParams p) {
+  using C = PairCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kStages] even CTA: both halves of a stage landed
+  uint64_t* empty = full + C::kStages;                 // [kStages] this CTA's stage consumed
+  uint64_t* tfull = empty + C::kStages;                // [kAcc] this CTA's accumulator complete
+  uint64_t* tempty = tfull + C::kAcc;                  // [kAcc] even CTA: drained by both epilogues
+  uint64_t* mma_done = tempty + C::kAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 960);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 964);
+  float* s_bias = reinterpret_cast<float*>(smem + kHeadBytes);
+  uint8_t* s_stg = smem + kHeadBytes + kBiasMax * 4;
+  uint8_t* stages = s_stg + kEpiWarps * kStgBytes;  // 1024-aligned: 1024 + 4096 + 16384
+  auto sA = [&](int st) { return stages + st * C::kStage; };
+  auto sB = [&](int st) { return stages + st * C::kStage + kABytes; };
+
+  const int tid = threadIdx.x;
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0), lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair0 = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+
+  if (tid == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);  // the even CTA's producer arrival + both CTAs' bytes
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < C::kAcc; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kEpiWarps);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  for (int i = tid; i < kBiasMax; i += kThreads) s_bias[i] = (p.bias != nullptr && i < p.Cout) ? __ldg(p.bias + i) : 0.f;
+  if (warp == kTmaWarp && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_a);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(tmem_slot, C::kAcc * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival or commit
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < kEpiWarps) {
+    uint8_t* stg = s_stg + warp * kStgBytes;
+    if (p.act == 1)
+      epilogue<BN, 1>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+    else if (p.act == 0)
+      epilogue<BN, 0>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+    else
+      epilogue<BN, 2>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+  } else if (warp == kTmaWarp) {
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t it = 0;
+      const int ohw = p.OH * p.OW, cpt = p.Cs_in / kBlockK;
+      for (int T = pair0; T < p.pair_tiles && ok; T += npairs) {
+        const int mp = T / p.n_tiles, nt = T - mp * p.n_tiles;
+        // an odd M-tile count leaves the last pair's odd half without rows:
+        // it loads a real tile (its results are never stored)
+        const int mt = min(2 * mp + static_cast<int>(rank), p.m_tiles - 1);
+        const int m0 = mt * kBlockM;
+        const int nimg = m0 / ohw, rem = m0 - nimg * ohw;
+        const int oh = rem / p.OW, ow = rem - oh * p.OW;
+        const int wst = ow * p.sw - p.pw, hst = oh * p.sh - p.ph;
+        const int brow = nt * BN + static_cast<int>(rank) * C::kBHalf;
+        int c0 = 0, s = 0, r = 0;
+        for (int kb = 0; kb < p.KB; ++kb, ++it) {
+          const int st = static_cast<int>(it % C::kStages);
+          if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kStages) & 1) ^ 1, kErrWaitEmpty, p.wait_limit)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[st], 2u * C::kStage);
+          const uint32_t fb = map_to(&full[st], 0);
+          tma_load_2d_pair(sB(st), &tmap_w, fb, kb * kBlockK, brow);
+          tma_load_im2col_4d_pair(sA(st), &tmap_a, fb, c0, wst, hst, nimg, static_cast<uint16_t>(s),
+                                  static_cast<uint16_t>(r));
+          c0 += kBlockK;
+          if (c0 == p.Cs_in) {
+            c0 = 0;
+            if (++s == p.kw) {
+              s = 0;
+              ++r;
+            }
+          }
+        }
+        (void)cpt;
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == kGateWarp) {
+    if (rank == 0) {
+      bool ok = true;
+      uint32_t it = 0, h = 0;
+      int lt = 0;
+      for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
+        const int ab = lt % C::kAcc;
+        for (int kb = 0; kb < p.KB; ++kb, ++it, ++h) {
+          const int st = static_cast<int>(it % C::kStages);
+          if (lane == 0 && ok) {
+            if (kb == 0)
+              ok = mbar_wait_cluster(&tempty[ab], ((lt / C::kAcc) & 1) ^ 1, kErrWaitAccum, p.wait_limit);
+            if (ok) ok = mbar_wait(&full[st], (it / C::kStages) & 1, kErrWaitFull, p.wait_limit);
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          const uint32_t id = 1u + h % C::kQueue;
+          if (ok) {
+            named_arrive(id, 64);
+          } else {
+            if (lane == 0) *abort_flag = 1;
+            named_sync(id, 64);  // lockstep from here on: never two arrivals ahead
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (rank == 0) {
+      // The whole warp runs this loop (warp-uniform values); one elected lane
+      // issues and commits.  It waits only on the gate's named barriers.
+      constexpr uint32_t idesc = idesc_pair(BN);
+      uint32_t it = 0, h = 0;
+      int lt = 0;
+      for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
+        const int ab = lt % C::kAcc;
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * BN);
+        for (int kb = 0; kb < p.KB; ++kb, ++it, ++h) {
+          const int st = static_cast<int>(it % C::kStages);
+          named_sync(1u + h % C::kQueue, 64);
+          tc_fence_after();
+          const uint64_t a_desc = make_sdesc_sw128(smem_u32(sA(st)));
+          const uint64_t b_desc = make_sdesc_sw128(smem_u32(sB(st)));
+          if (elect_one()) {
+#pragma unroll
+            for (int k = 0; k < kBlockK / 16; ++k)  // K step = 32 bytes = 2 start-address units
+              umma_f16_pair(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_commit_pair(smem_u32(&empty[st]));  // this CTA's stage
+            umma_commit_pair(map_to(&empty[st], 1));  // the odd CTA's stage
+          }
+          __syncwarp();
+        }
+        if (elect_one()) {
+          umma_commit_pair(smem_u32(&tfull[ab]));
+          umma_commit_pair(map_to(&tfull[ab], 1));
+        }
+        __syncwarp();
+      }
+      if (elect_one()) umma_commit_pair(smem_u32(mma_done));
+      __syncwarp();
+      mbar_wait(mma_done, 0, kErrWaitFull, p.wait_limit);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair's MMAs or loads may touch it
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::kAcc * BN);
+  }
+}
+
+// Weights [n_cols, k_pad] fp16: box {64, BN/2} (this CTA's half of a pair
+// tile's output channels), rows past n_cols read as zero.
+int make_w_map(CUtensorMap* map, const ConvTcArgs& a, int box_rows) {
+  auto enc = encode_tiled();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.k_pad), static_cast<cuuint64_t>(a.n_cols)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.k_pad) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.w_packed), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+// im2col map over the NHWC activation [N, H, W, Cs]: 128 output pixels x 64
+// channels per load, bounding box [-pad, dim - 1 + pad - (k - 1)],
+// traversal stride = conv stride.
+int make_im2col_map(CUtensorMap* map, const ConvTcArgs& a, int n_img) {
+  auto enc = encode_im2col();
+  if (!enc) return -1;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Cs_in), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
+                        static_cast<cuuint64_t>(n_img)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.Cs_in) * 2, static_cast<cuuint64_t>(a.W) * a.Cs_in * 2,
+                           static_cast<cuuint64_t>(a.H) * a.W * a.Cs_in * 2};
+  int lower[2] = {-a.pw, -a.ph};
+  int upper[2] = {a.pw - (a.kw - 1), a.ph - (a.kh - 1)};
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(a.sw), static_cast<cuuint32_t>(a.sh), 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(a.x), dims, strides, lower,
+                         upper, kBlockK, kBlockM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+template <int BN>
+int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
+  using C = PairCfg<BN>;
+  PairParams p{};
+  p.bias = a.bias;
+  p.residual = static_cast<const __half*>(a.residual);
+  p.y = static_cast<__half*>(a.y);
+  p.M = a.M;
+  p.Cout = a.n_cols;
+  p.Cs_out = a.Cs_out;
+  p.y_stride = a.y_stride != 0 ? a.y_stride : a.Cs_out;
+  p.act = a.act;
+  p.H = a.H;
+  p.W = a.W;
+  p.OH = a.OH;
+  p.OW = a.OW;
+  p.sh = a.sh;
+  p.sw = a.sw;
+  p.ph = a.ph;
+  p.pw = a.pw;
+  p.kh = a.kh;
+  p.kw = a.kw;
+  p.Cs_in = a.Cs_in;
+  p.KB = a.k_pad / kBlockK;
+  p.n_tiles = (a.n_cols + BN - 1) / BN;
+  p.m_tiles = (a.M + kBlockM - 1) / kBlockM;
+  p.pair_tiles = (p.m_tiles + 1) / 2 * p.n_tiles;
+  p.wait_limit = wait_limit_from_env();
+  const int n_img = a.M / (a.OH * a.OW);
+
+  CUtensorMap mw, ma;
+  if (make_w_map(&mw, a, C::kBHalf) != 0) {
+    *err = "pair conv: weight tensor map encoding failed";
+    return -3;
+  }
+  if (make_im2col_map(&ma, a, n_img) != 0) {
+    *err = "pair conv: im2col tensor map encoding failed";
+    return -2;
+  }
+  // per device and context: the shared-memory opt-in and the number of CTA
+  // pairs that can be resident at once
+  static std::atomic<uint64_t> attr_ctx[64];
+  static std::atomic<int> max_pairs[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = "pair conv: no usable device";
+    return -3;
+  }
+  const uint64_t ctx = current_context_id();
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (ctx == 0 || attr_ctx[dev].load(std::memory_order_acquire) != ctx) {
+    cudaError_t ae =
+        cudaFuncSetAttribute(conv_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (ae != cudaSuccess) {
+      *err = cudaGetErrorString(ae);
+      return -3;
+    }
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int clusters = 0;
+    ae = cudaOccupancyMaxActiveClusters(&clusters, conv_pair_kernel<BN>, &cfg);
+    if (ae != cudaSuccess || clusters < 1) {
+      *err = ae != cudaSuccess ? cudaGetErrorString(ae) : "pair conv: no CTA pair fits an SM pair";
+      return -3;
+    }
+    max_pairs[dev].store(clusters, std::memory_order_relaxed);
+    attr_ctx[dev].store(ctx, std::memory_order_release);
+  }
+  const int pairs = std::min(max_pairs[dev].load(std::memory_order_relaxed), p.pair_tiles);
+  cfg.gridDim = dim3(2 * pairs);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, conv_pair_kernel<BN>, mw, ma, p);
+  note_launch();
+  if (e != cudaSuccess) {
+    *err = cudaGetErrorString(e);
+    return -3;
+  }
+  return 0;
+}
+
+}  // namespace
+
+int conv_pair_check(const ConvTcArgs& a, int bn, const char** err) {
+  if (bn != 128 && bn != 256) {
+    *err = "pair conv: 128 or 256 columns per tile";
+    return -2;
+  }
+  if (a.out_kind != 0) {
+    *err = "pair conv: NHWC fp16 output only";
+    return -2;
+  }
+  if (a.Cs_in % kBlockK != 0 || a.k_pad != a.kh * a.kw * a.Cs_in) {
+    *err = "pair conv: input channels a multiple of 64";
+    return -2;
+  }
+  if (a.n_cols < 1 || a.n_cols > kBiasMax || a.Cs_out != (a.n_cols + 7) / 8 * 8) {
+    *err = "pair conv: 1..1024 output channels";
+    return -2;
+  }
+  if (a.y_stride != 0 && (a.y_stride < a.Cs_out || a.y_stride % 8 != 0)) {
+    *err = "pair conv: output pixel stride";
+    return -2;
+  }
+  if (a.OH < 1 || a.OW < 1 || a.M < 1 || a.M % (a.OH * a.OW) != 0 || a.kh > 256 || a.kw > 256) {
+    *err = "pair conv: shape";
+    return -2;
+  }
+  return 0;
+}
+
+int conv_pair_launch(const ConvTcArgs& a, int bn, cudaStream_t stream, const char** err) {
+  if (conv_pair_check(a, bn, err) != 0) return -2;
+  return bn == 256 ? launch_bn<256>(a, stream, err) : launch_bn<128>(a, stream, err);
+}
+
+int conv_pair_read_device_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, lotus_dev::g_lotus_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v != 0) {
+    int zero = 0;
+    cudaMemcpyToSymbol(lotus_dev::g_lotus_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace lotus_impl

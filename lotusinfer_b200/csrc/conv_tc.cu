@@ -1212,7 +1212,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   return fn;
 }
 
-static PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col() {
+PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col() {
   static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -1673,7 +1673,8 @@ int read_device_error() {
   const int a = read_own_device_error();
   const int b = conv_row_read_device_error();
   const int c = conv_rows_read_device_error();
-  return a != 0 ? a : b != 0 ? b : c;
+  const int d = conv_pair_read_device_error();
+  return a != 0 ? a : b != 0 ? b : c != 0 ? c : d;
 }
 
 }  // namespace lotus_impl

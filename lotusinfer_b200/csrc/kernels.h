@@ -56,6 +56,7 @@ int read_device_error();
 // the current CUDA context (0 = none).
 void* driver_fn(const char* name);
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
+PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col();
 int num_sms();
 uint32_t wait_limit_from_env();
 uint64_t current_context_id();
@@ -84,6 +85,15 @@ int conv_row_read_device_error();
 int conv_rows_check(const ConvTcArgs& a, int n, const char** err);
 int conv_rows_launch(const ConvTcArgs& a, int n, cudaStream_t stream, const char** err);
 int conv_rows_read_device_error();
+
+// conv_pair.cu: the conv on CTA pairs (tcgen05 cta_group::2) for inputs
+// with a multiple of 64 channels, NHWC fp16 output (optional residual, any
+// kernel / stride / padding the im2col TMA takes), output channels <= 1024.
+// `bn` = 128 or 256 columns per pair tile.  check: 0 when it takes the
+// shape, else -2 with the reason in *err.
+int conv_pair_check(const ConvTcArgs& a, int bn, const char** err);
+int conv_pair_launch(const ConvTcArgs& a, int bn, cudaStream_t stream, const char** err);
+int conv_pair_read_device_error();
 
 // pack.cu
 cudaError_t launch_conv_prepack(const float* w, void* wp, int cout, int cin, int kh, int kw, int cs_in, int k_pad,

@@ -215,6 +215,105 @@ def test_conv2d_rows_kernel_matches_general_kernel(with_res, monkeypatch):
     _no_device_error()
 
 
+PAIR_CASES = [
+    # id, n, c, h, w, cout, k, stride, pad, act, residual: convs over 64-channel
+    # multiples on CTA pairs (forced with LOTUS_CONV_PAIR=1)
+    ("pair_3x3_128_residual", 2, 128, 14, 14, 128, 3, 1, 1, 1, True),   # M = 392: odd M-tile count
+    ("pair_3x3s2_64to128", 3, 64, 20, 20, 128, 3, 2, 1, 1, False),
+    ("pair_1x1s2_64to256", 2, 64, 28, 28, 256, 1, 2, 0, 0, False),       # 256-column tiles
+    ("pair_cout192_partial_tile", 2, 128, 9, 9, 192, 3, 1, 1, 2, False),
+    ("pair_cout136_pad_channels", 1, 64, 12, 12, 136, 3, 1, 1, 1, True),
+    ("pair_cin192_5x5", 1, 192, 11, 11, 128, 5, 1, 2, 1, False),
+]
+
+
+@pytest.mark.parametrize("case", PAIR_CASES, ids=[c[0] for c in PAIR_CASES])
+def test_conv2d_pair_kernel_parity(case, monkeypatch):
+    monkeypatch.setenv("LOTUS_CONV_PAIR", "1")
+    _conv2d_parity_no_f32(case)
+
+
+def _conv2d_parity_no_f32(case):
+    K = _k()
+    _, n, c, h, w, cout, k, s, p, act, with_res = case
+    rng = _rng(zlib.crc32(case[0].encode()))
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / (c * k * k)), (cout, c, k, k)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, cout).astype(np.float32)
+    oh = (h + 2 * p - k) // s + 1
+    ow = (w + 2 * p - k) // s + 1
+    res = rng.normal(0, 1, (n, cout, oh, ow)).astype(np.float32) if with_res else None
+    want = oracle.conv2d(x, wt, b, (s, s), (p, p), act, residual=res)
+    xg = K.to_nhwc(_gpu(x))
+    wp = K.conv2d_prepack(_gpu(wt), c)
+    rg = K.to_nhwc(_gpu(res)) if with_res else None
+    y = K.conv2d(xg, c, wp, _gpu(b), cout, k, s, p, act, residual=rg)
+    assert_close(K.from_nhwc(y, cout).cpu().numpy(), want, what=case[0])
+    if y.shape[-1] != cout:
+        assert torch.count_nonzero(y[..., cout:]).item() == 0
+    _no_device_error()
+
+
+@pytest.mark.parametrize("case", [
+    # name, n, c, h, w, cout, k, stride, pad, residual, pair mode: ResNet-18
+    # stages 2-4 at batch 256 (many pair tiles per CTA pair: every stage ring
+    # and accumulator wraps), against the general single-CTA kernel
+    ("stage2_3x3_residual_128cols", 256, 128, 28, 28, 128, 3, 1, 1, True, "1"),
+    ("stage2_3x3s2_128cols", 256, 64, 56, 56, 128, 3, 2, 1, False, "1"),
+    ("stage3_3x3", 256, 256, 14, 14, 256, 3, 1, 1, False, "auto"),
+    ("stage3_1x1s2", 256, 128, 28, 28, 256, 1, 2, 0, False, "auto"),
+    ("stage4_3x3_residual", 256, 512, 7, 7, 512, 3, 1, 1, True, "auto"),
+    ("stage4_3x3_residual_256cols", 256, 512, 7, 7, 512, 3, 1, 1, True, "1"),
+], ids=lambda c: c[0])
+def test_conv2d_pair_kernel_matches_general_kernel(case, monkeypatch):
+    """Each output pixel is one SM's dot products in the same K order on
+    both kernels, so the outputs are equal bit for bit."""
+    K = _k()
+    _, n, c, h, w, cout, k, s, p, with_res, mode = case
+    g = torch.Generator(device=DEV).manual_seed(zlib.crc32(case[0].encode()))
+    x = K.to_nhwc(torch.rand((n, c, h, w), device=DEV, generator=g) * 2 - 1)
+    wt = torch.randn((cout, c, k, k), device=DEV, generator=g) * (2.0 / (c * k * k)) ** 0.5
+    b = torch.rand(cout, device=DEV, generator=g) * 0.2 - 0.1
+    oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    res = K.to_nhwc(torch.randn((n, cout, oh, ow), device=DEV, generator=g)) if with_res else None
+    wp = K.conv2d_prepack(wt, c)
+    if mode == "auto":
+        monkeypatch.delenv("LOTUS_CONV_PAIR", raising=False)
+    else:
+        monkeypatch.setenv("LOTUS_CONV_PAIR", mode)
+    y_pair = K.conv2d(x, c, wp, b, cout, k, s, p, 1, residual=res)
+    monkeypatch.setenv("LOTUS_CONV_PAIR", "0")
+    y_gen = K.conv2d(x, c, wp, b, cout, k, s, p, 1, residual=res)
+    torch.cuda.synchronize()
+    assert torch.equal(y_pair, y_gen)
+    _no_device_error()
+
+
+def test_conv2d_pair_kernel_channel_slice(monkeypatch):
+    """The pair kernel writes a channel slice of a wider NHWC tensor and
+    leaves the other channels untouched."""
+    monkeypatch.setenv("LOTUS_CONV_PAIR", "1")
+    K = _k()
+    from lotusinfer_b200 import abi
+    import ctypes
+    g = torch.Generator(device=DEV).manual_seed(3)
+    n, c, h, w, cout = 2, 128, 10, 10, 128
+    x = K.to_nhwc(torch.rand((n, c, h, w), device=DEV, generator=g) * 2 - 1)
+    wt = torch.randn((cout, c, 3, 3), device=DEV, generator=g) * (2.0 / (c * 9)) ** 0.5
+    b = torch.rand(cout, device=DEV, generator=g) * 0.2 - 0.1
+    wp = K.conv2d_prepack(wt, c)
+    ref = K.conv2d(x, c, wp, b, cout, 3, 1, 1, 1)
+    wide = torch.full((n, h, w, 256), 7.0, dtype=torch.float16, device=DEV)
+    d = K.conv_desc(n, c, h, w, cout, 3, 1, 1, 1)
+    K.check(abi.lib().lotus_conv2d_fwd_slice(K._ptr(x), K._ptr(wp), K._ptr(b), None,
+                                             ctypes.c_void_p(wide.data_ptr() + 64 * 2), 256, ctypes.byref(d),
+                                             None, 0, K._stream()))
+    torch.cuda.synchronize()
+    assert torch.equal(wide[..., 64:192], ref)
+    assert bool((wide[..., :64] == 7.0).all()) and bool((wide[..., 192:] == 7.0).all())
+    _no_device_error()
+
+
 SPLITK_CASES = [
     # id, n, c, h, w, cout, k, stride, pad, act, residual: output grids too
     # small to fill the GPU, so the K loop splits over CTAs
