@@ -493,7 +493,9 @@ def main():
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if peak else None, "traffic": traffic,
                 "scope": "the 20 conv launches of one forward: FLOPs and DRAM bytes summed over them",
-                "kernel": "conv_tc_kernel (tcgen05 implicit GEMM, fp16 x fp16 -> fp32)",
+                "kernel": "the conv launches of one forward: conv_row_kernel (stem + pool), conv_rows_kernel "
+                          "(stage 1), conv_tc_kernel (stage 2), conv_pair_kernel (stages 3-4, tcgen05 cta_group::2); "
+                          "fp16 x fp16 -> fp32",
                 "peak_source": f"{peak_src} bf16/fp16 dense burst", "frac_of_sustained": achieved / peak_sus if peak_sus else None,
                 "conv_ms_per_forward": conv_ms, "conv_gflop_per_forward": conv_flops / 1e9,
                 "conv_launches_per_forward": conv_launches,
