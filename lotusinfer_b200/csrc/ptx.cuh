@@ -302,6 +302,15 @@ __device__ __forceinline__ void tmem_st_zero_32x32b_x16(uint32_t taddr) {
       "r"(0u)
       : "memory");
 }
+// 32 lanes x 32 columns of fp32 zeros into TMEM (one lane per thread).
+__device__ __forceinline__ void tmem_st_zero_32x32b_x32(uint32_t taddr) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+          taddr),
+      "r"(0u)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Epilogue activation, same enum values as the reference's ActivationFunction.
