@@ -159,24 +159,30 @@ static bool use_rows_conv(const ConvTcArgs& a, int n) {
 }
 
 // The CTA-pair kernel takes NHWC fp16 convs over 64-channel multiples with
-// at least 256 output channels (256-column pair tiles) when the launch fills
-// every SM pair at least once.  With 128-column tiles the A and B bytes per
-// unit of math outrun the load pipeline (measured slower than the general
-// kernel on ResNet stage 2), so narrower layers and smaller launches go to
-// the general kernel, which can also split K.  LOTUS_CONV_PAIR=0 or 1
-// forces the choice (1: 256 columns when Cout > 128, else 128); a forced
-// general-kernel staging mode (LOTUS_CONV_AMODE) implies 0.
+// at least 128 output channels when its pair tiles fill every SM pair at
+// least once: 256 x 256 pair tiles above 128 output channels, 512 x 128 pair
+// tiles (two M tiles a CTA) at 128 with K <= 576 (one M tile a CTA with 128
+// columns was measured slower than the general kernel: too little MMA per
+// loaded stage).  Smaller launches go to the general kernel, which can split K.
+// LOTUS_CONV_PAIR=0 or 1 forces the choice (1: 256 columns when Cout > 128,
+// else 128); a forced general-kernel staging mode (LOTUS_CONV_AMODE)
+// implies 0.
 static int pair_conv_bn(const ConvTcArgs& a) {
   const char* env = std::getenv("LOTUS_CONV_PAIR");
   if (env != nullptr && env[0] == '0') return 0;
   if (env == nullptr && std::getenv("LOTUS_CONV_AMODE") != nullptr) return 0;
   const char* err = "";
   if (conv_pair_check(a, 128, &err) != 0 || a.n_cols < 128) return 0;
-  if (env != nullptr && env[0] == '1') return a.n_cols > 128 ? 256 : 128;
-  if (a.n_cols < 256) return 0;
+  const int bn = a.n_cols > 128 ? 256 : 128;
+  if (env != nullptr && env[0] == '1') return bn;
   const long pairs = num_sms() / 2;
-  const long m_pairs = ((a.M + 127) / 128 + 1) / 2;
-  return m_pairs * ((a.n_cols + 255) / 256) >= pairs ? 256 : 0;
+  const long m_tiles = (a.M + 127) / 128;
+  const long m_groups = bn == 256 ? (m_tiles + 1) / 2 : (m_tiles + 3) / 4;  // M tiles a pair tile covers: 2 or 4
+  // 512 x 128 pair tiles beat the general kernel on the short-K layers of
+  // ResNet stage 2 (1x1/2: 0.031 vs 0.039 ms; 3x3/2 equal) but not on its
+  // K = 1152 3x3 layers (0.060-0.071 vs 0.060-0.068)
+  if (bn == 128 && a.k_pad > 576) return 0;
+  return m_groups * ((a.n_cols + bn - 1) / bn) >= pairs ? bn : 0;
 }
 
 static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,

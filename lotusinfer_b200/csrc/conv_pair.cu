@@ -74,15 +74,19 @@ constexpr int kBiasMax = 1024;
 constexpr int kHeadBytes = 1024;                // barriers and misc words
 constexpr int kSmemLimit = 232448;
 
-template <int BN>
+// BN columns per pair tile; MT M tiles (of 128 rows) per CTA: a pair tile is
+// 2 * MT * 128 rows x BN columns, one M = 256 MMA per M tile and K step, all
+// MT of them reading the same B half.
+template <int BN, int MT>
 struct PairCfg {
   static constexpr int kBHalf = BN / 2;                    // weight rows per CTA
   static constexpr int kBBytes = kBHalf * kBlockK * 2;     // 8 or 16 KB
-  static constexpr int kStage = kABytes + kBBytes;
+  static constexpr int kStage = MT * kABytes + kBBytes;
   static constexpr int kFixed = 1024 + kHeadBytes + kBiasMax * 4 + kEpiWarps * kStgBytes;
   static constexpr int kStages = std::min(8, (kSmemLimit - kFixed) / kStage);
   static constexpr int kQueue = kStages + 1;               // named barriers 1 .. kQueue
-  static constexpr int kAcc = 512 / BN;                    // TMEM accumulators
+  static constexpr int kAccCols = BN * MT;                 // TMEM columns of one pair tile
+  static constexpr int kAcc = 512 / kAccCols;              // TMEM accumulators
   static constexpr int kSmemBytes = kFixed + kStages * kStage;
   static_assert(kQueue <= 15, "named barriers");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory");
@@ -97,7 +101,7 @@ struct PairParams {
   int KB;           // 64-wide K blocks
   int n_tiles;      // BN-column tiles
   int m_tiles;      // 128-row M tiles
-  int pair_tiles;   // ceil(m_tiles / 2) * n_tiles
+  int pair_tiles;   // ceil(m_tiles / (2 * MT)) * n_tiles
   uint32_t wait_limit;
 };
 
@@ -267,18 +271,23 @@ __device__ __forceinline__ void store_chunk(const PairParams& p, const uint32_t 
 }
 
 // Epilogue warps of both CTAs: this CTA's 128 rows of each pair tile.
-template <int BN, int ACT>
+template <int BN, int MT, int ACT>
 __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, uint64_t* tempty, const float* s_bias,
                                          uint8_t* stg, uint32_t tmem_base, uint32_t rank, volatile int* abort_flag) {
-  using C = PairCfg<BN>;
+  using C = PairCfg<BN, MT>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // warps 4h .. 4h+3 take half h of the tile's TMEM columns: with one M
+  // tile a CTA, columns BN/2*h ..; with two, all BN columns of M tile h
   const int q = warp & 3, half = warp >> 2;
+  const int mi = MT == 2 ? half : 0;                 // this warp's M tile
+  const int col_base = MT == 2 ? 0 : half * (BN / 2);  // its first output column in the tile
+  constexpr int kWarpCols = BN * MT / 2;
   const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
   const int pair0 = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
   int lt = 0;
   for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
     const int mp = T / p.n_tiles, nt = T - mp * p.n_tiles;
-    const int em = ((2 * mp + static_cast<int>(rank)) * kBlockM) + q * 32 + lane;
+    const int em = (((2 * mp + static_cast<int>(rank)) * MT + mi) * kBlockM) + q * 32 + lane;
     const bool valid = em < p.M;
     const int n0 = nt * BN;
     const int ab = lt % C::kAcc;
@@ -287,11 +296,12 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
     ok = __shfl_sync(0xffffffffu, ok, 0);
     tc_fence_after();
 #pragma unroll 1
-    for (int c = 0; c < C::kBHalf / 32; ++c) {
-      const int col = half * C::kBHalf + c * 32;  // column inside the tile
+    for (int c = 0; c < kWarpCols / 32; ++c) {
+      const int col = col_base + c * 32;  // output column inside the tile
       if (!ok || n0 + col >= p.Cs_out) continue;  // warp-uniform
       uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem_base + t_lane + static_cast<uint32_t>(ab * BN + col), v);
+      tmem_ld_32x32b_x32(tmem_base + t_lane + static_cast<uint32_t>(ab * C::kAccCols + half * kWarpCols + c * 32),
+                         v);
       tmem_ld_wait();
       store_chunk<ACT>(p, v, em, valid, n0 + col, s_bias, stg, lane);
     }
@@ -308,11 +318,11 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
   }
 }
 
-template <int BN>
+template <int BN, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
 conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                  const PairParams p) {
-  using C = PairCfg<BN>;
+  using C = PairCfg<BN, MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [kStages] even CTA: both halves of a stage landed
@@ -325,8 +335,8 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   float* s_bias = reinterpret_cast<float*>(smem + kHeadBytes);
   uint8_t* s_stg = smem + kHeadBytes + kBiasMax * 4;
   uint8_t* stages = s_stg + kEpiWarps * kStgBytes;  // 1024-aligned: 1024 + 4096 + 16384
-  auto sA = [&](int st) { return stages + st * C::kStage; };
-  auto sB = [&](int st) { return stages + st * C::kStage + kABytes; };
+  auto sA = [&](int st, int i) { return stages + st * C::kStage + i * kABytes; };
+  auto sB = [&](int st) { return stages + st * C::kStage + MT * kABytes; };
 
   const int tid = threadIdx.x;
   const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0), lane = tid & 31;
@@ -352,7 +362,7 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     tma_prefetch_desc(&tmap_a);
   }
   if (warp == kMmaWarp) {
-    tmem_alloc_pair(tmem_slot, C::kAcc * BN);
+    tmem_alloc_pair(tmem_slot, C::kAcc * C::kAccCols);
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -364,11 +374,11 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   if (warp < kEpiWarps) {
     uint8_t* stg = s_stg + warp * kStgBytes;
     if (p.act == 1)
-      epilogue<BN, 1>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+      epilogue<BN, MT, 1>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
     else if (p.act == 0)
-      epilogue<BN, 0>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+      epilogue<BN, MT, 0>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
     else
-      epilogue<BN, 2>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+      epilogue<BN, MT, 2>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
   } else if (warp == kTmaWarp) {
     if (lane == 0) {
       bool ok = true;
@@ -376,13 +386,20 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       const int ohw = p.OH * p.OW, cpt = p.Cs_in / kBlockK;
       for (int T = pair0; T < p.pair_tiles && ok; T += npairs) {
         const int mp = T / p.n_tiles, nt = T - mp * p.n_tiles;
-        // an odd M-tile count leaves the last pair's odd half without rows:
-        // it loads a real tile (its results are never stored)
-        const int mt = min(2 * mp + static_cast<int>(rank), p.m_tiles - 1);
-        const int m0 = mt * kBlockM;
-        const int nimg = m0 / ohw, rem = m0 - nimg * ohw;
-        const int oh = rem / p.OW, ow = rem - oh * p.OW;
-        const int wst = ow * p.sw - p.pw, hst = oh * p.sh - p.ph;
+        // this CTA's M tiles; past the last M tile (a pair tile that overhangs
+        // the output) it loads the last real tile (those results are never
+        // stored)
+        int wst[MT], hst[MT], nimg[MT];
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          const int mt = min((2 * mp + static_cast<int>(rank)) * MT + i, p.m_tiles - 1);
+          const int m0 = mt * kBlockM;
+          nimg[i] = m0 / ohw;
+          const int rem = m0 - nimg[i] * ohw;
+          const int oh = rem / p.OW, ow = rem - oh * p.OW;
+          wst[i] = ow * p.sw - p.pw;
+          hst[i] = oh * p.sh - p.ph;
+        }
         const int brow = nt * BN + static_cast<int>(rank) * C::kBHalf;
         int c0 = 0, s = 0, r = 0;
         for (int kb = 0; kb < p.KB; ++kb, ++it) {
@@ -394,8 +411,10 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
           if (rank == 0) mbar_arrive_expect_tx(&full[st], 2u * C::kStage);
           const uint32_t fb = map_to(&full[st], 0);
           tma_load_2d_pair(sB(st), &tmap_w, fb, kb * kBlockK, brow);
-          tma_load_im2col_4d_pair(sA(st), &tmap_a, fb, c0, wst, hst, nimg, static_cast<uint16_t>(s),
-                                  static_cast<uint16_t>(r));
+#pragma unroll
+          for (int i = 0; i < MT; ++i)
+            tma_load_im2col_4d_pair(sA(st, i), &tmap_a, fb, c0, wst[i], hst[i], nimg[i], static_cast<uint16_t>(s),
+                                    static_cast<uint16_t>(r));
           c0 += kBlockK;
           if (c0 == p.Cs_in) {
             c0 = 0;
@@ -443,17 +462,20 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       int lt = 0;
       for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
         const int ab = lt % C::kAcc;
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * C::kAccCols);
         for (int kb = 0; kb < p.KB; ++kb, ++it, ++h) {
           const int st = static_cast<int>(it % C::kStages);
           named_sync(1u + h % C::kQueue, 64);
           tc_fence_after();
-          const uint64_t a_desc = make_sdesc_sw128(smem_u32(sA(st)));
+          const uint64_t a_desc = make_sdesc_sw128(smem_u32(sA(st, 0)));
           const uint64_t b_desc = make_sdesc_sw128(smem_u32(sB(st)));
           if (elect_one()) {
 #pragma unroll
             for (int k = 0; k < kBlockK / 16; ++k)  // K step = 32 bytes = 2 start-address units
-              umma_f16_pair(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+              for (int i = 0; i < MT; ++i)  // M tile i: its A 16 KB further, its accumulator BN columns further
+                umma_f16_pair(d_tmem + static_cast<uint32_t>(i * BN), a_desc + 2u * k + static_cast<uint32_t>(i * (kABytes >> 4)),
+                              b_desc + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
             umma_commit_pair(smem_u32(&empty[st]));  // this CTA's stage
             umma_commit_pair(map_to(&empty[st], 1));  // the odd CTA's stage
           }
@@ -476,7 +498,7 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   cluster_sync();  // neither CTA leaves while the pair's MMAs or loads may touch it
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, C::kAcc * BN);
+    tmem_dealloc_pair(tmem_base, C::kAcc * C::kAccCols);
   }
 }
 
@@ -514,9 +536,9 @@ int make_im2col_map(CUtensorMap* map, const ConvTcArgs& a, int n_img) {
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-template <int BN>
+template <int BN, int MT>
 int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
-  using C = PairCfg<BN>;
+  using C = PairCfg<BN, MT>;
   PairParams p{};
   p.bias = a.bias;
   p.residual = static_cast<const __half*>(a.residual);
@@ -540,7 +562,7 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   p.KB = a.k_pad / kBlockK;
   p.n_tiles = (a.n_cols + BN - 1) / BN;
   p.m_tiles = (a.M + kBlockM - 1) / kBlockM;
-  p.pair_tiles = (p.m_tiles + 1) / 2 * p.n_tiles;
+  p.pair_tiles = (p.m_tiles + 2 * MT - 1) / (2 * MT) * p.n_tiles;
   p.wait_limit = wait_limit_from_env();
   const int n_img = a.M / (a.OH * a.OW);
 
@@ -576,14 +598,14 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   cfg.numAttrs = 1;
   if (ctx == 0 || attr_ctx[dev].load(std::memory_order_acquire) != ctx) {
     cudaError_t ae =
-        cudaFuncSetAttribute(conv_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+        cudaFuncSetAttribute(conv_pair_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (ae != cudaSuccess) {
       *err = cudaGetErrorString(ae);
       return -3;
     }
     cfg.gridDim = dim3(2 * (num_sms() / 2));
     int clusters = 0;
-    ae = cudaOccupancyMaxActiveClusters(&clusters, conv_pair_kernel<BN>, &cfg);
+    ae = cudaOccupancyMaxActiveClusters(&clusters, conv_pair_kernel<BN, MT>, &cfg);
     if (ae != cudaSuccess || clusters < 1) {
       *err = ae != cudaSuccess ? cudaGetErrorString(ae) : "pair conv: no CTA pair fits an SM pair";
       return -3;
@@ -593,7 +615,7 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   }
   const int pairs = std::min(max_pairs[dev].load(std::memory_order_relaxed), p.pair_tiles);
   cfg.gridDim = dim3(2 * pairs);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, conv_pair_kernel<BN>, mw, ma, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, conv_pair_kernel<BN, MT>, mw, ma, p);
   note_launch();
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);
@@ -634,7 +656,9 @@ int conv_pair_check(const ConvTcArgs& a, int bn, const char** err) {
 
 int conv_pair_launch(const ConvTcArgs& a, int bn, cudaStream_t stream, const char** err) {
   if (conv_pair_check(a, bn, err) != 0) return -2;
-  return bn == 256 ? launch_bn<256>(a, stream, err) : launch_bn<128>(a, stream, err);
+  // 128 columns: two M tiles a CTA (a 512 x 128 pair tile), so each weight
+  // stage feeds two MMAs per K step
+  return bn == 256 ? launch_bn<256, 1>(a, stream, err) : launch_bn<128, 2>(a, stream, err);
 }
 
 int conv_pair_read_device_error() {

@@ -89,7 +89,8 @@ int conv_rows_read_device_error();
 // conv_pair.cu: the conv on CTA pairs (tcgen05 cta_group::2) for inputs
 // with a multiple of 64 channels, NHWC fp16 output (optional residual, any
 // kernel / stride / padding the im2col TMA takes), output channels <= 1024.
-// `bn` = 128 or 256 columns per pair tile.  check: 0 when it takes the
+// `bn` = 256 (256 x 256 pair tiles) or 128 (512 x 128 pair tiles: two M
+// tiles a CTA).  check: 0 when it takes the
 // shape, else -2 with the reason in *err.
 int conv_pair_check(const ConvTcArgs& a, int bn, const char** err);
 int conv_pair_launch(const ConvTcArgs& a, int bn, cudaStream_t stream, const char** err);
