@@ -223,12 +223,24 @@ __device__ __forceinline__ void store_chunk(const PairParams& p, const uint32_t 
                                             int col0, const float* s_bias, uint8_t* stg, int lane) {
   uint4* st = reinterpret_cast<uint4*>(stg);
   const bool full = col0 + 32 <= p.Cout;
+  const int row_em = valid ? em : -1;
   uint4 res[4];
+  if (p.residual != nullptr) {
+    // the chunk's residual rows, read as 8 rows x 64 contiguous bytes per
+    // instruction into the staging buffer, then each lane takes its row
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    res[g] = make_uint4(0, 0, 0, 0);
-    if (p.residual != nullptr && valid && col0 + 8 * g < p.Cs_out)
-      res[g] = __ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em) * p.Cs_out + col0 + 8 * g));
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2), c = lane & 3;
+      const int em_r = __shfl_sync(0xffffffffu, row_em, r);
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (em_r >= 0 && col0 + c * 8 < p.Cs_out)
+        val = __ldg(reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(em_r) * p.Cs_out + col0 + c * 8));
+      st[r * 4 + ((c ^ (r >> 1)) & 3)] = val;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < 4; ++g) res[g] = st[lane * 4 + ((g ^ (lane >> 1)) & 3)];
+    __syncwarp();  // the buffer takes the output next
   }
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
@@ -256,7 +268,6 @@ __device__ __forceinline__ void store_chunk(const PairParams& p, const uint32_t 
         make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]), pack_h2(f[6], f[7]));
   }
   __syncwarp();
-  const int row_em = valid ? em : -1;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = 8 * i + (lane >> 2);  // staged row this lane stores
