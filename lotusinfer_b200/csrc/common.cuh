@@ -33,6 +33,18 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it is still running; it
+// calls griddep_wait() before its first access to memory an earlier kernel
+// writes or reads (activations, workspaces), which returns once every
+// prerequisite grid has completed and its memory is visible.  Reads of
+// weights and biases, shared-memory and TMEM set-up may come before it.
+// griddep_launch() lets this grid's own dependents start being scheduled
+// (they are, once every CTA of this grid has issued it or exited).  Both are
+// no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // Grid size for a grid-stride loop: enough CTAs to fill 148 SMs several
 // times over, never more than the work needs.
 __host__ __forceinline__ unsigned grid_for(size_t work, int block, int per_sm_ctas = 8) {

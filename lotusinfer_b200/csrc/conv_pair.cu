@@ -381,8 +381,10 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   cluster_sync();  // both CTAs' barriers exist before any remote arrival or commit
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (tid == 0) griddep_launch();  // set-up done: the next kernel may start being scheduled
 
   if (warp < kEpiWarps) {
+    griddep_wait();  // residual and output buffers belong to earlier kernels
     uint8_t* stg = s_stg + warp * kStgBytes;
     if (p.act == 1)
       epilogue<BN, MT, 1>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
@@ -392,6 +394,7 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       epilogue<BN, MT, 2>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
   } else if (warp == kTmaWarp) {
     if (lane == 0) {
+      griddep_wait();  // the activations of earlier kernels
       bool ok = true;
       uint32_t it = 0;
       const int ohw = p.OH * p.OW, cpt = p.Cs_in / kBlockK;
@@ -597,11 +600,13 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   }
   const uint64_t ctx = current_context_id();
   cudaLaunchConfig_t cfg{};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
@@ -626,6 +631,7 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   }
   const int pairs = std::min(max_pairs[dev].load(std::memory_order_relaxed), p.pair_tiles);
   cfg.gridDim = dim3(2 * pairs);
+  cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, conv_pair_kernel<BN, MT>, mw, ma, p);
   note_launch();
   if (e != cudaSuccess) {

@@ -382,8 +382,10 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (tid == 0) griddep_launch();  // set-up done: the next kernel may start being scheduled
 
   if (warp < kEpiWarps) {
+    griddep_wait();  // its output buffer may still be in use by earlier kernels
     if (p.act == 1)
       epilogue<1>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
     else if (p.act == 0)
@@ -395,6 +397,7 @@ conv_row_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constan
       bool ok = true;
       mbar_arrive_expect_tx(wfull, static_cast<uint32_t>(p.w_bytes));
       for (int r = 0; r < p.kh; ++r) tma_load_2d(sW + r * kWBlockBytes, &tmap_w, wfull, r * 64, 0);
+      griddep_wait();  // the weights do not depend on earlier kernels; the input rows do
       uint32_t L = 0;
       int u = u0;
       Seg sg;
@@ -627,9 +630,9 @@ int conv_row_launch(const ConvRowArgs& a, cudaStream_t stream, const char** err)
     attr_ctx[dev].store(ctx, std::memory_order_release);
   }
   const int grid = std::min(num_sms(), p.units);
-  conv_row_kernel<<<grid, kThreads, kSmemBytes, stream>>>(mw, mx, p);
+  cudaError_t e = launch_pdl(conv_row_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, mw, mx, p);
   note_launch();
-  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);
     return -3;

@@ -275,8 +275,10 @@ conv_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (tid == 0) griddep_launch();  // set-up done: the next kernel may start being scheduled
 
   if (warp < kEpiWarps) {
+    griddep_wait();  // residual and output buffers belong to earlier kernels
     if (p.act == 1)
       epilogue<1>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
     else if (p.act == 0)
@@ -291,6 +293,7 @@ conv_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       for (int s = 0; s < p.kw; ++s)
         for (int j = 0; j < p.kh; ++j)
           tma_load_2d(sW + (s * p.kh + j) * kWBlock, &tmap_w, wfull, (j * p.kw + s) * 64, 0);
+      griddep_wait();  // the weights do not depend on earlier kernels; the input rows do
       uint32_t L = 0;
       int u = u0;
       Seg sg;
@@ -541,9 +544,9 @@ int conv_rows_launch(const ConvTcArgs& a, int n, cudaStream_t stream, const char
     attr_ctx[dev].store(ctx, std::memory_order_release);
   }
   const int grid = std::min(num_sms(), p.units);
-  conv_rows_kernel<<<grid, kThreads, smem, stream>>>(mw, mx, p);
+  cudaError_t e = launch_pdl(conv_rows_kernel, dim3(grid), dim3(kThreads), smem, stream, mw, mx, p);
   note_launch();
-  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);
     return -3;

@@ -541,6 +541,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int ohw = p.OH * p.OW;
+  // set-up done: let the next kernel start being scheduled, then wait for
+  // the kernels before this one (activations, residual, workspace)
+  if (tid == 0) griddep_launch();
+  griddep_wait();
 
   if (warp < C::kEpiWarps) {
     // ================================================================ epilogue
@@ -1346,6 +1350,14 @@ static double halo4_plan(const ConvTcArgs& a, int bn, int stages, ConvTcParams* 
 
 // Bounded-wait limit of a launch: LOTUS_WAIT_LIMIT try_wait rounds (1 .. 2^30)
 // when set, kMaxWaitIters otherwise.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("LOTUS_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
 uint32_t wait_limit_from_env() {
   const char* e = std::getenv("LOTUS_WAIT_LIMIT");
   if (!e) return kMaxWaitIters;
@@ -1360,6 +1372,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
                                      const float* __restrict__ bias, const __half* __restrict__ residual,
                                      void* __restrict__ y, int M, int cout, int cs_out, int y_stride, int act,
                                      int out_kind) {
+  if (threadIdx.x == 0) griddep_launch();
+  griddep_wait();  // the partial sums of the kernel before
   const int groups = out_kind == 0 ? cs_out / 8 : (cout + 7) / 8;
   const int total = M * groups;  // < 2^31, checked by the launcher
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -1448,9 +1462,9 @@ static cudaError_t launch_impl(const CUtensorMap& mw, const CUtensorMap& ma, con
     attr_ctx[dev].store(ctx, std::memory_order_release);
   }
   const int grid = p.tiles < num_sms() ? p.tiles : num_sms();
-  kern<<<grid, C::kThreads, smem, stream>>>(mw, ma, p);
+  const cudaError_t le = launch_pdl(kern, dim3(grid), dim3(C::kThreads), smem, stream, mw, ma, p);
   note_launch();
-  return cudaGetLastError();
+  return le != cudaSuccess ? le : cudaGetLastError();
 }
 
 int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, size_t* ws_need) {
@@ -1607,11 +1621,11 @@ int conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream, const char** err, s
   if (e == cudaSuccess && p.ksplit > 1) {
     const size_t total = static_cast<size_t>(a.M) * (a.out_kind == 0 ? a.Cs_out / 8 : (a.n_cols + 7) / 8);
     const unsigned grid = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, static_cast<size_t>(num_sms()) * 8));
-    splitk_reduce_kernel<<<grid, 256, 0, stream>>>(p.ws, p.ksplit, p.ws_rows, p.ws_ld, a.bias,
-                                                   static_cast<const __half*>(a.residual), a.y, a.M, a.n_cols,
-                                                   a.Cs_out, p.y_stride, a.act, a.out_kind);
+    e = launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, stream, static_cast<const float*>(p.ws), p.ksplit,
+                   p.ws_rows, p.ws_ld, a.bias, static_cast<const __half*>(a.residual), a.y, a.M, a.n_cols, a.Cs_out,
+                   p.y_stride, a.act, a.out_kind);
     note_launch();
-    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
   }
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);

@@ -55,6 +55,25 @@ int read_device_error();
 // of a launch (LOTUS_WAIT_LIMIT or the default) and the process-unique id of
 // the current CUDA context (0 = none).
 void* driver_fn(const char* name);
+// LOTUS_PDL=0 turns programmatic dependent launch off (default on).
+bool pdl_enabled();
+// Launch that allows programmatic dependent launch (the kernel must call
+// griddep_wait() before touching data earlier kernels wrote).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
 PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col();
 int num_sms();

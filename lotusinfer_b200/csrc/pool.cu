@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(256) adaptive_avgpool_window_kernel(const __ha
                                                                       void* __restrict__ y, int c, int cs, int h,
                                                                       int w, int oh, int ow, int act, int out_f32) {
   __shared__ float red[256 * 8];
+  if (threadIdx.x == 0) griddep_launch();
+  griddep_wait();  // the activations of the kernel before
   const int groups = cs / 8;
   const int slices = static_cast<int>(blockDim.x) / groups;
   const int g = static_cast<int>(threadIdx.x) % groups;
@@ -187,10 +189,10 @@ cudaError_t launch_adaptive_avgpool(const void* x, void* y, int n, int c, int cs
   const size_t total = static_cast<size_t>(n) * oh * ow * (cs / 8);
   const size_t pixels = static_cast<size_t>(n) * oh * ow;
   if (cs / 8 <= 256 && (h / oh) * (w / ow) >= 16 && pixels < (1u << 31) && static_cast<size_t>(h) * w * cs < (1u << 31)) {
-    adaptive_avgpool_window_kernel<<<static_cast<unsigned>(pixels), 256, 0, s>>>(static_cast<const __half*>(x), y, c,
-                                                                                 cs, h, w, oh, ow, act, out_f32);
+    const cudaError_t e = launch_pdl(adaptive_avgpool_window_kernel, dim3(static_cast<unsigned>(pixels)), dim3(256), 0,
+                                     s, static_cast<const __half*>(x), y, c, cs, h, w, oh, ow, act, out_f32);
     note_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
   }
   adaptive_avgpool_nhwc_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half*>(x), y, n, c, cs, h, w,
                                                                     oh, ow, act, out_f32);

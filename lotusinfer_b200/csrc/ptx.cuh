@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 
+#include "common.cuh"
+
 namespace lotus_dev {
 
 // Error word written by a kernel whose bounded wait expired (0 = none).
