@@ -94,6 +94,13 @@ int lotus_conv2d_fwd(const void* x, const void* w_packed, const float* bias, con
  * between the two kernels of one call, so calls sharing it must not overlap
  * on the GPU.  The same reference kernels as lotus_conv2d_fwd. */
 size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d);
+/* The workspace lotus_conv2d_fwd_ws can use for this shape: the split-K need
+ * above, or, for the large launches that run as 2-SM pair tiles, the fp32
+ * partial sums of the last wave of tiles split over K (so that the wave keeps
+ * every SM pair busy) and finished by the same reduction.  Optional: with
+ * less workspace those launches run unsplit.  Split and unsplit results
+ * differ only by the fp32 summation order. */
+size_t lotus_conv2d_workspace_bytes_max(const lotus_conv2d_desc* d);
 int lotus_conv2d_fwd_ws(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                         const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 

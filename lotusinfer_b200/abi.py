@@ -55,6 +55,7 @@ SIGNATURES = {
     "lotus_conv2d_prepack": (_I, [_V, _V, _CD, _V]),
     "lotus_conv2d_fwd": (_I, [_V, _V, _V, _V, _V, _CD, _V]),
     "lotus_conv2d_workspace_bytes": (_S, [_CD]),
+    "lotus_conv2d_workspace_bytes_max": (_S, [_CD]),
     "lotus_conv2d_fwd_ws": (_I, [_V, _V, _V, _V, _V, _CD, _V, _S, _V]),
     "lotus_conv2d_fwd_noalloc": (_I, [_V, _V, _V, _V, _V, _CD, _V]),
     "lotus_conv2d_fwd_slice": (_I, [_V, _V, _V, _V, _V, _I, _CD, _V, _S, _V]),

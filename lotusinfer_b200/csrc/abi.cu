@@ -187,7 +187,7 @@ static int pair_conv_bn(const ConvTcArgs& a) {
 
 static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias, const void* residual, void* y,
                          const lotus_conv2d_desc* d, void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                         int y_stride = 0) {
+                         int y_stride = 0, bool pair_split = true) {
   int oh, ow;
   const int st = check_conv_desc(d, &oh, &ow);
   if (st != LOTUS_OK) return st;
@@ -213,7 +213,14 @@ static int conv_fwd_impl(const void* x, const void* w_packed, const float* bias,
     return ok();
   }
   if (const int bn = pair_conv_bn(a)) {
-    const int rr = conv_pair_launch(a, bn, stream, &err);
+    // the pair kernel splits its last wave over K when the workspace holds
+    // conv_pair_workspace_bytes; pair_split = false keeps it whole
+    ConvTcArgs pa = a;
+    if (!pair_split) {
+      pa.ws = nullptr;
+      pa.ws_bytes = 0;
+    }
+    const int rr = conv_pair_launch(pa, bn, stream, &err);
     if (rr != 0) return fail(rr == -2 ? LOTUS_ERR_UNSUPPORTED : LOTUS_ERR_CUDA, std::string("conv2d: ") + err);
     return ok();
   }
@@ -256,7 +263,8 @@ int lotus_conv2d_fwd_noalloc(const void* x, const void* w_packed, const float* b
     if (conv_tc_noalloc_scratch(&scratch, &err) != 0)
       return fail(LOTUS_ERR_CUDA, std::string("conv2d_noalloc: scratch set-up: ") + err);
   }
-  return conv_fwd_impl(x, w_packed, bias, residual, y, d, scratch, scratch ? kNoAllocScratchBytes : 0, stream);
+  return conv_fwd_impl(x, w_packed, bias, residual, y, d, scratch, scratch ? kNoAllocScratchBytes : 0, stream, 0,
+                       /*pair_split=*/false);
 }
 
 size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d) {
@@ -270,6 +278,23 @@ size_t lotus_conv2d_workspace_bytes(const lotus_conv2d_desc* d) {
   if (conv_tc_launch(a, nullptr, &err, &need) != 0) return 0;
   ok();
   return need;
+}
+
+// The general kernel's split-K need, or, for launches the CTA-pair kernel
+// takes, the workspace it uses to split the K loop of its last wave of tiles
+// (optional: with less the pair kernel runs unsplit, which is why
+// lotus_conv2d_workspace_bytes leaves it out).
+size_t lotus_conv2d_workspace_bytes_max(const lotus_conv2d_desc* d) {
+  int oh, ow;
+  if (check_conv_desc(d, &oh, &ow) != LOTUS_OK) return 0;
+  void* fake = reinterpret_cast<void*>(static_cast<uintptr_t>(256));
+  ConvTcArgs a = conv_args(fake, fake, nullptr, nullptr, fake, d, oh, ow);
+  if (!use_rows_conv(a, d->n))
+    if (const int bn = pair_conv_bn(a)) {
+      ok();
+      return conv_pair_workspace_bytes(a, bn);
+    }
+  return lotus_conv2d_workspace_bytes(d);
 }
 
 // ------------------------------------------------------------------ tconv

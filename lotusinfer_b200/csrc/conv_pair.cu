@@ -102,8 +102,38 @@ struct PairParams {
   int n_tiles;      // BN-column tiles
   int m_tiles;      // 128-row M tiles
   int pair_tiles;   // ceil(m_tiles / (2 * MT)) * n_tiles
+  // Work units: pair tiles 0 .. full_units-1 whole, then each later tile as
+  // ksplit units of kbs K blocks (the last wave's tiles, so that it keeps
+  // every SM pair busy); a partial unit writes its raw fp32 sums to
+  // ws[split][row - row0][ws_ld] and a split-K reduction finishes rows
+  // row0 .. M-1.  ksplit == 1: every tile whole.
+  int full_units, ksplit, kbs, units, row0, ws_ld;
+  float* ws;
   uint32_t wait_limit;
 };
+
+// Work unit u: pair tile T, its K blocks kb0 .. kb0+nkb-1, and the split
+// index of a partial unit (-1: the whole tile).
+struct Unit {
+  int T, kb0, nkb, split;
+};
+__device__ __forceinline__ Unit unit_of(const PairParams& p, int u) {
+  Unit w;
+  if (u < p.full_units) {
+    w.T = u;
+    w.kb0 = 0;
+    w.nkb = p.KB;
+    w.split = -1;
+    return w;
+  }
+  const int v = u - p.full_units;
+  const int t = v / p.ksplit;
+  w.T = p.full_units + t;
+  w.split = v - t * p.ksplit;
+  w.kb0 = w.split * p.kbs;
+  w.nkb = min(p.KB, w.kb0 + p.kbs) - w.kb0;
+  return w;
+}
 
 // ------------------------------------------------------------ cluster PTX
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -281,6 +311,34 @@ __device__ __forceinline__ void store_chunk(const PairParams& p, const uint32_t 
   __syncwarp();  // the buffer is rewritten by the next chunk
 }
 
+// One 32-column chunk of raw fp32 sums for the split-K reduction, at
+// ws[split][em - row0][col0 ..]: two 16-column halves, each staged in the
+// warp's 32 x 64-byte buffer like store_chunk and stored as 8 rows x 64
+// contiguous bytes per instruction.  Warp-collective.
+__device__ __forceinline__ void store_partial_chunk(const PairParams& p, const uint32_t (&v)[32], int em, bool valid,
+                                                    int split, int col0, uint8_t* stg, int lane) {
+  uint4* st = reinterpret_cast<uint4*>(stg);
+  const int row_em = valid ? em : -1;
+  float* base = p.ws + static_cast<int64_t>(split) * (p.M - p.row0) * p.ws_ld + col0;
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      st[lane * 4 + ((g ^ (lane >> 1)) & 3)] = make_uint4(v[16 * hf + 4 * g], v[16 * hf + 4 * g + 1],
+                                                          v[16 * hf + 4 * g + 2], v[16 * hf + 4 * g + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2), c = lane & 3;
+      const int em_r = __shfl_sync(0xffffffffu, row_em, r);
+      const uint4 val = st[r * 4 + ((c ^ (r >> 1)) & 3)];
+      if (em_r >= 0)
+        *reinterpret_cast<uint4*>(base + static_cast<int64_t>(em_r - p.row0) * p.ws_ld + 16 * hf + 4 * c) = val;
+    }
+    __syncwarp();  // the buffer is rewritten next
+  }
+}
+
 // Epilogue warps of both CTAs: this CTA's 128 rows of each pair tile.
 template <int BN, int MT, int ACT>
 __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, uint64_t* tempty, const float* s_bias,
@@ -296,8 +354,9 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
   const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
   const int pair0 = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
   int lt = 0;
-  for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
-    const int mp = T / p.n_tiles, nt = T - mp * p.n_tiles;
+  for (int u = pair0; u < p.units; u += npairs, ++lt) {
+    const Unit w = unit_of(p, u);
+    const int mp = w.T / p.n_tiles, nt = w.T - mp * p.n_tiles;
     const int em = (((2 * mp + static_cast<int>(rank)) * MT + mi) * kBlockM) + q * 32 + lane;
     const bool valid = em < p.M;
     const int n0 = nt * BN;
@@ -314,7 +373,10 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
       tmem_ld_32x32b_x32(tmem_base + t_lane + static_cast<uint32_t>(ab * C::kAccCols + half * kWarpCols + c * 32),
                          v);
       tmem_ld_wait();
-      store_chunk<ACT>(p, v, em, valid, n0 + col, s_bias, stg, lane);
+      if (w.split < 0)
+        store_chunk<ACT>(p, v, em, valid, n0 + col, s_bias, stg, lane);
+      else  // a partial unit
+        store_partial_chunk(p, v, em, valid, w.split, n0 + col, stg, lane);
     }
     tc_fence_before();
     __syncwarp();
@@ -398,8 +460,9 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       bool ok = true;
       uint32_t it = 0;
       const int ohw = p.OH * p.OW, cpt = p.Cs_in / kBlockK;
-      for (int T = pair0; T < p.pair_tiles && ok; T += npairs) {
-        const int mp = T / p.n_tiles, nt = T - mp * p.n_tiles;
+      for (int u = pair0; u < p.units && ok; u += npairs) {
+        const Unit w = unit_of(p, u);
+        const int mp = w.T / p.n_tiles, nt = w.T - mp * p.n_tiles;
         // this CTA's M tiles; past the last M tile (a pair tile that overhangs
         // the output) it loads the last real tile (those results are never
         // stored)
@@ -415,8 +478,10 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
           hst[i] = oh * p.sh - p.ph;
         }
         const int brow = nt * BN + static_cast<int>(rank) * C::kBHalf;
-        int c0 = 0, s = 0, r = 0;
-        for (int kb = 0; kb < p.KB; ++kb, ++it) {
+        // (tap, channel) position of the unit's first K block
+        const int tap0 = w.kb0 / cpt;
+        int c0 = (w.kb0 - tap0 * cpt) * kBlockK, r = tap0 / p.kw, s = tap0 - r * p.kw;
+        for (int kb = w.kb0; kb < w.kb0 + w.nkb; ++kb, ++it) {
           const int st = static_cast<int>(it % C::kStages);
           if (*abort_flag || !mbar_wait(&empty[st], ((it / C::kStages) & 1) ^ 1, kErrWaitEmpty, p.wait_limit)) {
             ok = false;
@@ -438,7 +503,6 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
             }
           }
         }
-        (void)cpt;
       }
       if (!ok) *abort_flag = 1;
     }
@@ -447,9 +511,10 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       bool ok = true;
       uint32_t it = 0, h = 0;
       int lt = 0;
-      for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
+      for (int u = pair0; u < p.units; u += npairs, ++lt) {
+        const Unit w = unit_of(p, u);
         const int ab = lt % C::kAcc;
-        for (int kb = 0; kb < p.KB; ++kb, ++it, ++h) {
+        for (int kb = 0; kb < w.nkb; ++kb, ++it, ++h) {
           const int st = static_cast<int>(it % C::kStages);
           if (lane == 0 && ok) {
             if (kb == 0)
@@ -474,10 +539,11 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
       constexpr uint32_t idesc = idesc_pair(BN);
       uint32_t it = 0, h = 0;
       int lt = 0;
-      for (int T = pair0; T < p.pair_tiles; T += npairs, ++lt) {
+      for (int u = pair0; u < p.units; u += npairs, ++lt) {
+        const Unit w = unit_of(p, u);
         const int ab = lt % C::kAcc;
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * C::kAccCols);
-        for (int kb = 0; kb < p.KB; ++kb, ++it, ++h) {
+        for (int kb = 0; kb < w.nkb; ++kb, ++it, ++h) {
           const int st = static_cast<int>(it % C::kStages);
           named_sync(1u + h % C::kQueue, 64);
           tc_fence_after();
@@ -550,6 +616,133 @@ int make_im2col_map(CUtensorMap* map, const ConvTcArgs& a, int n_img) {
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// How the pair tiles are walked.  With `pairs` SM pairs, the tiles of the
+// full waves are processed whole; when a workspace can be used, each tile of
+// the last, partial wave is split over its K loop into k units (k = 2..4,
+// each unit at least one K block), chosen when the round-robin makespan
+// (full tile = 1, unit = its share of the K blocks) plus the split-K
+// reduction it needs is estimated at least 8% below the unsplit makespan.
+// The full part is a multiple of the N-tile count, so the split tiles cover
+// whole output rows row0 .. M-1.  LOTUS_PAIR_SPLIT=0 never splits; =1 splits
+// whenever that shortens the makespan, ignoring the reduction's cost.
+struct PairPlan {
+  int pair_tiles, full_units, ksplit, kbs, units, row0, ws_ld;
+  size_t ws_bytes;  // 0 when nothing is split
+};
+
+PairPlan plan_pairs(const ConvTcArgs& a, int bn, int mt, int pairs, bool allow_split) {
+  PairPlan pl{};
+  const int KB = a.k_pad / kBlockK;
+  const int n_tiles = (a.n_cols + bn - 1) / bn;
+  const int m_tiles = (a.M + kBlockM - 1) / kBlockM;
+  pl.pair_tiles = (m_tiles + 2 * mt - 1) / (2 * mt) * n_tiles;
+  pl.full_units = pl.pair_tiles;
+  pl.ksplit = 1;
+  pl.kbs = KB;
+  pl.units = pl.pair_tiles;
+  pl.ws_ld = n_tiles * bn;
+  const char* env = std::getenv("LOTUS_PAIR_SPLIT");
+  if (!allow_split || pairs < 1 || (env != nullptr && env[0] == '0')) return pl;
+  const bool force = env != nullptr && env[0] == '1';
+  const int full = (pl.pair_tiles / pairs) * pairs / n_tiles * n_tiles;
+  const int rem = pl.pair_tiles - full;
+  if (rem <= 0) return pl;
+  auto makespan = [&](int k, int kbs) {
+    const int units = full + k * rem;
+    double worst = 0;
+    for (int q = 0; q < pairs && q < units; ++q) {
+      double t = 0;
+      for (int u = q; u < units; u += pairs) {
+        if (u < full) {
+          t += 1.0;
+        } else {
+          const int sp = (u - full) % k;
+          t += static_cast<double>(std::min(KB, (sp + 1) * kbs) - sp * kbs) / KB;
+        }
+      }
+      worst = std::max(worst, t);
+    }
+    return worst;
+  };
+  // Estimated time in microseconds: a pair tile at ~20 TFLOP/s (one SM
+  // pair's share of the dense fp16 rate), the reduction as its HBM bytes at
+  // ~6 TB/s (k fp32 partial rows read, fp16 rows written, the residual
+  // read) plus ~2 us for its launch and tail.
+  const double tile_us = 2.0 * (2 * mt * kBlockM) * bn * a.k_pad / 2.0e7;
+  const int row0 = full / n_tiles * 2 * mt * kBlockM;
+  auto reduce_us = [&](int k) {
+    const double rows = static_cast<double>(a.M - row0);
+    const double bytes = rows * (4.0 * k * pl.ws_ld + 2.0 * a.Cs_out * (a.residual != nullptr ? 2 : 1));
+    return bytes / 6.0e6 + 2.0;
+  };
+  const double base = makespan(1, KB) * tile_us;
+  int best_k = 1, best_kbs = KB;
+  double best = base;
+  for (int k = 2; k <= 4 && k <= KB; ++k) {
+    const int kbs = (KB + k - 1) / k;
+    const int keff = (KB + kbs - 1) / kbs;  // every unit gets at least one K block
+    // LOTUS_PAIR_SPLIT=1: the split with the shortest makespan, whatever it costs
+    const double t = makespan(keff, kbs) * tile_us + (force ? 0.0 : reduce_us(keff));
+    if (t < best - 1e-9) {
+      best = t;
+      best_k = keff;
+      best_kbs = kbs;
+    }
+  }
+  if (best_k == 1 || (!force && best > 0.92 * base)) return pl;
+  pl.full_units = full;
+  pl.ksplit = best_k;
+  pl.kbs = best_kbs;
+  pl.units = full + best_k * rem;
+  pl.row0 = row0;
+  pl.ws_bytes = static_cast<size_t>(best_k) * (a.M - pl.row0) * pl.ws_ld * sizeof(float);
+  return pl;
+}
+
+// Per device and context: the shared-memory opt-in of the kernel and the
+// number of CTA pairs that can be resident at once (0 with *err set on
+// failure).
+template <int BN, int MT>
+int resident_pairs(const char** err) {
+  using C = PairCfg<BN, MT>;
+  static std::atomic<uint64_t> attr_ctx[64];
+  static std::atomic<int> max_pairs[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = "pair conv: no usable device";
+    return 0;
+  }
+  const uint64_t ctx = current_context_id();
+  if (ctx == 0 || attr_ctx[dev].load(std::memory_order_acquire) != ctx) {
+    cudaError_t ae =
+        cudaFuncSetAttribute(conv_pair_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (ae != cudaSuccess) {
+      *err = cudaGetErrorString(ae);
+      return 0;
+    }
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int clusters = 0;
+    ae = cudaOccupancyMaxActiveClusters(&clusters, conv_pair_kernel<BN, MT>, &cfg);
+    if (ae != cudaSuccess || clusters < 1) {
+      *err = ae != cudaSuccess ? cudaGetErrorString(ae) : "pair conv: no CTA pair fits an SM pair";
+      return 0;
+    }
+    max_pairs[dev].store(clusters, std::memory_order_relaxed);
+    attr_ctx[dev].store(ctx, std::memory_order_release);
+  }
+  return max_pairs[dev].load(std::memory_order_relaxed);
+}
+
 template <int BN, int MT>
 int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   using C = PairCfg<BN, MT>;
@@ -576,7 +769,19 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   p.KB = a.k_pad / kBlockK;
   p.n_tiles = (a.n_cols + BN - 1) / BN;
   p.m_tiles = (a.M + kBlockM - 1) / kBlockM;
-  p.pair_tiles = (p.m_tiles + 2 * MT - 1) / (2 * MT) * p.n_tiles;
+  const int resident = resident_pairs<BN, MT>(err);
+  if (resident < 1) return -3;
+  // the split of the last wave needs the caller's workspace (and room in it)
+  PairPlan pl = plan_pairs(a, BN, MT, resident, a.ws != nullptr);
+  if (pl.ws_bytes > a.ws_bytes) pl = plan_pairs(a, BN, MT, resident, false);
+  p.pair_tiles = pl.pair_tiles;
+  p.full_units = pl.full_units;
+  p.ksplit = pl.ksplit;
+  p.kbs = pl.kbs;
+  p.units = pl.units;
+  p.row0 = pl.row0;
+  p.ws_ld = pl.ws_ld;
+  p.ws = pl.ksplit > 1 ? a.ws : nullptr;
   p.wait_limit = wait_limit_from_env();
   const int n_img = a.M / (a.OH * a.OW);
 
@@ -589,16 +794,6 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
     *err = "pair conv: im2col tensor map encoding failed";
     return -2;
   }
-  // per device and context: the shared-memory opt-in and the number of CTA
-  // pairs that can be resident at once
-  static std::atomic<uint64_t> attr_ctx[64];
-  static std::atomic<int> max_pairs[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    *err = "pair conv: no usable device";
-    return -3;
-  }
-  const uint64_t ctx = current_context_id();
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -611,34 +806,28 @@ int launch_bn(const ConvTcArgs& a, cudaStream_t stream, const char** err) {
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (ctx == 0 || attr_ctx[dev].load(std::memory_order_acquire) != ctx) {
-    cudaError_t ae =
-        cudaFuncSetAttribute(conv_pair_kernel<BN, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    if (ae != cudaSuccess) {
-      *err = cudaGetErrorString(ae);
-      return -3;
-    }
-    cfg.gridDim = dim3(2 * (num_sms() / 2));
-    int clusters = 0;
-    ae = cudaOccupancyMaxActiveClusters(&clusters, conv_pair_kernel<BN, MT>, &cfg);
-    if (ae != cudaSuccess || clusters < 1) {
-      *err = ae != cudaSuccess ? cudaGetErrorString(ae) : "pair conv: no CTA pair fits an SM pair";
-      return -3;
-    }
-    max_pairs[dev].store(clusters, std::memory_order_relaxed);
-    attr_ctx[dev].store(ctx, std::memory_order_release);
-  }
-  const int pairs = std::min(max_pairs[dev].load(std::memory_order_relaxed), p.pair_tiles);
+  const int pairs = std::min(resident, p.units);
   cfg.gridDim = dim3(2 * pairs);
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, conv_pair_kernel<BN, MT>, mw, ma, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, conv_pair_kernel<BN, MT>, mw, ma, p);
   note_launch();
+  if (e == cudaSuccess && p.ksplit > 1)  // rows row0 .. M-1: sum the split units in order, bias, residual, act
+    e = launch_splitk_reduce(p.ws, p.ksplit, a.M - p.row0, p.ws_ld, a.bias,
+                             p.residual != nullptr ? p.residual + static_cast<int64_t>(p.row0) * p.Cs_out : nullptr,
+                             p.y + static_cast<int64_t>(p.row0) * p.y_stride, a.M - p.row0, p.Cout, p.Cs_out,
+                             p.y_stride, p.act, stream);
   if (e != cudaSuccess) {
     *err = cudaGetErrorString(e);
     return -3;
   }
   return 0;
+}
+
+template <int BN, int MT>
+size_t workspace_bn(const ConvTcArgs& a) {
+  const char* err = "";
+  const int resident = resident_pairs<BN, MT>(&err);
+  return resident < 1 ? 0 : plan_pairs(a, BN, MT, resident, true).ws_bytes;
 }
 
 }  // namespace
@@ -669,6 +858,12 @@ int conv_pair_check(const ConvTcArgs& a, int bn, const char** err) {
     return -2;
   }
   return 0;
+}
+
+size_t conv_pair_workspace_bytes(const ConvTcArgs& a, int bn) {
+  const char* err = "";
+  if (conv_pair_check(a, bn, &err) != 0) return 0;
+  return bn == 256 ? workspace_bn<256, 1>(a) : workspace_bn<128, 2>(a);
 }
 
 int conv_pair_launch(const ConvTcArgs& a, int bn, cudaStream_t stream, const char** err) {

@@ -1416,6 +1416,21 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   }
 }
 
+// Split-K reduction of `splits` fp32 partial tiles in ws[split][row][ws_ld]
+// into an NHWC fp16 output of `rows` rows (bias, residual, activation; pad
+// channels zero), on `stream`, allowing programmatic dependent launch.
+cudaError_t launch_splitk_reduce(const float* ws, int splits, int rows, int ws_ld, const float* bias,
+                                 const __half* residual, __half* y, int M, int cout, int cs_out, int y_stride,
+                                 int act, cudaStream_t stream) {
+  const size_t total = static_cast<size_t>(M) * (cs_out / 8);
+  const unsigned grid =
+      static_cast<unsigned>(std::min<size_t>((total + 255) / 256, static_cast<size_t>(num_sms()) * 8));
+  cudaError_t e = launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, stream, ws, splits, rows, ws_ld, bias,
+                             residual, static_cast<void*>(y), M, cout, cs_out, y_stride, act, 0);
+  note_launch();
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 // Split count for an output-tile grid of `mn` tiles over KB K blocks on `sms`
 // SMs: none unless the grid fills at most half of the SMs; at least 4 K blocks
 // per split; every split non-empty.

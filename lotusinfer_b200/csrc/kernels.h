@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
 namespace lotus_impl {
 
@@ -113,6 +114,13 @@ int conv_rows_read_device_error();
 // shape, else -2 with the reason in *err.
 int conv_pair_check(const ConvTcArgs& a, int bn, const char** err);
 int conv_pair_launch(const ConvTcArgs& a, int bn, cudaStream_t stream, const char** err);
+// Workspace bytes the pair kernel uses to split its last wave over K (0: it
+// does not split this shape); without that much workspace it runs unsplit.
+size_t conv_pair_workspace_bytes(const ConvTcArgs& a, int bn);
+// conv_tc.cu: the split-K reduction into an NHWC fp16 output.
+cudaError_t launch_splitk_reduce(const float* ws, int splits, int rows, int ws_ld, const float* bias,
+                                 const __half* residual, __half* y, int M, int cout, int cs_out, int y_stride,
+                                 int act, cudaStream_t stream);
 int conv_pair_read_device_error();
 
 // pack.cu

@@ -214,7 +214,9 @@ void Conv2dLayer::Forward(cudaStream_t stream) {
              name_);
 }
 
-size_t Conv2dLayer::WorkspaceBytes() const { return has_pool_ ? 0 : lotus_conv2d_workspace_bytes(&desc_); }
+size_t Conv2dLayer::WorkspaceBytes() const {
+  return has_pool_ ? 0 : lotus_conv2d_workspace_bytes_max(&desc_);
+}
 
 int Conv2dLayer::Launches() const {
   if (has_pool_) return 1;

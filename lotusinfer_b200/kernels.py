@@ -79,10 +79,13 @@ def conv2d_prepack(w_oihw: torch.Tensor, c_in: int) -> torch.Tensor:
     return out.view(cout, -1)
 
 
-def conv2d_workspace_bytes(n, c_in, h, w, c_out, k, stride=1, pad=0, act=ACT_NONE, out_f32=False) -> int:
-    """Workspace bytes the split-K plan of this conv wants (0 = no split)."""
+def conv2d_workspace_bytes(n, c_in, h, w, c_out, k, stride=1, pad=0, act=ACT_NONE, out_f32=False,
+                           use_max=False) -> int:
+    """Workspace bytes the split-K plan of this conv wants (0 = no split);
+    use_max: also the pair-tile kernel's optional last-wave split."""
     d = conv_desc(n, c_in, h, w, c_out, k, stride, pad, act, OUT_ROWS_F32 if out_f32 else OUT_NHWC_F16)
-    return int(abi.lib().lotus_conv2d_workspace_bytes(ctypes.byref(d)))
+    fn = abi.lib().lotus_conv2d_workspace_bytes_max if use_max else abi.lib().lotus_conv2d_workspace_bytes
+    return int(fn(ctypes.byref(d)))
 
 
 def conv2d(x: torch.Tensor, c_in: int, w_packed: torch.Tensor, bias: Optional[torch.Tensor], c_out: int,

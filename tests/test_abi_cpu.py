@@ -100,6 +100,10 @@ def test_splitk_workspace_queries():
     assert K.conv2d_workspace_bytes(1, 512, 7, 7, 512, 3, 1, 1) > 0      # 4 output tiles, K = 4608
     assert K.conv2d_workspace_bytes(256, 512, 7, 7, 512, 3, 1, 1) == 0   # 196 tiles fill the GPU
     assert K.conv2d_workspace_bytes(1, 3, 20, 20, 8, 3, 1, 1) == 0       # K = 64: one K block
+    # the max query adds the pair kernel's last-wave split, which needs the
+    # device's resident-pair count: without a GPU it equals the split-K need
+    for shape in [(1, 512, 7, 7, 512, 3, 1, 1), (256, 512, 7, 7, 512, 3, 1, 1), (2, 64, 20, 20, 64, 3, 1, 1)]:
+        assert K.conv2d_workspace_bytes(*shape, use_max=True) >= K.conv2d_workspace_bytes(*shape)
     L = abi.lib()
     assert L.lotus_linear_workspace_bytes(32, 9216, 4096) > 0
     assert L.lotus_linear_workspace_bytes(4, 9216, 4096) == 0            # batch <= 8 runs the GEMV

@@ -290,6 +290,86 @@ def test_conv2d_pair_kernel_matches_general_kernel(case, monkeypatch):
     _no_device_error()
 
 
+@pytest.mark.parametrize("case", [
+    # name, n, c, h, w, cout, k, stride, pad, residual: ResNet-18 stage 4 at
+    # batch 256 (98 pair tiles on 74 SM pairs: the last 24 split over K)
+    ("stage4_3x3_residual", 256, 512, 7, 7, 512, 3, 1, 1, True),
+    ("stage4_3x3", 256, 512, 7, 7, 512, 3, 1, 1, False),
+    ("stage4_3x3s2", 256, 256, 14, 14, 512, 3, 2, 1, False),
+], ids=lambda c: c[0])
+def test_conv2d_pair_last_wave_split(case, monkeypatch):
+    """With the workspace lotus_conv2d_workspace_bytes_max asks for, the pair
+    kernel splits its last wave over K and a split-K reduction finishes those
+    rows: the rows of the full waves are bit-exact with the unsplit call, the
+    split rows differ only by the fp32 summation order: one fp16 ulp, or
+    for results near zero the fp32 rounding of a 4608-term sum (< 1e-4)."""
+    from lotusinfer_b200 import abi
+    monkeypatch.delenv("LOTUS_CONV_PAIR", raising=False)
+    monkeypatch.delenv("LOTUS_PAIR_SPLIT", raising=False)
+    K = _k()
+    _, n, c, h, w, cout, k, s, p, with_res = case
+    need = K.conv2d_workspace_bytes(n, c, h, w, cout, k, s, p, 1, use_max=True)
+    assert need > 0 and K.conv2d_workspace_bytes(n, c, h, w, cout, k, s, p, 1) == 0
+    g = torch.Generator(device=DEV).manual_seed(zlib.crc32(case[0].encode()))
+    x = K.to_nhwc(torch.rand((n, c, h, w), device=DEV, generator=g) * 2 - 1)
+    wt = torch.randn((cout, c, k, k), device=DEV, generator=g) * (2.0 / (c * k * k)) ** 0.5
+    b = torch.rand(cout, device=DEV, generator=g) * 0.2 - 0.1
+    oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    res = K.to_nhwc(torch.randn((n, cout, oh, ow), device=DEV, generator=g)) if with_res else None
+    wp = K.conv2d_prepack(wt, c)
+    ws = torch.full((need // 4,), float("nan"), dtype=torch.float32, device=DEV)  # every read slot is written first
+    launches0 = abi.launch_count()
+    y_split = K.conv2d(x, c, wp, b, cout, k, s, p, 1, residual=res, workspace=ws)
+    assert abi.launch_count() - launches0 == 2  # pair kernel + reduction
+    y_whole = K.conv2d(x, c, wp, b, cout, k, s, p, 1, residual=res)
+    torch.cuda.synchronize()
+    rows_s, rows_w = y_split.reshape(-1, y_split.shape[-1]), y_whole.reshape(-1, y_whole.shape[-1])
+    same = (rows_s == rows_w).all(dim=1)
+    first_diff = int(torch.nonzero(~same)[0]) if not bool(same.all()) else rows_s.shape[0]
+    assert first_diff >= rows_s.shape[0] // 2  # the full waves: whole rows, bit-exact
+    fs, fw = rows_s.float(), rows_w.float()
+    excess = (fs - fw).abs() - (torch.maximum(fs.abs(), fw.abs()) * 2.0 ** -10 + 1e-4)
+    assert float(excess.max()) <= 0, f"worst excess {float(excess.max())}"
+    assert not bool(torch.isnan(rows_s.float()).any())
+    _no_device_error()
+
+
+SPLIT_PAIR_CASES = [
+    # the pair kernel with every pair tile split over K (LOTUS_PAIR_SPLIT=1
+    # on launches smaller than one wave), against the oracle
+    ("pair_split_3x3_128_residual", 2, 128, 14, 14, 128, 3, 1, 1, 1, True),  # 512 x 128 pair tiles
+    ("pair_split_cout192_partial_tile", 2, 128, 9, 9, 192, 3, 1, 1, 2, False),
+    ("pair_split_cout136_pad_channels", 1, 64, 12, 12, 136, 3, 1, 1, 1, True),
+    ("pair_split_cin192_5x5", 1, 192, 11, 11, 128, 5, 1, 2, 1, False),
+]
+
+
+@pytest.mark.parametrize("case", SPLIT_PAIR_CASES, ids=[c[0] for c in SPLIT_PAIR_CASES])
+def test_conv2d_pair_split_parity(case, monkeypatch):
+    monkeypatch.setenv("LOTUS_CONV_PAIR", "1")
+    monkeypatch.setenv("LOTUS_PAIR_SPLIT", "1")
+    K = _k()
+    _, n, c, h, w, cout, k, s, p, act, with_res = case
+    need = K.conv2d_workspace_bytes(n, c, h, w, cout, k, s, p, act, use_max=True)
+    assert need > 0
+    rng = _rng(zlib.crc32(case[0].encode()))
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = rng.normal(0, np.sqrt(2.0 / (c * k * k)), (cout, c, k, k)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, cout).astype(np.float32)
+    oh = (h + 2 * p - k) // s + 1
+    ow = (w + 2 * p - k) // s + 1
+    res = rng.normal(0, 1, (n, cout, oh, ow)).astype(np.float32) if with_res else None
+    want = oracle.conv2d(x, wt, b, (s, s), (p, p), act, residual=res)
+    ws = torch.full((need // 4,), float("nan"), dtype=torch.float32, device=DEV)
+    xg = K.to_nhwc(_gpu(x))
+    y = K.conv2d(xg, c, K.conv2d_prepack(_gpu(wt), c), _gpu(b), cout, k, s, p, act,
+                 residual=K.to_nhwc(_gpu(res)) if with_res else None, workspace=ws)
+    assert_close(K.from_nhwc(y, cout).cpu().numpy(), want, what=case[0])
+    if y.shape[-1] != cout:
+        assert torch.count_nonzero(y[..., cout:]).item() == 0
+    _no_device_error()
+
+
 def test_conv2d_pair_kernel_channel_slice(monkeypatch):
     """The pair kernel writes a channel slice of a wider NHWC tensor and
     leaves the other channels untouched."""
