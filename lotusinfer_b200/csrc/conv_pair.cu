@@ -153,6 +153,15 @@ __device__ __forceinline__ uint32_t map_to(const void* p, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Arrivals that order no memory accesses (no fence, so no wait for this
+// thread's global stores to drain): for barriers that only hand back TMEM
+// whose tcgen05.ld results are already in registers.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -361,10 +370,31 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
     const bool valid = em < p.M;
     const int n0 = nt * BN;
     const int ab = lt % C::kAcc;
+    if (p.residual != nullptr && w.split < 0 && valid) {
+      // pull this lane's residual row segment into L2 while the MMAs run
+      const __half* rrow = p.residual + static_cast<int64_t>(em) * p.Cs_out;
+      for (int c0 = n0 + col_base; c0 < min(n0 + col_base + kWarpCols, p.Cs_out); c0 += 64)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(rrow + c0));
+    }
     bool ok = true;
     if (lane == 0) ok = !*abort_flag && mbar_wait(&tfull[ab], (lt / C::kAcc) & 1, kErrWaitAccum, p.wait_limit);
     ok = __shfl_sync(0xffffffffu, ok, 0);
     tc_fence_after();
+    // The accumulator goes back to the MMA warp (the ring lives on the even
+    // CTA's barriers) right after this warp's last TMEM load, before its
+    // last chunk is stored, with a relaxed arrival that waits for no stores.
+    bool released = false;
+    auto release = [&]() {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive_relaxed(&tempty[ab]);
+        else
+          mbar_arrive_remote_relaxed(map_to(&tempty[ab], 0));
+      }
+      released = true;
+    };
 #pragma unroll 1
     for (int c = 0; c < kWarpCols / 32; ++c) {
       const int col = col_base + c * 32;  // output column inside the tile
@@ -373,21 +403,14 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
       tmem_ld_32x32b_x32(tmem_base + t_lane + static_cast<uint32_t>(ab * C::kAccCols + half * kWarpCols + c * 32),
                          v);
       tmem_ld_wait();
+      if (c + 1 == kWarpCols / 32 || n0 + col + 32 >= p.Cs_out) release();  // no TMEM load after this one
       if (w.split < 0)
         store_chunk<ACT>(p, v, em, valid, n0 + col, s_bias, stg, lane);
       else  // a partial unit
         store_partial_chunk(p, v, em, valid, w.split, n0 + col, stg, lane);
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      // the accumulator ring lives on the even CTA's barriers
-      if (rank == 0)
-        mbar_arrive(&tempty[ab]);
-      else
-        mbar_arrive_remote(map_to(&tempty[ab], 0));
-      if (!ok) *abort_flag = 1;
-    }
+    if (!released) release();
+    if (lane == 0 && !ok) *abort_flag = 1;
   }
 }
 
