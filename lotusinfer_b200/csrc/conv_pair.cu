@@ -257,14 +257,14 @@ __device__ __forceinline__ float act_p(float v) {
 // channels zero.  The chunk is staged in the warp's 32 x 64-byte buffer
 // (16-byte pieces XOR-swizzled by row) and stored as 8 rows x 64 contiguous
 // bytes per instruction.  Warp-collective.
-template <int ACT>
+template <int ACT, bool RES>
 __device__ __forceinline__ void store_chunk(const PairParams& p, const uint32_t (&v)[32], int em, bool valid,
                                             int col0, const float* s_bias, uint8_t* stg, int lane) {
   uint4* st = reinterpret_cast<uint4*>(stg);
   const bool full = col0 + 32 <= p.Cout;
   const int row_em = valid ? em : -1;
   uint4 res[4];
-  if (p.residual != nullptr) {
+  if (RES) {
     // the chunk's residual rows, read as 8 rows x 64 contiguous bytes per
     // instruction into the staging buffer, then each lane takes its row
 #pragma unroll
@@ -287,7 +287,7 @@ __device__ __forceinline__ void store_chunk(const PairParams& p, const uint32_t 
     float f[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) f[j] = s_bias[c + j] + __uint_as_float(v[8 * g + j]);
-    if (p.residual != nullptr) {
+    if (RES) {
       const __half2* rh = reinterpret_cast<const __half2*>(&res[g]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -349,7 +349,7 @@ __device__ __forceinline__ void store_partial_chunk(const PairParams& p, const u
 }
 
 // Epilogue warps of both CTAs: this CTA's 128 rows of each pair tile.
-template <int BN, int MT, int ACT>
+template <int BN, int MT, int ACT, bool RES>
 __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, uint64_t* tempty, const float* s_bias,
                                          uint8_t* stg, uint32_t tmem_base, uint32_t rank, volatile int* abort_flag) {
   using C = PairCfg<BN, MT>;
@@ -370,7 +370,7 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
     const bool valid = em < p.M;
     const int n0 = nt * BN;
     const int ab = lt % C::kAcc;
-    if (p.residual != nullptr && w.split < 0 && valid) {
+    if (RES && w.split < 0 && valid) {
       // pull this lane's residual row segment into L2 while the MMAs run
       const __half* rrow = p.residual + static_cast<int64_t>(em) * p.Cs_out;
       for (int c0 = n0 + col_base; c0 < min(n0 + col_base + kWarpCols, p.Cs_out); c0 += 64)
@@ -405,13 +405,26 @@ __device__ __forceinline__ void epilogue(const PairParams& p, uint64_t* tfull, u
       tmem_ld_wait();
       if (c + 1 == kWarpCols / 32 || n0 + col + 32 >= p.Cs_out) release();  // no TMEM load after this one
       if (w.split < 0)
-        store_chunk<ACT>(p, v, em, valid, n0 + col, s_bias, stg, lane);
+        store_chunk<ACT, RES>(p, v, em, valid, n0 + col, s_bias, stg, lane);
       else  // a partial unit
         store_partial_chunk(p, v, em, valid, w.split, n0 + col, stg, lane);
     }
     if (!released) release();
     if (lane == 0 && !ok) *abort_flag = 1;
   }
+}
+
+// The residual add compiled in or out: a residual path that is only skipped
+// at run time slowed the no-residual layers' epilogue (ResNet stage-2
+// downsample 21.0 -> 24.2 us).
+template <int BN, int MT, int ACT>
+__device__ __forceinline__ void epilogue_act(const PairParams& p, uint64_t* tfull, uint64_t* tempty,
+                                             const float* s_bias, uint8_t* stg, uint32_t tmem_base, uint32_t rank,
+                                             volatile int* abort_flag) {
+  if (p.residual != nullptr)
+    epilogue<BN, MT, ACT, true>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+  else
+    epilogue<BN, MT, ACT, false>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
 }
 
 template <int BN, int MT>
@@ -472,11 +485,11 @@ conv_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
     griddep_wait();  // residual and output buffers belong to earlier kernels
     uint8_t* stg = s_stg + warp * kStgBytes;
     if (p.act == 1)
-      epilogue<BN, MT, 1>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+      epilogue_act<BN, MT, 1>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
     else if (p.act == 0)
-      epilogue<BN, MT, 0>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+      epilogue_act<BN, MT, 0>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
     else
-      epilogue<BN, MT, 2>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
+      epilogue_act<BN, MT, 2>(p, tfull, tempty, s_bias, stg, tmem_base, rank, abort_flag);
   } else if (warp == kTmaWarp) {
     if (lane == 0) {
       griddep_wait();  // the activations of earlier kernels

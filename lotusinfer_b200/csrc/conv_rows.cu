@@ -144,7 +144,7 @@ __device__ __forceinline__ float act_f(float v) {
 // conv kernel's order), fp16 store; pad channels zero.  The residual of a
 // tile is read before its accumulator wait.  Drained blocks are zeroed and
 // released one tile later (the store completes under the next tile's load).
-template <int ACT>
+template <int ACT, bool RES>
 __device__ __forceinline__ void epilogue(const RsParams& p, uint64_t* tfull, uint64_t* tempty, const float* s_bias,
                                          volatile int* abort_flag, uint32_t tmem_base, int u0, int u1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -178,7 +178,7 @@ __device__ __forceinline__ void epilogue(const RsParams& p, uint64_t* tfull, uin
       const int ab = acc_block(lt);
       const int64_t off = (pix0 + static_cast<int64_t>(oy) * p.OW) * p.Cs_out + c0;
       uint4 rv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-      if (p.residual != nullptr && valid) {
+      if (RES && valid) {
         rv[0] = __ldg(reinterpret_cast<const uint4*>(p.residual + off));
         if (two) rv[1] = __ldg(reinterpret_cast<const uint4*>(p.residual + off + 8));
       }
@@ -207,7 +207,7 @@ __device__ __forceinline__ void epilogue(const RsParams& p, uint64_t* tfull, uin
 #pragma unroll
       for (int k = 0; k < kEpiCols / 2; ++k) {
         float2 v = __fadd2_rn(make_float2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])), bias[k]);
-        if (p.residual != nullptr) v = __fadd2_rn(v, __half22float2(rh[k]));
+        if (RES) v = __fadd2_rn(v, __half22float2(rh[k]));
         float f0 = act_f<ACT>(v.x), f1 = act_f<ACT>(v.y);
         if (pad && c0 + 2 * k >= p.Cout) f0 = 0.f;  // pad channels stay zero
         if (pad && c0 + 2 * k + 1 >= p.Cout) f1 = 0.f;
@@ -224,6 +224,17 @@ __device__ __forceinline__ void epilogue(const RsParams& p, uint64_t* tfull, uin
     __syncwarp();
     if (lane == 0) mbar_arrive(&tempty[pend]);
   }
+}
+
+// The residual add compiled in or out (as in the pair kernel's epilogue).
+template <int ACT>
+__device__ __forceinline__ void epilogue_act(const RsParams& p, uint64_t* tfull, uint64_t* tempty,
+                                             const float* s_bias, volatile int* abort_flag, uint32_t tmem_base,
+                                             int u0, int u1) {
+  if (p.residual != nullptr)
+    epilogue<ACT, true>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
+  else
+    epilogue<ACT, false>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -280,11 +291,11 @@ conv_rows_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_consta
   if (warp < kEpiWarps) {
     griddep_wait();  // residual and output buffers belong to earlier kernels
     if (p.act == 1)
-      epilogue<1>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
+      epilogue_act<1>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
     else if (p.act == 0)
-      epilogue<0>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
+      epilogue_act<0>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
     else
-      epilogue<2>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
+      epilogue_act<2>(p, tfull, tempty, s_bias, abort_flag, tmem_base, u0, u1);
   } else if (warp == kProducer) {
     if (lane == 0) {
       bool ok = true;
