@@ -494,7 +494,8 @@ def main():
                 "frac": achieved / peak if peak else None, "traffic": traffic,
                 "scope": "the 20 conv launches of one forward: FLOPs and DRAM bytes summed over them",
                 "kernel": "the conv launches of one forward: conv_row_kernel (stem + pool), conv_rows_kernel "
-                          "(stage 1), conv_tc_kernel (stage 2), conv_pair_kernel (stages 3-4, tcgen05 cta_group::2); "
+                          "(stage 1), conv_pair_kernel (stages 2-4, tcgen05 cta_group::2: 512 x 128 pair tiles at "
+                          "128 channels, 256 x 256 above); "
                           "fp16 x fp16 -> fp32",
                 "peak_source": f"{peak_src} bf16/fp16 dense burst", "frac_of_sustained": achieved / peak_sus if peak_sus else None,
                 "conv_ms_per_forward": conv_ms, "conv_gflop_per_forward": conv_flops / 1e9,

@@ -161,9 +161,8 @@ static bool use_rows_conv(const ConvTcArgs& a, int n) {
 // The CTA-pair kernel takes NHWC fp16 convs over 64-channel multiples with
 // at least 128 output channels when its pair tiles fill every SM pair at
 // least once: 256 x 256 pair tiles above 128 output channels, 512 x 128 pair
-// tiles (two M tiles a CTA) at 128 with K <= 576 (one M tile a CTA with 128
-// columns was measured slower than the general kernel: too little MMA per
-// loaded stage).  Smaller launches go to the general kernel, which can split K.
+// tiles (two M tiles a CTA) at 128 (one M tile a CTA with 128 columns was
+// measured slower than the general kernel: too little MMA per loaded stage).  Smaller launches go to the general kernel, which can split K.
 // LOTUS_CONV_PAIR=0 or 1 forces the choice (1: 256 columns when Cout > 128,
 // else 128); a forced general-kernel staging mode (LOTUS_CONV_AMODE)
 // implies 0.
@@ -178,10 +177,10 @@ static int pair_conv_bn(const ConvTcArgs& a) {
   const long pairs = num_sms() / 2;
   const long m_tiles = (a.M + 127) / 128;
   const long m_groups = bn == 256 ? (m_tiles + 1) / 2 : (m_tiles + 3) / 4;  // M tiles a pair tile covers: 2 or 4
-  // 512 x 128 pair tiles beat the general kernel on the short-K layers of
-  // ResNet stage 2 (1x1/2: 0.031 vs 0.039 ms; 3x3/2 equal) but not on its
-  // K = 1152 3x3 layers (0.060-0.071 vs 0.060-0.068)
-  if (bn == 128 && a.k_pad > 576) return 0;
+  // 512 x 128 pair tiles beat the general kernel on ResNet stage 2: 1x1/2
+  // 0.031 vs 0.039 ms, and since the pair epilogue hands TMEM back early and
+  // compiles the residual add in or out, the K = 1152 3x3 layers too (54.2 vs
+  // 59.6 us, 64.7 vs 67.7 us with the residual)
   return m_groups * ((a.n_cols + bn - 1) / bn) >= pairs ? bn : 0;
 }
 

@@ -55,7 +55,9 @@ def test_two_rank_gather_equals_single_process():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, x, w, b, q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=120)
+    # generous: the spawned ranks import torch afresh, which takes minutes in
+    # a cold container
+    got = q.get(timeout=600)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -259,6 +259,7 @@ def _conv2d_parity_no_f32(case):
     # stages 2-4 at batch 256 (many pair tiles per CTA pair: every stage ring
     # and accumulator wraps), against the general single-CTA kernel
     ("stage2_3x3_residual", 256, 128, 28, 28, 128, 3, 1, 1, True, "1"),   # 512 x 128 pair tiles
+    ("stage2_3x3", 256, 128, 28, 28, 128, 3, 1, 1, False, "auto"),
     ("stage2_3x3s2", 256, 64, 56, 56, 128, 3, 2, 1, False, "auto"),
     ("stage2_1x1s2", 256, 64, 56, 56, 128, 1, 2, 0, False, "auto"),
     ("stage3_3x3", 256, 256, 14, 14, 256, 3, 1, 1, False, "auto"),
