@@ -150,9 +150,6 @@ __device__ __forceinline__ uint32_t map_to(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
 // Arrivals that order no memory accesses (no fence, so no wait for this
 // thread's global stores to drain): for barriers that only hand back TMEM
 // whose tcgen05.ld results are already in registers.

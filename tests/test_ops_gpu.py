@@ -472,7 +472,10 @@ def test_conv2d_repeatable_and_no_bias():
 
 
 @pytest.mark.parametrize("case", [(2, 3, 224, 224, 2, 3, 112 + 3, 112 + 3), (1, 3, 224, 224, 4, 2, 57, 57),
-                                  (1, 5, 17, 13, 3, 1, 7, 6)])
+                                  (1, 5, 17, 13, 3, 1, 7, 6),
+                                  # factor 2 over 3 channels (the row-staged kernel): odd width (4-byte
+                                  # loads), output past the image on both axes
+                                  (2, 3, 37, 29, 2, 1, 19, 15), (1, 3, 20, 22, 2, 3, 14, 14)])
 def test_space_to_depth_exact(case):
     K = _k()
     n, c, h, w, f, p, oh, ow = case
