@@ -492,7 +492,8 @@ def main():
             traffic = None
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if peak else None, "traffic": traffic,
-                "scope": "the 20 conv launches of one forward: FLOPs and DRAM bytes summed over them",
+                "scope": "the 20 conv layers of one forward (20 conv launches plus the split-K reductions of the "
+                         "4 stage-4 layers whose last wave is split over K): FLOPs and DRAM bytes summed over them",
                 "kernel": "the conv launches of one forward: conv_row_kernel (stem + pool), conv_rows_kernel "
                           "(stage 1), conv_pair_kernel (stages 2-4, tcgen05 cta_group::2: 512 x 128 pair tiles at "
                           "128 channels, 256 x 256 above); "
