@@ -101,12 +101,19 @@ class ClockSampler:
                 "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None}
 
 
-def cpu_baseline_sample(seconds_budget: float = 20.0):
+def parity_images(n: int, batch: int):
+    """Indices of the parity sample in the benchmarked batch: the first
+    ceil(n/2) and the last floor(n/2) images, so that the rows a launch
+    handles in its last wave (split over K in stage 4) are checked too."""
+    return list(range(n - n // 2)) + list(range(batch - n // 2, batch))
+
+
+def cpu_baseline_sample(batch: int, seconds_budget: float = 20.0):
     """The oracle's ResNet-18 on all host threads over a bounded image sample.
 
-    Returns the baseline record and the oracle's logits of the first n images
-    of the seed-0 batch (the images rank 0 benchmarks), which the parity
-    check reuses."""
+    Returns the baseline record, the oracle's logits of the sample (images
+    parity_images(n, batch) of the seed-0 batch, which rank 0 benchmarks) and
+    their indices, which the parity check reuses."""
     from lotusinfer_b200 import synth
     from oracle import oracle
     param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
@@ -118,30 +125,35 @@ def cpu_baseline_sample(seconds_budget: float = 20.0):
     oracle.run_graph(param, binp, x1, weights=w)
     t1 = time.perf_counter() - t0
     n = int(max(1, min(16, (seconds_budget - t1) / max(t1, 1e-3))))
-    x = synth.synthetic_input("resnet18", n, seed=0)
+    idx = parity_images(n, batch)
+    x = np.ascontiguousarray(synth.synthetic_input("resnet18", batch, seed=0)[idx])
     t0 = time.perf_counter()
     want = oracle.run_graph(param, binp, x, weights=w)
     dt = time.perf_counter() - t0
     return ({"value": n / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-             "sample": f"ResNet-18 forward over {n} of the 256 synthetic images (fp32 oracle, OpenMP)"}, want)
+             "sample": f"ResNet-18 forward over {n} of the {batch} synthetic images (fp32 oracle, OpenMP)"}, want, idx)
 
 
-def oracle_logits(n: int):
-    """The oracle's ResNet-18 logits of the first n images of the seed-0 batch."""
+def oracle_logits(n: int, batch: int):
+    """The oracle's ResNet-18 logits of images parity_images(n, batch) of the
+    seed-0 batch, and those indices."""
     from lotusinfer_b200 import synth
     from oracle import oracle
     param, binp = synth.make_model("resnet18", MODEL_DIR, seed=0)
-    return oracle.run_graph(param, binp, synth.synthetic_input("resnet18", n, seed=0))
+    idx = parity_images(n, batch)
+    x = np.ascontiguousarray(synth.synthetic_input("resnet18", batch, seed=0)[idx])
+    return oracle.run_graph(param, binp, x), idx
 
 
 def parity_check(got, want):
-    """Benchmarked logits of the first images against the oracle's: max-abs,
+    """Benchmarked logits of the sample images against the oracle's: max-abs,
     max-abs over the oracle's largest magnitude, rel-L2 and top-1 agreement."""
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
     err = float(np.abs(got - want).max())
     srt = np.sort(want, axis=1)
-    return {"images": int(want.shape[0]), "reference": "CPU oracle (fp32), first images of rank 0's batch",
+    return {"images": int(want.shape[0]),
+            "reference": "CPU oracle (fp32), the first and the last images of rank 0's batch",
             "max_abs": err, "norm_max_abs": err / float(np.abs(want).max()),
             "rel_l2": float(np.linalg.norm(got - want) / np.linalg.norm(want)),
             "top1_equal": int(np.sum(np.argmax(got, 1) == np.argmax(want, 1))),
@@ -520,12 +532,12 @@ def main():
         # last e2e step's logits (rank 0's seed-0 batch) against the oracle
         want = None
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"], want = cpu_baseline_sample()
+            line["cpu_baseline"], want, idx = cpu_baseline_sample(B)
         else:
             line["cpu_baseline"] = None
         if want is None:
-            want = oracle_logits(4)
-        line["parity"] = parity_check(logits_host.numpy()[:want.shape[0]], want)
+            want, idx = oracle_logits(4, B)
+        line["parity"] = parity_check(logits_host.numpy()[idx], want)
     assert abi.device_error() == 0
     g.close()
     if world > 1:
