@@ -292,11 +292,16 @@ def test_conv2d_pair_kernel_matches_general_kernel(case, monkeypatch):
 
 
 @pytest.mark.parametrize("case", [
-    # name, n, c, h, w, cout, k, stride, pad, residual: ResNet-18 stage 4 at
-    # batch 256 (98 pair tiles on 74 SM pairs: the last 24 split over K)
-    ("stage4_3x3_residual", 256, 512, 7, 7, 512, 3, 1, 1, True),
-    ("stage4_3x3", 256, 512, 7, 7, 512, 3, 1, 1, False),
-    ("stage4_3x3s2", 256, 256, 14, 14, 512, 3, 2, 1, False),
+    # name, n, c, h, w, cout, k, stride, pad, residual, LOTUS_PAIR_SPLIT:
+    # ResNet-18 stage 4 at batch 256 (98 pair tiles on 74 SM pairs: the last
+    # 24 split over K), and, split on request although the cost model keeps
+    # them whole, stage 3 (196 tiles, the last 48 split) and stage 2 (392
+    # 512 x 128 tiles, the last 22 split)
+    ("stage4_3x3_residual", 256, 512, 7, 7, 512, 3, 1, 1, True, None),
+    ("stage4_3x3", 256, 512, 7, 7, 512, 3, 1, 1, False, None),
+    ("stage4_3x3s2", 256, 256, 14, 14, 512, 3, 2, 1, False, None),
+    ("stage3_3x3_residual_forced", 256, 256, 14, 14, 256, 3, 1, 1, True, "1"),
+    ("stage2_3x3_residual_forced", 256, 128, 28, 28, 128, 3, 1, 1, True, "1"),
 ], ids=lambda c: c[0])
 def test_conv2d_pair_last_wave_split(case, monkeypatch):
     """With the workspace lotus_conv2d_workspace_bytes_max asks for, the pair
@@ -306,9 +311,12 @@ def test_conv2d_pair_last_wave_split(case, monkeypatch):
     for results near zero the fp32 rounding of a 4608-term sum (< 1e-4)."""
     from lotusinfer_b200 import abi
     monkeypatch.delenv("LOTUS_CONV_PAIR", raising=False)
-    monkeypatch.delenv("LOTUS_PAIR_SPLIT", raising=False)
+    _, n, c, h, w, cout, k, s, p, with_res, split = case
+    if split is None:
+        monkeypatch.delenv("LOTUS_PAIR_SPLIT", raising=False)
+    else:
+        monkeypatch.setenv("LOTUS_PAIR_SPLIT", split)
     K = _k()
-    _, n, c, h, w, cout, k, s, p, with_res = case
     need = K.conv2d_workspace_bytes(n, c, h, w, cout, k, s, p, 1, use_max=True)
     assert need > 0 and K.conv2d_workspace_bytes(n, c, h, w, cout, k, s, p, 1) == 0
     g = torch.Generator(device=DEV).manual_seed(zlib.crc32(case[0].encode()))
